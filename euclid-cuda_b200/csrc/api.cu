@@ -1,0 +1,571 @@
+// C ABI of the distance engine (declared in include/euclid_b200.h).
+//
+// Each reference operator is one row of kOps: the numeric recipe it follows
+// (input type, how S is produced and rounded, how the norms are accumulated, the
+// cancellation threshold, the fallback arithmetic and the output type).  All
+// distance entries go through run_distance(): prep (norms, low copies) ->
+// tensor-core or CUDA-core distance kernel -> compacted recompute -> labels.
+#include "engine.h"
+#include "../../include/euclid_b200.h"
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <algorithm>
+
+namespace euc {
+
+// clang-format off
+static const OpSpec kOps[] = {
+  // op                         name                                   in       gemm        sround   norm          form           flag    rec            out      kform u
+  {EUC_OP_SINGLE,             "pairwise_euclidean_single",             IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_F32, 0, 0.0},
+  {EUC_OP_DOUBLE,             "pairwise_euclidean_double",             IN_F64,  G_SIMT_F64, SR_NONE, NM_F64_FMA,   FM_F64,        FL_NONE, RC_NONE,      OUT_F64, 0, 0.0},
+  {EUC_OP_MIX_FP16_FP64,      "pairwise_euclidean_fp16_fp64",          IN_F32,  G_TC_F16,   SR_F16,  NM_LOW_F16,   FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_MIX_BF16_FP64,      "pairwise_euclidean_bf16_fp64",          IN_F32,  G_TC_BF16,  SR_BF16, NM_LOW_BF16,  FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-7},
+  {EUC_OP_MIX_TF32_FP64,      "pairwise_euclidean_tf32_fp64",          IN_F32,  G_TC_TF32,  SR_NONE, NM_F32_FMA,   FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_MIX_FP32_FP64,      "pairwise_euclidean_fp32_fp64",          IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_FMA,   FM_F32,        FL_F32,  RC_F64,       OUT_F32, 1, 0x1p-23},
+  {EUC_OP_MIX_FP16_FP16,      "pairwise_euclidean_fp16_fp16",          IN_F32,  G_TC_F16,   SR_F16,  NM_LOW_F16,   FM_F32,        FL_F32,  RC_F16_ARITH, OUT_F32, 0, 0x1p-11},
+  {EUC_OP_MIX_FP16_FP32,      "pairwise_euclidean_fp16_fp32",          IN_F32,  G_TC_F16,   SR_F16,  NM_LOW_F16,   FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_MIX_BF16_BF16,      "pairwise_euclidean_bf16_bf16",          IN_F32,  G_TC_BF16,  SR_BF16, NM_LOW_BF16,  FM_F32,        FL_F32,  RC_BF16_ARITH,OUT_F32, 0, 0x1p-7},
+  {EUC_OP_MIX_BF16_FP32,      "pairwise_euclidean_bf16_fp32",          IN_F32,  G_TC_BF16,  SR_BF16, NM_LOW_BF16,  FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-7},
+  {EUC_OP_MIX_FP32_FP32,      "pairwise_euclidean_fp32_fp32",          IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_FMA,   FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-23},
+  {EUC_OP_TILED_FP16_FP64,    "pairwise_euclidean_tiled_fp16_fp64",    IN_F32,  G_TC_F16,   SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_TILED_FP16_FP32,    "pairwise_euclidean_tiled_fp16_fp32",    IN_F32,  G_TC_F16,   SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_TILED_BF16_FP64,    "pairwise_euclidean_tiled_bf16_fp64",    IN_F32,  G_TC_BF16,  SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-8},
+  {EUC_OP_TILED_BF16_FP32,    "pairwise_euclidean_tiled_bf16_fp32",    IN_F32,  G_TC_BF16,  SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-8},
+  {EUC_OP_TILED_FP32_FP64,    "pairwise_euclidean_tiled_fp32_fp64",    IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-23},
+  {EUC_OP_TILED_FP32_FP32,    "pairwise_euclidean_tiled_fp32_fp32",    IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-23},
+  {EUC_OP_TC_FP16_FP64,       "pairwise_euclidean_tensorcore_fp16_fp64", IN_F32, G_TC_F16,  SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_TC_FP16_FP32,       "pairwise_euclidean_tensorcore_fp16_fp32", IN_F32, G_TC_F16,  SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-11},
+  {EUC_OP_TC_BF16_FP64,       "pairwise_euclidean_tensorcore_bf16_fp64", IN_F32, G_TC_BF16, SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F64,       OUT_F32, 0, 0x1p-8},
+  {EUC_OP_TC_BF16_FP32,       "pairwise_euclidean_tensorcore_bf16_fp32", IN_F32, G_TC_BF16, SR_NONE, NM_F32_SUMSQ, FM_F32,        FL_F32,  RC_F32,       OUT_F32, 0, 0x1p-8},
+  {EUC_OP_UNI_FP16,           "pairwise_euclidean_uniform_fp16",       IN_F16,  G_TC_F16,   SR_F16,  NM_LOW_F16,   FM_F32,        FL_NONE, RC_NONE,      OUT_F16, 0, 0.0},
+  {EUC_OP_UNI_BF16,           "pairwise_euclidean_uniform_bf16",       IN_BF16, G_TC_BF16,  SR_BF16, NM_LOW_BF16,  FM_F32,        FL_NONE, RC_NONE,      OUT_BF16,0, 0.0},
+  {EUC_OP_UNI_TF32,           "pairwise_euclidean_uniform_tf32",       IN_F32,  G_SIMT_F32, SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_F32, 0, 0.0},
+  {EUC_OP_UNI_FP16_DIRECT,    "pairwise_euclidean_uniform_fp16_direct", IN_F16, G_DIRECT,   SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_F16, 0, 0.0},
+  {EUC_OP_UNI_BF16_DIRECT,    "pairwise_euclidean_uniform_bf16_direct", IN_BF16,G_DIRECT,   SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_BF16,0, 0.0},
+  {EUC_OP_UNI_TF32_DIRECT,    "pairwise_euclidean_uniform_tf32_direct", IN_F32, G_DIRECT,   SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_F32, 0, 0.0},
+  {EUC_OP_UNI_FP32_DIRECT,    "pairwise_euclidean_uniform_fp32_direct", IN_F32, G_DIRECT,   SR_NONE, NM_F32_FMA,   FM_F32,        FL_NONE, RC_NONE,      OUT_F32, 0, 0.0},
+  {EUC_OP_UNI_FP64_DIRECT,    "pairwise_euclidean_uniform_fp64_direct", IN_F64, G_DIRECT,   SR_NONE, NM_F64_FMA,   FM_F64,        FL_NONE, RC_NONE,      OUT_F64, 0, 0.0},
+  {EUC_OP_ADV_FP64_FP16,      "pairwise_euclidean_fp64_fp16",          IN_F16,  G_SIMT_F64, SR_NONE, NM_F32_FMA,   FM_F64_TO_F32, FL_F32,  RC_F64,       OUT_F32, 1, 0x1p-23},
+  {EUC_OP_ADV_FP64_BF16,      "pairwise_euclidean_fp64_bf16",          IN_BF16, G_SIMT_F64, SR_NONE, NM_F32_FMA,   FM_F64_TO_F32, FL_F32,  RC_F64,       OUT_F32, 1, 0x1p-23},
+  {EUC_OP_ADV_FP64_TF32,      "pairwise_euclidean_fp64_tf32",          IN_F32,  G_SIMT_F32, SR_NONE, NM_F64_FMA,   FM_F64,        FL_F64,  RC_F64,       OUT_F64, 2, 0x1p-52},
+  {EUC_OP_ADV_FP64_FP32_GEMM, "pairwise_euclidean_fp64_fp32_gemm",     IN_F64,  G_SIMT_F32, SR_NONE, NM_F64_FMA,   FM_F64,        FL_F64,  RC_F64,       OUT_F64, 2, 0x1p-52},
+};
+// clang-format on
+
+const OpSpec* find_op(int op) {
+  for (const auto& s : kOps)
+    if (s.op == op) return &s;
+  return nullptr;
+}
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+static int fail(int status, const std::string& msg) {
+  g_err = msg;
+  return status;
+}
+static int ok() { return EUC_OK; }
+static int cuda_fail(cudaError_t e, const char* where) {
+  return fail(EUC_ERR_LAUNCH, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------ device info
+static int g_sms[64];
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (g_sms[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    g_sms[dev] = v > 0 ? v : 1;
+  }
+  return g_sms[dev];
+}
+int tc_error_and_clear();
+int device_error_and_clear() { return tc_error_and_clear(); }
+
+bool device_is_sm100() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+// ------------------------------------------------------------------ timing
+static bool g_timing = false;
+static cudaEvent_t g_ev0 = nullptr, g_ev1 = nullptr;
+static bool g_ev_recorded = false;
+static const char* g_ev_name = "";
+void timing_begin(cudaStream_t st, const char* name) {
+  if (!g_timing) return;
+  if (!g_ev0) {
+    cudaEventCreate(&g_ev0);
+    cudaEventCreate(&g_ev1);
+  }
+  g_ev_name = name;
+  cudaEventRecord(g_ev0, st);
+}
+void timing_end(cudaStream_t st) {
+  if (!g_timing || !g_ev1) return;
+  cudaEventRecord(g_ev1, st);
+  g_ev_recorded = true;
+}
+
+// ------------------------------------------------------------------ workspace
+static inline size_t al(size_t b) { return (b + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t hdr, pp, cc, plow, clow, list, key, val64, idx64, total;
+  unsigned long long cap;
+  int ldlow;
+};
+
+static int low_esize(const OpSpec* s) { return s->gemm == G_TC_TF32 ? 4 : 2; }
+static bool is_tc(const OpSpec* s) { return s->gemm == G_TC_F16 || s->gemm == G_TC_BF16 || s->gemm == G_TC_TF32; }
+
+static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, bool argmin) {
+  Layout L{};
+  const size_t nsz = (s->form == FM_F64) ? 8 : 4;
+  const int es = low_esize(s);
+  const int per_box = 128 / es;
+  L.ldlow = static_cast<int>(((dim + per_box - 1) / per_box) * per_box);
+  size_t off = 0;
+  L.hdr = off; off += 256;
+  L.pp = off; off += al(static_cast<size_t>(n) * nsz);
+  L.cc = off; off += al(static_cast<size_t>(m) * nsz);
+  if (is_tc(s)) {
+    L.plow = off; off += al(static_cast<size_t>(n) * L.ldlow * es);
+    L.clow = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
+  }
+  L.cap = 0;
+  if (s->flag != FL_NONE) {
+    const unsigned long long nm = static_cast<unsigned long long>(n) * static_cast<unsigned long long>(m);
+    unsigned long long cap = nm / 256;
+    cap = std::max<unsigned long long>(cap, 1ull << 16);
+    cap = std::min<unsigned long long>(cap, 1ull << 26);
+    cap = std::min<unsigned long long>(cap, nm);
+    L.cap = cap;
+    L.list = off; off += al(cap * 8);
+  }
+  if (argmin) {
+    if (s->form == FM_F64 && s->flag == FL_NONE) {
+      L.val64 = off; off += al(static_cast<size_t>(n) * 8);
+      L.idx64 = off; off += al(static_cast<size_t>(n) * 8);
+    } else {
+      L.key = off; off += al(static_cast<size_t>(n) * 8);
+    }
+  }
+  L.total = off;
+  return L;
+}
+
+static double k_double(const OpSpec* s, float kappa, int64_t dim) {
+  if (s->kform == 2) return (static_cast<double>(kappa) * 2.0) * (static_cast<double>(dim) * s->u);
+  return 0.0;
+}
+static float k_float(const OpSpec* s, float kappa, int64_t dim) {
+  const float u = static_cast<float>(s->u);
+  if (s->kform == 0) {
+    const int r = 2 * static_cast<int>(dim) + 4;
+    const float gamma_r = static_cast<float>(r) * u;
+    return kappa * gamma_r;
+  }
+  if (s->kform == 1) {
+    const float gamma_n = static_cast<float>(static_cast<int>(dim)) * u;
+    return (kappa * 2.f) * gamma_n;
+  }
+  return 0.f;
+}
+
+struct RunOut {
+  void* D = nullptr;                 // D mode
+  int64_t* labels = nullptr;         // argmin mode
+  int32_t* labels32 = nullptr;
+  void* min_dist = nullptr;
+  uint64_t* d_count = nullptr;
+  int32_t* tile_counts = nullptr;
+  int tile_T = 0;
+};
+
+static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
+                        float kappa, const RunOut& o, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (n < 0 || m < 0 || dim < 0) return fail(EUC_ERR_SHAPE, "negative size");
+  if (dim > (1 << 20) || m > 0xffffffffll || n > 0xffffffffll)
+    return fail(EUC_ERR_SHAPE, "shape too large");
+  const bool argmin = (o.D == nullptr);
+  if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
+  if (n == 0 || m == 0) {
+    if (o.d_count) cudaMemsetAsync(o.d_count, 0, 8, st);
+    return ok();
+  }
+  if (!P || !C) return fail(EUC_ERR_ARG, "null input pointer");
+  if (dim == 0) return fail(EUC_ERR_SHAPE, "dim must be >= 1");
+  if (s->gemm == G_DIRECT) {
+    if (argmin) return fail(EUC_ERR_UNSUPPORTED, "direct operators have no fused argmin");
+    cudaError_t e = launch_direct(s, P, C, n, m, static_cast<int>(dim), o.D, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, s->name);
+  }
+  const Layout L = layout_for(s, n, m, dim, argmin);
+  if (!ws || ws_bytes < L.total)
+    return fail(EUC_ERR_WORKSPACE, std::string(s->name) + ": workspace of " + std::to_string(L.total) +
+                                       " bytes required, got " + std::to_string(ws_bytes));
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  DistJob j{};
+  j.spec = s;
+  j.P = P;
+  j.C = C;
+  j.n = n;
+  j.m = m;
+  j.dim = static_cast<int>(dim);
+  j.kf = k_float(s, kappa, dim);
+  j.kd = k_double(s, kappa, dim);
+  j.D = o.D;
+  j.count = o.d_count ? reinterpret_cast<unsigned long long*>(o.d_count)
+                      : reinterpret_cast<unsigned long long*>(w + L.hdr);
+  j.list = s->flag != FL_NONE ? reinterpret_cast<unsigned long long*>(w + L.list) : nullptr;
+  j.list_cap = L.cap;
+  j.tile_counts = o.tile_counts;
+  j.tile_T = o.tile_T;
+  j.tiles_j = o.tile_T > 0 ? (m + o.tile_T - 1) / o.tile_T : 0;
+  j.pp = w + L.pp;
+  j.cc = w + L.cc;
+  j.Plow = is_tc(s) ? w + L.plow : nullptr;
+  j.Clow = is_tc(s) ? w + L.clow : nullptr;
+  j.ldlow = L.ldlow;
+  j.row_key = (argmin && L.key) ? reinterpret_cast<unsigned long long*>(w + L.key) : nullptr;
+  j.row_val64 = (argmin && L.val64) ? reinterpret_cast<double*>(w + L.val64) : nullptr;
+  j.row_idx64 = (argmin && L.idx64) ? reinterpret_cast<long long*>(w + L.idx64) : nullptr;
+  j.stream = st;
+
+  cudaError_t e = cudaMemsetAsync(j.count, 0, 8, st);
+  if (e == cudaSuccess && o.tile_counts) {
+    const int64_t nt = ((n + o.tile_T - 1) / o.tile_T) * j.tiles_j;
+    e = cudaMemsetAsync(o.tile_counts, 0, static_cast<size_t>(nt) * 4, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  e = launch_prep(j, true, is_tc(s));
+  if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
+  if (e != cudaSuccess) return cuda_fail(e, "prep");
+  e = is_tc(s) ? launch_tc(j) : launch_simt(j);
+  if (e != cudaSuccess) return cuda_fail(e, s->name);
+  e = launch_recompute(j);
+  if (e != cudaSuccess) return cuda_fail(e, "recompute");
+  if (argmin) {
+    if (j.row_key) {
+      e = launch_keys_to_labels(j.row_key, n, o.labels, o.labels32, static_cast<float*>(o.min_dist), st);
+    } else {
+      e = launch_f64_to_labels(j.row_idx64, n, o.labels, o.labels32, st);
+      if (e == cudaSuccess && o.min_dist)
+        e = cudaMemcpyAsync(o.min_dist, j.row_val64, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToDevice, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "labels");
+  }
+  return ok();
+}
+
+static int run_named(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa,
+                     const RunOut& o, void* ws, size_t ws_bytes, void* stream) {
+  const OpSpec* s = find_op(op);
+  if (!s) return fail(EUC_ERR_ARG, "unknown operator id");
+  if (!o.D) return fail(EUC_ERR_ARG, std::string(s->name) + ": null output D");
+  return run_distance(s, P, C, n, m, dim, kappa, o, ws, ws_bytes, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace euc
+
+using namespace euc;
+
+// ==================================================================== C ABI
+extern "C" {
+
+const char* euc_version(void) { return "euclid_b200 0.1 (sm_100a)"; }
+
+const char* euc_status_string(int s) {
+  switch (s) {
+    case EUC_OK: return "ok";
+    case EUC_ERR_SHAPE: return "bad shape";
+    case EUC_ERR_DTYPE: return "bad dtype";
+    case EUC_ERR_UNSUPPORTED: return "unsupported argument";
+    case EUC_ERR_LAUNCH: return "CUDA launch error";
+    case EUC_ERR_TIMEOUT: return "device wait timed out";
+    case EUC_ERR_WORKSPACE: return "workspace too small";
+    case EUC_ERR_ARG: return "invalid argument";
+    case EUC_ERR_DEVICE: return "unsupported device";
+  }
+  return "unknown status";
+}
+
+const char* euc_last_error(void) { return g_err.c_str(); }
+
+int euc_device_check(void) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "device_check");
+  const int v = device_error_and_clear();
+  if (v != 0) return fail(EUC_ERR_TIMEOUT, "a bounded device wait expired (code " + std::to_string(v) + ")");
+  return EUC_OK;
+}
+
+size_t euc_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim) {
+  if (op == EUC_OP_CENTERS_FP32 || op == EUC_OP_CENTERS_FP64)
+    return al(static_cast<size_t>(m) * (dim + 1) * 8) + center_ws_bytes(n, dim, m);
+  const OpSpec* s = find_op(op);
+  if (!s) return 0;
+  if (s->gemm == G_DIRECT) return 0;
+  return layout_for(s, n, m, dim, false).total;
+}
+
+size_t euc_argmin_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim) {
+  const OpSpec* s = find_op(op);
+  if (!s || s->gemm == G_DIRECT) return 0;
+  return layout_for(s, n, m, dim, true).total;
+}
+
+void euc_set_kernel_timing(int enable) { g_timing = enable != 0; }
+
+float euc_last_kernel_ms(void) {
+  if (!g_ev_recorded) return -1.f;
+  float ms = -1.f;
+  if (cudaEventSynchronize(g_ev1) != cudaSuccess) return -1.f;
+  cudaEventElapsedTime(&ms, g_ev0, g_ev1);
+  return ms;
+}
+
+const char* euc_last_kernel_name(void) { return g_ev_name; }
+
+int euc_pairwise_single(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float* D, void* ws,
+                        size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  return run_named(EUC_OP_SINGLE, P, C, n, m, dim, 0.f, o, ws, ws_bytes, stream);
+}
+int euc_pairwise_double(const double* P, const double* C, int64_t n, int64_t m, int64_t dim, double* D, void* ws,
+                        size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  return run_named(EUC_OP_DOUBLE, P, C, n, m, dim, 0.f, o, ws, ws_bytes, stream);
+}
+
+#define EUC_MIX_DEF(fname, OPID)                                                                        \
+  int fname(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa, float* D,   \
+            uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {                               \
+    RunOut o;                                                                                            \
+    o.D = D;                                                                                             \
+    o.d_count = d_count;                                                                                 \
+    return run_named(OPID, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);                             \
+  }
+EUC_MIX_DEF(euc_mix_fp16_fp64, EUC_OP_MIX_FP16_FP64)
+EUC_MIX_DEF(euc_mix_bf16_fp64, EUC_OP_MIX_BF16_FP64)
+EUC_MIX_DEF(euc_mix_tf32_fp64, EUC_OP_MIX_TF32_FP64)
+EUC_MIX_DEF(euc_mix_fp32_fp64, EUC_OP_MIX_FP32_FP64)
+EUC_MIX_DEF(euc_mix_fp16_fp16, EUC_OP_MIX_FP16_FP16)
+EUC_MIX_DEF(euc_mix_fp16_fp32, EUC_OP_MIX_FP16_FP32)
+EUC_MIX_DEF(euc_mix_bf16_bf16, EUC_OP_MIX_BF16_BF16)
+EUC_MIX_DEF(euc_mix_bf16_fp32, EUC_OP_MIX_BF16_FP32)
+EUC_MIX_DEF(euc_mix_fp32_fp32, EUC_OP_MIX_FP32_FP32)
+#undef EUC_MIX_DEF
+
+// tile_size rules of euclidean_kernels_tiled.cu:331-336
+static int tiled_tile(int tile_size, int64_t dim, int* T) {
+  if (tile_size <= 0) tile_size = dim <= 128 ? 32 : 16;
+  if (tile_size != 16 && tile_size != 32) return fail(EUC_ERR_UNSUPPORTED, "Supported tile_size: 16 or 32");
+  if (dim > 512) return fail(EUC_ERR_UNSUPPORTED, "D too large for full caching (max 512)");
+  *T = tile_size;
+  return EUC_OK;
+}
+
+#define EUC_TILED_DEF(fname, OPID)                                                                          \
+  int fname(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa, int tile_size,  \
+            float* D, int32_t* d_tile_counts, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) { \
+    int T = 0;                                                                                               \
+    int rc = tiled_tile(tile_size, dim, &T);                                                                 \
+    if (rc != EUC_OK) return rc;                                                                             \
+    RunOut o;                                                                                                \
+    o.D = D;                                                                                                 \
+    o.d_count = d_count;                                                                                     \
+    o.tile_counts = d_tile_counts;                                                                           \
+    o.tile_T = T;                                                                                            \
+    return run_named(OPID, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);                                 \
+  }
+EUC_TILED_DEF(euc_tiled_fp16_fp64, EUC_OP_TILED_FP16_FP64)
+EUC_TILED_DEF(euc_tiled_fp16_fp32, EUC_OP_TILED_FP16_FP32)
+EUC_TILED_DEF(euc_tiled_bf16_fp64, EUC_OP_TILED_BF16_FP64)
+EUC_TILED_DEF(euc_tiled_bf16_fp32, EUC_OP_TILED_BF16_FP32)
+EUC_TILED_DEF(euc_tiled_fp32_fp64, EUC_OP_TILED_FP32_FP64)
+EUC_TILED_DEF(euc_tiled_fp32_fp32, EUC_OP_TILED_FP32_FP32)
+#undef EUC_TILED_DEF
+
+// tile_size / dim rules of euclidean_kernels_tiled_tc.cu:246-248
+#define EUC_TC_DEF(fname, OPID)                                                                             \
+  int fname(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa, int tile_size,  \
+            float* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {                         \
+    if (tile_size <= 0) tile_size = 32;                                                                      \
+    if (tile_size != 32) return fail(EUC_ERR_UNSUPPORTED, "This fixed kernel supports tile_size=32 only");   \
+    if (dim % 16 != 0)                                                                                       \
+      return fail(EUC_ERR_UNSUPPORTED, "For WMMA path, D must be multiple of 16 (pad input if needed)");     \
+    RunOut o;                                                                                                \
+    o.D = D;                                                                                                 \
+    o.d_count = d_count;                                                                                     \
+    return run_named(OPID, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);                                 \
+  }
+EUC_TC_DEF(euc_tensorcore_fp16_fp64, EUC_OP_TC_FP16_FP64)
+EUC_TC_DEF(euc_tensorcore_fp16_fp32, EUC_OP_TC_FP16_FP32)
+EUC_TC_DEF(euc_tensorcore_bf16_fp64, EUC_OP_TC_BF16_FP64)
+EUC_TC_DEF(euc_tensorcore_bf16_fp32, EUC_OP_TC_BF16_FP32)
+#undef EUC_TC_DEF
+
+int euc_uniform_fp16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim, uint16_t* D, void* ws,
+                     size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  return run_named(EUC_OP_UNI_FP16, P, C, n, m, dim, 0.f, o, ws, ws_bytes, stream);
+}
+int euc_uniform_bf16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim, uint16_t* D, void* ws,
+                     size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  return run_named(EUC_OP_UNI_BF16, P, C, n, m, dim, 0.f, o, ws, ws_bytes, stream);
+}
+int euc_uniform_tf32(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float* D, void* ws,
+                     size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  return run_named(EUC_OP_UNI_TF32, P, C, n, m, dim, 0.f, o, ws, ws_bytes, stream);
+}
+
+#define EUC_DIRECT_DEF(fname, OPID, T)                                                                  \
+  int fname(const T* P, const T* C, int64_t n, int64_t m, int64_t dim, T* D, void* stream) {            \
+    RunOut o;                                                                                            \
+    o.D = D;                                                                                             \
+    return run_named(OPID, P, C, n, m, dim, 0.f, o, nullptr, 0, stream);                                 \
+  }
+EUC_DIRECT_DEF(euc_uniform_fp16_direct, EUC_OP_UNI_FP16_DIRECT, uint16_t)
+EUC_DIRECT_DEF(euc_uniform_bf16_direct, EUC_OP_UNI_BF16_DIRECT, uint16_t)
+EUC_DIRECT_DEF(euc_uniform_tf32_direct, EUC_OP_UNI_TF32_DIRECT, float)
+EUC_DIRECT_DEF(euc_uniform_fp32_direct, EUC_OP_UNI_FP32_DIRECT, float)
+EUC_DIRECT_DEF(euc_uniform_fp64_direct, EUC_OP_UNI_FP64_DIRECT, double)
+#undef EUC_DIRECT_DEF
+
+int euc_advanced_fp64_fp16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim, float kappa,
+                           float* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  o.d_count = d_count;
+  return run_named(EUC_OP_ADV_FP64_FP16, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);
+}
+int euc_advanced_fp64_bf16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim, float kappa,
+                           float* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  o.d_count = d_count;
+  return run_named(EUC_OP_ADV_FP64_BF16, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);
+}
+int euc_advanced_fp64_tf32(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa,
+                           double* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  o.d_count = d_count;
+  return run_named(EUC_OP_ADV_FP64_TF32, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);
+}
+int euc_advanced_fp64_fp32_gemm(const double* P, const double* C, int64_t n, int64_t m, int64_t dim, float kappa,
+                                double* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream) {
+  RunOut o;
+  o.D = D;
+  o.d_count = d_count;
+  return run_named(EUC_OP_ADV_FP64_FP32_GEMM, P, C, n, m, dim, kappa, o, ws, ws_bytes, stream);
+}
+
+int euc_read_count_i32(const int32_t* d_counter, int32_t* host_out) {
+  if (!d_counter || !host_out) return fail(EUC_ERR_ARG, "null pointer");
+  cudaError_t e = cudaMemcpy(host_out, d_counter, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "read_count");
+}
+int euc_read_count_u64(const uint64_t* d_counter, uint64_t* host_out) {
+  if (!d_counter || !host_out) return fail(EUC_ERR_ARG, "null pointer");
+  cudaError_t e = cudaMemcpy(host_out, d_counter, sizeof(uint64_t), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "read_count");
+}
+
+// ------------------------------------------------------------------ centers
+static int centers_impl(const void* X, bool f64, const int64_t* labels, int64_t n, int64_t dim, int64_t k,
+                        void* centers, int64_t* d_counts, void* ws, size_t ws_bytes, void* stream) {
+  if (n < 0 || dim < 0 || k < 0) return fail(EUC_ERR_SHAPE, "negative size");
+  if (k == 0 || dim == 0) return EUC_OK;
+  if (dim > 1024) return fail(EUC_ERR_UNSUPPORTED, "dim > 1024 not supported by the center update");
+  if (k > 0x7fffffffll) return fail(EUC_ERR_SHAPE, "too many clusters");
+  if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
+  if (!centers || (n > 0 && (!X || !labels))) return fail(EUC_ERR_ARG, "null pointer");
+  const size_t stats_b = al(static_cast<size_t>(k) * (dim + 1) * 8);
+  const size_t need = stats_b + center_ws_bytes(n, dim, k);
+  if (!ws || ws_bytes < need)
+    return fail(EUC_ERR_WORKSPACE, "update_centers: workspace of " + std::to_string(need) + " bytes required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  double* stats = static_cast<double*>(ws);
+  cudaError_t e = launch_center_stats(X, f64, labels, true, n, dim, k, stats, static_cast<uint8_t*>(ws) + stats_b,
+                                      ws_bytes - stats_b, st);
+  if (e == cudaSuccess) e = launch_center_finalize(stats, dim, k, centers, f64, nullptr, 0, st);
+  if (e == cudaSuccess && d_counts) {
+    // counts column -> int64 (strided copy: one element per (dim+1)-wide row)
+    e = cudaMemcpy2DAsync(d_counts, sizeof(int64_t), stats + dim, (dim + 1) * sizeof(double), sizeof(double), k,
+                          cudaMemcpyDeviceToDevice, st);
+  }
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "update_centers");
+}
+
+int euc_update_centers_fp32(const float* X, const int64_t* labels, int64_t n, int64_t dim, int64_t k, float* centers,
+                            int64_t* d_counts, void* ws, size_t ws_bytes, void* stream) {
+  return centers_impl(X, false, labels, n, dim, k, centers, d_counts, ws, ws_bytes, stream);
+}
+int euc_update_centers_fp64(const double* X, const int64_t* labels, int64_t n, int64_t dim, int64_t k,
+                            double* centers, int64_t* d_counts, void* ws, size_t ws_bytes, void* stream) {
+  return centers_impl(X, true, labels, n, dim, k, centers, d_counts, ws, ws_bytes, stream);
+}
+
+size_t euc_center_stats_workspace_bytes(int64_t n, int64_t dim, int64_t k) { return center_ws_bytes(n, dim, k); }
+
+int euc_center_stats(const void* X, int x_is_f64, const void* labels, int labels_are_i64, int64_t n, int64_t dim,
+                     int64_t k, double* stats, void* ws, size_t ws_bytes, void* stream) {
+  if (n < 0 || dim <= 0 || k <= 0) return fail(EUC_ERR_SHAPE, "bad size");
+  if (dim > 1024) return fail(EUC_ERR_UNSUPPORTED, "dim > 1024 not supported by the center update");
+  if (!stats || (n > 0 && (!X || !labels))) return fail(EUC_ERR_ARG, "null pointer");
+  if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
+  if (ws_bytes < center_ws_bytes(n, dim, k) || !ws)
+    return fail(EUC_ERR_WORKSPACE, "center_stats: workspace too small");
+  cudaError_t e = launch_center_stats(X, x_is_f64 != 0, labels, labels_are_i64 != 0, n, dim, k, stats, ws, ws_bytes,
+                                      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "center_stats");
+}
+
+int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* centers, int centers_are_f64,
+                        const void* prev, int empty_policy, void* stream) {
+  if (dim <= 0 || k <= 0) return fail(EUC_ERR_SHAPE, "bad size");
+  if (!stats || !centers) return fail(EUC_ERR_ARG, "null pointer");
+  if (empty_policy == 1 && !prev) return fail(EUC_ERR_ARG, "empty_policy 1 needs prev centers");
+  cudaError_t e = launch_center_finalize(stats, dim, k, centers, centers_are_f64 != 0, prev, empty_policy,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "center_finalize");
+}
+
+// ------------------------------------------------------------------ fused argmin
+int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa,
+               int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count, void* ws, size_t ws_bytes,
+               void* stream) {
+  const OpSpec* s = find_op(op);
+  if (!s) return fail(EUC_ERR_ARG, "unknown operator id");
+  const bool allowed = op == EUC_OP_SINGLE || op == EUC_OP_DOUBLE || (op >= EUC_OP_MIX_FP16_FP64 && op <= EUC_OP_MIX_FP32_FP32) ||
+                       (op >= EUC_OP_TILED_FP16_FP64 && op <= EUC_OP_TILED_FP32_FP32) ||
+                       (op >= EUC_OP_TC_FP16_FP64 && op <= EUC_OP_TC_BF16_FP32);
+  if (!allowed) return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) + ": no fused argmin form");
+  if (m > 0xffffffffll) return fail(EUC_ERR_SHAPE, "too many centers");
+  RunOut o;
+  o.labels = labels;
+  o.labels32 = labels32;
+  o.min_dist = min_dist;
+  o.d_count = d_count;
+  return run_distance(s, P, C, n, m, dim, kappa, o, ws, ws_bytes, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

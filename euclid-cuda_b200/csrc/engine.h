@@ -1,0 +1,129 @@
+// Internal interface of the distance engine: the per-operator numeric recipe
+// (which rounding, which GEMM, which cancellation test, which recompute) and the
+// launchers of the individual kernels.  The C ABI (api.cu) maps every reference
+// entry point onto one OpSpec row and runs it through run_distance().
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace euc {
+
+enum InType { IN_F32 = 0, IN_F16 = 1, IN_BF16 = 2, IN_F64 = 3 };
+// How S = P.C^T is produced.
+enum Gemm {
+  G_TC_F16 = 0,    // tcgen05 kind::f16, fp16 operands, fp32 accumulate
+  G_TC_BF16 = 1,   // tcgen05 kind::f16, bf16 operands, fp32 accumulate
+  G_TC_TF32 = 2,   // tcgen05 kind::tf32, fp32 operands rounded to tf32, fp32 accumulate
+  G_SIMT_F32 = 3,  // CUDA-core fp32 FMA, inputs rounded to fp32
+  G_SIMT_F64 = 4,  // CUDA-core fp64 FMA, inputs widened to fp64
+  G_DIRECT = 5     // no GEMM: direct sum of squared differences
+};
+// Rounding applied to S before the distance is formed (the reference's cuBLAS
+// GEMM writes S in the low precision, euclidean_kernels_mix.cu:538).
+enum SRound { SR_NONE = 0, SR_F16 = 1, SR_BF16 = 2 };
+enum Norm {
+  NM_LOW_F16 = 0,   // fp32 fmaf over fp16-rounded values, result stored as fp16 (mix.cu:106-119)
+  NM_LOW_BF16 = 1,  // same for bf16 (mix.cu:122-135)
+  NM_F32_FMA = 2,   // fp32 fmaf over fp32 values (euclidean_kernels.cu:16-26)
+  NM_F32_SUMSQ = 3, // sum of fp32-rounded squares: (P*P).sum(1) (tiled.cu:338)
+  NM_F64_FMA = 4    // fp64 fma over fp64 values (euclidean_kernels.cu:28-38)
+};
+enum Form {
+  FM_F32 = 0,        // d = max((pp - 2s) + cc, 0) in fp32
+  FM_F64 = 1,        // same in fp64
+  FM_F64_TO_F32 = 2  // fp64 formula on fp32 norms, result rounded to fp32 (advanced.cu:103-115)
+};
+enum Flag { FL_NONE = 0, FL_F32 = 1, FL_F64 = 2 };
+// Recompute of flagged pairs (the "fallback" kernels).
+enum Rec {
+  RC_NONE = 0,
+  RC_F64 = 1,        // direct formula, fp64 FMA, on the inputs widened to fp64 (mix.cu:156-177)
+  RC_F32 = 2,        // direct formula, fp32 FMA on fp32 inputs (mix.cu:481-504)
+  RC_F16_ARITH = 3,  // direct formula in fp16 arithmetic on the fp16-rounded inputs (mix.cu:412-439)
+  RC_BF16_ARITH = 4  // same in bf16 arithmetic (mix.cu:442-469)
+};
+enum Out { OUT_F32 = 0, OUT_F16 = 1, OUT_BF16 = 2, OUT_F64 = 3 };
+
+struct OpSpec {
+  int op;
+  const char* name;
+  InType in;
+  Gemm gemm;
+  SRound sround;
+  Norm norm;
+  Form form;
+  Flag flag;
+  Rec rec;
+  Out out;
+  // Cancellation threshold: eps = K * (pp + cc) with K built exactly as the
+  // reference's float expression, either
+  //   kform 0: K = kappa * ((float)(2*dim+4) * u)            (mix.cu:207-211, tiled.cu:133,201)
+  //   kform 1: K = (kappa * 2) * ((float)dim * u)            (euclidean_kernels.cu:71, mix.cu:930-931)
+  //   kform 2: K = ((double)kappa * 2.0) * ((double)dim * u) (advanced.cu:138,353)
+  int kform;
+  double u;
+};
+
+const OpSpec* find_op(int op);
+
+// Distance job: everything the launchers need, resolved from an OpSpec.
+struct DistJob {
+  const OpSpec* spec;
+  const void* P;
+  const void* C;
+  int64_t n, m;
+  int dim;
+  float kf;    // flag constant (fp32 forms)
+  double kd;   // flag constant (fp64 forms)
+  // outputs
+  void* D;                       // D mode (null in argmin mode)
+  unsigned long long* row_key;   // argmin mode (fp32 distances)
+  double* row_val64;             // argmin mode, fp64 distances (no flag ops)
+  long long* row_idx64;          // argmin mode, fp64 distances
+  unsigned long long* count;     // flagged-pair counter (device)
+  unsigned long long* list;      // flagged (i<<32|j) entries
+  unsigned long long list_cap;
+  int32_t* tile_counts;          // nullable
+  int tile_T;
+  int64_t tiles_j;
+  // workspace-resident intermediates
+  void* pp;                      // fp32 or fp64 norms
+  void* cc;
+  void* Plow;                    // padded low-precision copies (tcgen05 path)
+  void* Clow;
+  int ldlow;                     // padded row length (elements)
+  cudaStream_t stream;
+};
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_prep(const DistJob& j, bool points, bool make_low);
+cudaError_t launch_tc(const DistJob& j);
+cudaError_t launch_simt(const DistJob& j);
+cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
+                          void* D, cudaStream_t st);
+cudaError_t launch_recompute(const DistJob& j);
+cudaError_t launch_keys_to_labels(const unsigned long long* keys, int64_t n, int64_t* labels, int32_t* labels32,
+                                  float* mind, cudaStream_t st);
+cudaError_t launch_f64_to_labels(const long long* idx, int64_t n, int64_t* labels, int32_t* labels32,
+                                 cudaStream_t st);
+cudaError_t launch_fill_u64(unsigned long long* p, int64_t n, unsigned long long v, cudaStream_t st);
+
+// Center statistics (k x (dim+1) fp64 rows: sums then count).
+size_t center_ws_bytes(int64_t n, int64_t dim, int64_t k);
+cudaError_t launch_center_stats(const void* X, bool x_f64, const void* labels, bool labels_i64, int64_t n,
+                                int64_t dim, int64_t k, double* stats, void* ws, size_t ws_bytes,
+                                cudaStream_t st);
+cudaError_t launch_center_finalize(const double* stats, int64_t dim, int64_t k, void* centers, bool f64,
+                                   const void* prev, int empty_policy, cudaStream_t st);
+
+// Kernel timing hook (api.cu).
+void timing_begin(cudaStream_t st, const char* name);
+void timing_end(cudaStream_t st);
+
+int num_sms();
+bool device_is_sm100();
+int device_error_and_clear();
+
+}  // namespace euc

@@ -1,0 +1,179 @@
+// Row preparation: squared norms with the reference's exact accumulation order and,
+// for the tensor-core path, a zero-padded low-precision copy whose rows are a whole
+// number of 128-byte TMA boxes.
+//
+// Norm recipes (all accumulate k = 0 .. dim-1 in order, one row per thread):
+//   NM_LOW_F16 / NM_LOW_BF16: s = fmaf(h, h, s) over h = low(x), stored low
+//                             (compute_norms_fp16_uniform, euclidean_kernels_mix.cu:106-135)
+//   NM_F32_FMA:   s = fmaf(x, x, s)            (compute_norms_rowmajor_float, euclidean_kernels.cu:16-26)
+//   NM_F32_SUMSQ: s = s + fl(x*x)              ((P*P).sum(1), euclidean_kernels_tiled.cu:338)
+//   NM_F64_FMA:   s = fma(x, x, s) in fp64     (compute_norms_rowmajor_double, euclidean_kernels.cu:28-38)
+//
+// Layout: a warp owns 32 rows; 32-column slabs are read coalesced into a padded
+// shared tile (33 words per row, conflict-free transposed reads), then lane r folds
+// row r's slab into its running norm and the slab is written back out as the low copy.
+#include "common.cuh"
+#include "engine.h"
+
+namespace euc {
+
+template <typename T> __device__ __forceinline__ double to_d(T x);
+template <> __device__ __forceinline__ double to_d<float>(float x) { return static_cast<double>(x); }
+template <> __device__ __forceinline__ double to_d<double>(double x) { return x; }
+template <> __device__ __forceinline__ double to_d<__half>(__half x) { return static_cast<double>(__half2float(x)); }
+template <> __device__ __forceinline__ double to_d<__nv_bfloat16>(__nv_bfloat16 x) {
+  return static_cast<double>(__bfloat162float(x));
+}
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<double>(double x) { return static_cast<float>(x); }
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// LOWT: 0 none, 1 fp16, 2 bf16, 3 tf32 (fp32 storage, rounded to 10 mantissa bits)
+template <typename TIN, int NORM, int LOWT>
+__global__ void __launch_bounds__(128) prep_rows_kernel(const TIN* __restrict__ X, int64_t rows, int dim,
+                                                        void* __restrict__ low, int ldl,
+                                                        void* __restrict__ norms) {
+  constexpr bool kDouble = (NORM == NM_F64_FMA);
+  using TS = typename std::conditional<kDouble, double, float>::type;
+  __shared__ TS tile[4][32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 4 + warp) * 32;
+  if (row0 >= rows) return;
+  TS (*t)[33] = tile[warp];
+  TS acc = 0;
+  const int64_t my_row = row0 + lane;
+  for (int c0 = 0; c0 < dim; c0 += 32) {
+    const int c = c0 + lane;
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) {
+      const int64_t gr = row0 + r;
+      TS v = 0;
+      if (gr < rows && c < dim) {
+        if constexpr (kDouble)
+          v = to_d(X[gr * dim + c]);
+        else
+          v = to_f(X[gr * dim + c]);
+      }
+      t[r][lane] = v;
+    }
+    __syncwarp();
+    const int cend = min(32, dim - c0);
+    for (int cc = 0; cc < cend; ++cc) {
+      TS x = t[lane][cc];
+      if constexpr (NORM == NM_LOW_F16) {
+        const float h = round_f16(x);
+        acc = __fmaf_rn(h, h, acc);
+      } else if constexpr (NORM == NM_LOW_BF16) {
+        const float h = round_bf16(x);
+        acc = __fmaf_rn(h, h, acc);
+      } else if constexpr (NORM == NM_F32_FMA) {
+        acc = __fmaf_rn(x, x, acc);
+      } else if constexpr (NORM == NM_F32_SUMSQ) {
+        acc = __fadd_rn(acc, __fmul_rn(x, x));
+      } else {
+        acc = fma(x, x, acc);
+      }
+    }
+    if constexpr (LOWT != 0) {
+#pragma unroll 4
+      for (int r = 0; r < 32; ++r) {
+        const int64_t gr = row0 + r;
+        if (gr < rows) {
+          const float x = static_cast<float>(t[r][lane]);
+          if constexpr (LOWT == 1)
+            static_cast<__half*>(low)[gr * ldl + c] = __float2half_rn(c < dim ? x : 0.f);
+          else if constexpr (LOWT == 2)
+            static_cast<__nv_bfloat16*>(low)[gr * ldl + c] = __float2bfloat16_rn(c < dim ? x : 0.f);
+          else {
+            uint32_t b;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b) : "f"(c < dim ? x : 0.f));
+            static_cast<uint32_t*>(low)[gr * ldl + c] = b;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+  // zero padding up to the padded row length
+  if constexpr (LOWT != 0) {
+    const int cstart = ((dim + 31) / 32) * 32;
+    for (int r = 0; r < 32; ++r) {
+      const int64_t gr = row0 + r;
+      if (gr >= rows) break;
+      for (int c = cstart + lane; c < ldl; c += 32) {
+        if constexpr (LOWT == 1)
+          static_cast<__half*>(low)[gr * ldl + c] = __float2half_rn(0.f);
+        else if constexpr (LOWT == 2)
+          static_cast<__nv_bfloat16*>(low)[gr * ldl + c] = __float2bfloat16_rn(0.f);
+        else
+          static_cast<uint32_t*>(low)[gr * ldl + c] = 0u;
+      }
+    }
+  }
+  if (my_row < rows) {
+    if constexpr (NORM == NM_LOW_F16)
+      static_cast<float*>(norms)[my_row] = round_f16(acc);
+    else if constexpr (NORM == NM_LOW_BF16)
+      static_cast<float*>(norms)[my_row] = round_bf16(acc);
+    else if constexpr (kDouble)
+      static_cast<double*>(norms)[my_row] = acc;
+    else
+      static_cast<float*>(norms)[my_row] = acc;
+  }
+}
+
+template <typename TIN, int NORM, int LOWT>
+static cudaError_t go(const void* X, int64_t rows, int dim, void* low, int ldl, void* norms, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const int64_t blocks = (rows + 127) / 128;
+  prep_rows_kernel<TIN, NORM, LOWT><<<static_cast<unsigned>(blocks), 128, 0, st>>>(
+      static_cast<const TIN*>(X), rows, dim, low, ldl, norms);
+  return cudaGetLastError();
+}
+
+// points=true prepares P (n rows), else C (m rows).
+cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
+  const OpSpec* s = j.spec;
+  const void* X = points ? j.P : j.C;
+  const int64_t rows = points ? j.n : j.m;
+  void* low = make_low ? (points ? j.Plow : j.Clow) : nullptr;
+  void* nrm = points ? j.pp : j.cc;
+  const int ldl = j.ldlow;
+  int lowt = 0;
+  if (make_low) lowt = (s->gemm == G_TC_F16) ? 1 : (s->gemm == G_TC_BF16 ? 2 : 3);
+  cudaStream_t st = j.stream;
+
+#define PREP(TIN_, NORM_, LOWT_)                                   \
+  if (s->norm == NORM_ && lowt == LOWT_)                           \
+    return go<TIN_, NORM_, LOWT_>(X, rows, j.dim, low, ldl, nrm, st);
+
+  switch (s->in) {
+    case IN_F32:
+      PREP(float, NM_LOW_F16, 1)
+      PREP(float, NM_LOW_BF16, 2)
+      PREP(float, NM_F32_FMA, 3)
+      PREP(float, NM_F32_FMA, 0)
+      PREP(float, NM_F32_SUMSQ, 1)
+      PREP(float, NM_F32_SUMSQ, 2)
+      PREP(float, NM_F32_SUMSQ, 0)
+      PREP(float, NM_F64_FMA, 0)
+      break;
+    case IN_F16:
+      PREP(__half, NM_LOW_F16, 1)
+      PREP(__half, NM_F32_FMA, 0)
+      break;
+    case IN_BF16:
+      PREP(__nv_bfloat16, NM_LOW_BF16, 2)
+      PREP(__nv_bfloat16, NM_F32_FMA, 0)
+      break;
+    case IN_F64:
+      PREP(double, NM_F64_FMA, 0)
+      break;
+  }
+#undef PREP
+  return cudaErrorNotSupported;
+}
+
+}  // namespace euc

@@ -1,0 +1,365 @@
+// CUDA-core distance kernels.
+//
+// simt_dist_kernel: S = P.C^T by sequential fused multiply-adds (fp32 or fp64),
+//   64x64 output tile per CTA, 4x4 outputs per thread, 16-wide K slabs staged in
+//   shared memory; the epilogue is the same form / cancellation test / store-or-argmin
+//   logic as the tensor-core kernel.  It serves the operators whose S comes from an
+//   fp32 or fp64 GEMM in the reference (torch::mm, euclidean_kernels.cu:107,142;
+//   euclidean_kernels_mix.cu:949,1550; euclidean_kernels_uniform.cu:239;
+//   euclidean_kernels_advanced.cu:253,311,370,426) and the fp32 tiled operators
+//   (euclidean_kernels_tiled.cu:500-528).
+// direct_kernel: D = sum_k (p_k - c_k)^2 for every pair, same tiling
+//   (pairwise_distance_direct_*, euclidean_kernels_uniform.cu:262-505).
+#include "common.cuh"
+#include "engine.h"
+#include "direct.cuh"
+
+namespace euc {
+
+struct SimtArgs {
+  const void* P;
+  const void* C;
+  int64_t n, m;
+  int dim;
+  const void* pp;
+  const void* cc;
+  float kf;
+  double kd;
+  void* D;
+  unsigned long long* row_key;
+  double* row_val64;
+  long long* row_idx64;
+  unsigned long long* count;
+  unsigned long long* list;
+  unsigned long long cap;
+  int32_t* tile_counts;
+  int tile_T;
+  int64_t tiles_j;
+};
+
+constexpr int SB = 64;   // tile edge
+constexpr int SK = 16;   // K slab
+enum SimtMode { SM_D = 0, SM_ARGMIN_KEY = 1, SM_ARGMIN_F64 = 2 };
+
+template <typename TACC, typename TIN> __device__ __forceinline__ TACC cvt_in(TIN x);
+template <> __device__ __forceinline__ float cvt_in<float, float>(float x) { return x; }
+template <> __device__ __forceinline__ float cvt_in<float, double>(double x) { return __double2float_rn(x); }
+template <> __device__ __forceinline__ double cvt_in<double, float>(float x) { return static_cast<double>(x); }
+template <> __device__ __forceinline__ double cvt_in<double, double>(double x) { return x; }
+template <> __device__ __forceinline__ double cvt_in<double, __half>(__half x) {
+  return static_cast<double>(__half2float(x));
+}
+template <> __device__ __forceinline__ double cvt_in<double, __nv_bfloat16>(__nv_bfloat16 x) {
+  return static_cast<double>(__bfloat162float(x));
+}
+template <> __device__ __forceinline__ float cvt_in<float, __half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float cvt_in<float, __nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+__device__ __forceinline__ float fma_t(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_t(double a, double b, double c) { return __fma_rn(a, b, c); }
+
+template <typename T> __device__ __forceinline__ void store_out(T* p, double v);
+template <> __device__ __forceinline__ void store_out<float>(float* p, double v) { *p = static_cast<float>(v); }
+template <> __device__ __forceinline__ void store_out<double>(double* p, double v) { *p = v; }
+template <> __device__ __forceinline__ void store_out<__half>(__half* p, double v) {
+  *p = __float2half_rn(static_cast<float>(v));
+}
+template <> __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat16* p, double v) {
+  *p = __float2bfloat16_rn(static_cast<float>(v));
+}
+
+// Stage a 64 x 16 slab of rows [r0, r0+64) x cols [k0, k0+16) transposed into s[k][r].
+template <typename TACC, typename TIN>
+__device__ __forceinline__ void load_slab(TACC (*s)[SB + 4], const TIN* __restrict__ X, int64_t rows, int dim,
+                                          int64_t r0, int k0) {
+  for (int t = threadIdx.x; t < SB * SK; t += 256) {
+    const int r = t >> 4, kk = t & 15;
+    const int64_t gr = r0 + r;
+    const int gk = k0 + kk;
+    TACC v = 0;
+    if (gr < rows && gk < dim) v = cvt_in<TACC>(X[gr * dim + gk]);
+    s[kk][r] = v;
+  }
+}
+
+template <typename TIN, typename TACC, int FORM, int FLAG, int REC, typename TOUT, int MODE>
+__global__ void __launch_bounds__(256) simt_dist_kernel(const SimtArgs a) {
+  __shared__ TACC As[SK][SB + 4];
+  __shared__ TACC Bs[SK][SB + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * SB;
+  const TIN* P = static_cast<const TIN*>(a.P);
+  const TIN* C = static_cast<const TIN*>(a.C);
+  using TN = typename std::conditional<FORM == FM_F64, double, float>::type;  // norm storage
+  const TN* ppv = static_cast<const TN*>(a.pp);
+  const TN* ccv = static_cast<const TN*>(a.cc);
+
+  TN pp[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t i = row0 + ty * 4 + r;
+    pp[r] = (i < a.n) ? ppv[i] : TN(0);
+  }
+  unsigned long long bkey[4] = {~0ull, ~0ull, ~0ull, ~0ull};
+  double bval[4];
+  long long bidx[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) { bval[r] = __longlong_as_double(0x7ff0000000000000ll); bidx[r] = -1; }
+
+  const int64_t n_ct = (a.m + SB - 1) / SB;
+  const int64_t ct_begin = (MODE == SM_D) ? blockIdx.y : 0;
+  const int64_t ct_end = (MODE == SM_D) ? blockIdx.y + 1 : n_ct;
+  for (int64_t ct = ct_begin; ct < ct_end; ++ct) {
+    const int64_t col0 = ct * SB;
+    TACC acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[r][c] = 0;
+    for (int k0 = 0; k0 < a.dim; k0 += SK) {
+      load_slab<TACC, TIN>(As, P, a.n, a.dim, row0, k0);
+      load_slab<TACC, TIN>(Bs, C, a.m, a.dim, col0, k0);
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < SK; ++kk) {
+        TACC av[4], bv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) av[r] = As[kk][ty * 4 + r];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) bv[c] = Bs[kk][tx * 4 + c];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[r][c] = fma_t(av[r], bv[c], acc[r][c]);
+      }
+      __syncthreads();
+    }
+    // epilogue
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t i = row0 + ty * 4 + r;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int64_t j = col0 + tx * 4 + c;
+        if (i >= a.n || j >= a.m) continue;
+        const TN cc = ccv[j];
+        double dval;  // distance as stored
+        bool flag = false;
+        if constexpr (FORM == FM_F32) {
+          const float s = static_cast<float>(acc[r][c]);
+          float d = __fadd_rn(__fmaf_rn(-2.f, s, static_cast<float>(pp[r])), static_cast<float>(cc));
+          d = fmaxf(d, 0.f);
+          if constexpr (FLAG == FL_F32)
+            flag = d <= __fmul_rn(a.kf, __fadd_rn(static_cast<float>(pp[r]), static_cast<float>(cc)));
+          dval = d;
+        } else if constexpr (FORM == FM_F64) {
+          const double s = static_cast<double>(acc[r][c]);
+          double d = __dadd_rn(fma(-2.0, s, static_cast<double>(pp[r])), static_cast<double>(cc));
+          d = fmax(d, 0.0);
+          if constexpr (FLAG == FL_F64)
+            flag = d <= a.kd * (static_cast<double>(pp[r]) + static_cast<double>(cc));
+          dval = d;
+        } else {  // FM_F64_TO_F32
+          const double s = static_cast<double>(acc[r][c]);
+          const double d64 = __dadd_rn(fma(-2.0, s, static_cast<double>(pp[r])), static_cast<double>(cc));
+          const float d = static_cast<float>(fmax(d64, 0.0));
+          if constexpr (FLAG == FL_F32)
+            flag = d <= __fmul_rn(a.kf, __fadd_rn(static_cast<float>(pp[r]), static_cast<float>(cc)));
+          dval = d;
+        }
+        if constexpr (MODE == SM_D) {
+          store_out<TOUT>(static_cast<TOUT*>(a.D) + i * a.m + j, dval);
+        } else if constexpr (MODE == SM_ARGMIN_KEY) {
+          if (!flag) {
+            const unsigned long long key = make_key(static_cast<float>(dval), static_cast<uint32_t>(j));
+            bkey[r] = key < bkey[r] ? key : bkey[r];
+          }
+        } else {
+          if (dval < bval[r] || (dval == bval[r] && j < bidx[r])) { bval[r] = dval; bidx[r] = j; }
+        }
+        if constexpr (FLAG != FL_NONE) {
+          if (flag) {
+            const unsigned long long pos = atomicAdd(a.count, 1ull);
+            if (pos < a.cap) {
+              a.list[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(j);
+            } else if constexpr (MODE == SM_ARGMIN_KEY) {
+              const float dd = static_cast<float>(direct_dist<TIN, REC>(P + i * a.dim, C + j * a.dim, a.dim));
+              const unsigned long long key = make_key(dd, static_cast<uint32_t>(j));
+              bkey[r] = key < bkey[r] ? key : bkey[r];
+            }
+            if (a.tile_counts != nullptr) atomicAdd(&a.tile_counts[(i / a.tile_T) * a.tiles_j + j / a.tile_T], 1);
+          }
+        }
+      }
+    }
+  }
+  if constexpr (MODE != SM_D) {
+    // reduce over the 16 threads (tx) that share rows ty*4 .. ty*4+3
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) {
+        if constexpr (MODE == SM_ARGMIN_KEY) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, bkey[r], off);
+          bkey[r] = o < bkey[r] ? o : bkey[r];
+        } else {
+          const double ov = __shfl_xor_sync(0xffffffffu, bval[r], off);
+          const long long oi = __shfl_xor_sync(0xffffffffu, bidx[r], off);
+          if (ov < bval[r] || (ov == bval[r] && oi < bidx[r])) { bval[r] = ov; bidx[r] = oi; }
+        }
+      }
+      const int64_t i = row0 + ty * 4 + r;
+      if (tx == 0 && i < a.n) {
+        if constexpr (MODE == SM_ARGMIN_KEY)
+          a.row_key[i] = bkey[r];
+        else {
+          a.row_val64[i] = bval[r];
+          a.row_idx64[i] = bidx[r];
+        }
+      }
+    }
+  }
+}
+
+template <typename TIN, typename TACC, int FORM, int FLAG, int REC, typename TOUT, int MODE>
+static cudaError_t go_simt(const DistJob& j) {
+  SimtArgs a{};
+  a.P = j.P;
+  a.C = j.C;
+  a.n = j.n;
+  a.m = j.m;
+  a.dim = j.dim;
+  a.pp = j.pp;
+  a.cc = j.cc;
+  a.kf = j.kf;
+  a.kd = j.kd;
+  a.D = j.D;
+  a.row_key = j.row_key;
+  a.row_val64 = j.row_val64;
+  a.row_idx64 = j.row_idx64;
+  a.count = j.count;
+  a.list = j.list;
+  a.cap = j.list_cap;
+  a.tile_counts = j.tile_counts;
+  a.tile_T = j.tile_T > 0 ? j.tile_T : 1;
+  a.tiles_j = j.tiles_j;
+  const int64_t nrt = (j.n + SB - 1) / SB;
+  const int64_t nct = (j.m + SB - 1) / SB;
+  if (nrt == 0 || nct == 0) return cudaSuccess;
+  if (nct > 65535 && MODE == SM_D) return cudaErrorInvalidConfiguration;
+  dim3 grid(static_cast<unsigned>(nrt), MODE == SM_D ? static_cast<unsigned>(nct) : 1u);
+  timing_begin(j.stream, "simt_dist_kernel");
+  simt_dist_kernel<TIN, TACC, FORM, FLAG, REC, TOUT, MODE><<<grid, 256, 0, j.stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  timing_end(j.stream);
+  return e;
+}
+
+cudaError_t launch_simt(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  const bool argmin = (j.D == nullptr);
+  const bool f64key = argmin && s->form == FM_F64;
+  const int mode = !argmin ? SM_D : (f64key ? SM_ARGMIN_F64 : SM_ARGMIN_KEY);
+
+#define SIMT_CASE(IN_, TIN_, GEMM_, TACC_, FORM_, FLAG_, REC_, OUT_, TOUT_, MODE_)                   \
+  if (s->in == IN_ && s->gemm == GEMM_ && s->form == FORM_ && s->flag == FLAG_ && mode == MODE_ &&  \
+      (MODE_ == SM_D ? s->out == OUT_ : true) && (FLAG_ == FL_NONE || s->rec == REC_))               \
+    return go_simt<TIN_, TACC_, FORM_, FLAG_, REC_, TOUT_, MODE_>(j);
+
+  // base single / uniform tf32: fp32 GEMM, no flag
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_NONE, RC_NONE, OUT_F32, float, SM_D)
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_NONE, RC_NONE, OUT_F32, float, SM_ARGMIN_KEY)
+  // base double: fp64 GEMM, no flag
+  SIMT_CASE(IN_F64, double, G_SIMT_F64, double, FM_F64, FL_NONE, RC_NONE, OUT_F64, double, SM_D)
+  SIMT_CASE(IN_F64, double, G_SIMT_F64, double, FM_F64, FL_NONE, RC_NONE, OUT_F64, double, SM_ARGMIN_F64)
+  // mix fp32_fp64 / fp32_fp32, tiled fp32_*
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_F32, RC_F64, OUT_F32, float, SM_D)
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_F32, RC_F32, OUT_F32, float, SM_D)
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_F32, RC_F64, OUT_F32, float, SM_ARGMIN_KEY)
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F32, FL_F32, RC_F32, OUT_F32, float, SM_ARGMIN_KEY)
+  // advanced fp64_fp16 / fp64_bf16: fp64 GEMM on low inputs, float distances
+  SIMT_CASE(IN_F16, __half, G_SIMT_F64, double, FM_F64_TO_F32, FL_F32, RC_F64, OUT_F32, float, SM_D)
+  SIMT_CASE(IN_BF16, __nv_bfloat16, G_SIMT_F64, double, FM_F64_TO_F32, FL_F32, RC_F64, OUT_F32, float, SM_D)
+  // advanced fp64_tf32 (fp32 GEMM, fp64 form) / fp64_fp32_gemm (fp64 in, fp32 GEMM)
+  SIMT_CASE(IN_F32, float, G_SIMT_F32, float, FM_F64, FL_F64, RC_F64, OUT_F64, double, SM_D)
+  SIMT_CASE(IN_F64, double, G_SIMT_F32, float, FM_F64, FL_F64, RC_F64, OUT_F64, double, SM_D)
+#undef SIMT_CASE
+  return cudaErrorNotSupported;
+}
+
+// ------------------------------------------------------------------ direct
+
+template <typename TIN, typename TACC, typename TOUT>
+__global__ void __launch_bounds__(256) direct_kernel(const TIN* __restrict__ P, const TIN* __restrict__ C,
+                                                     int64_t n, int64_t m, int dim, TOUT* __restrict__ D) {
+  __shared__ TACC As[SK][SB + 4];
+  __shared__ TACC Bs[SK][SB + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * SB;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.y) * SB;
+  TACC acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0;
+  for (int k0 = 0; k0 < dim; k0 += SK) {
+    load_slab<TACC, TIN>(As, P, n, dim, row0, k0);
+    load_slab<TACC, TIN>(Bs, C, m, dim, col0, k0);
+    __syncthreads();
+    const int kend = min(SK, dim - k0);  // padded columns must not contribute (p-c)^2 terms
+    for (int kk = 0; kk < kend; ++kk) {
+      TACC av[4], bv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) av[r] = As[kk][ty * 4 + r];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) bv[c] = Bs[kk][tx * 4 + c];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const TACC d = av[r] - bv[c];
+          acc[r][c] = fma_t(d, d, acc[r][c]);
+        }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t i = row0 + ty * 4 + r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int64_t j = col0 + tx * 4 + c;
+      if (i < n && j < m) store_out<TOUT>(D + i * m + j, static_cast<double>(acc[r][c]));
+    }
+  }
+}
+
+template <typename TIN, typename TACC, typename TOUT>
+static cudaError_t go_direct(const void* P, const void* C, int64_t n, int64_t m, int dim, void* D,
+                             cudaStream_t st) {
+  const int64_t nrt = (n + SB - 1) / SB, nct = (m + SB - 1) / SB;
+  if (nrt == 0 || nct == 0) return cudaSuccess;
+  if (nct > 65535) return cudaErrorInvalidConfiguration;
+  dim3 grid(static_cast<unsigned>(nrt), static_cast<unsigned>(nct));
+  timing_begin(st, "direct_kernel");
+  direct_kernel<TIN, TACC, TOUT><<<grid, 256, 0, st>>>(static_cast<const TIN*>(P), static_cast<const TIN*>(C), n,
+                                                       m, dim, static_cast<TOUT*>(D));
+  cudaError_t e = cudaGetLastError();
+  timing_end(st);
+  return e;
+}
+
+cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim, void* D,
+                          cudaStream_t st) {
+  switch (s->in) {
+    case IN_F16: return go_direct<__half, float, __half>(P, C, n, m, dim, D, st);
+    case IN_BF16: return go_direct<__nv_bfloat16, float, __nv_bfloat16>(P, C, n, m, dim, D, st);
+    case IN_F32: return go_direct<float, float, float>(P, C, n, m, dim, D, st);
+    case IN_F64: return go_direct<double, double, double>(P, C, n, m, dim, D, st);
+  }
+  return cudaErrorNotSupported;
+}
+
+}  // namespace euc

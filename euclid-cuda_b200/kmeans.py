@@ -1,0 +1,82 @@
+"""Lloyd iterations on the B200 engine, data-parallel over the GPUs of one node.
+
+The reference ships the pieces (distance operators, update_centers_*) but not the
+loop; this is the caller those pieces are meant for (distances -> argmin labels ->
+center update), composed without materialising D:
+
+    labels      = euc_argmin(op, X_local, C)            fused GEMM + test + argmin
+    stats       = euc_center_stats(X_local, labels)     k x (dim+1) fp64 sums, counts
+    all_reduce(stats)                                    one collective per iteration
+    C           = euc_center_finalize(stats)            mean; empty -> 0 (reference) or keep
+
+Points are sharded by rows, centers replicated.  With one process per GPU
+(torchrun), every rank runs the same sequence on its shard and the single
+all-reduce (NCCL over NVLink) makes the centers identical on all ranks.  Cluster
+counts are exact integers in fp64, so they are bit-identical for any GPU count.
+"""
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+import _ops
+from _lib import check, lib, ptr, stream_of, workspace
+
+EMPTY_POLICY = {"zero": 0, "keep": 1}
+
+
+class LloydKMeans:
+    """One Lloyd iteration per `step`; `op` is the distance operator (e.g. 'bf16_fp32',
+    'fp16_fp32', 'double') whose cancellation test and recompute define the labels."""
+
+    def __init__(self, n_clusters, op="bf16_fp32", kappa=5.0, empty="zero", group=None):
+        self.k = int(n_clusters)
+        self.op = op
+        self.kappa = float(kappa)
+        self.empty = EMPTY_POLICY[empty]
+        self.group = group
+        self._ws = None
+
+    def _world(self):
+        return dist.get_world_size(self.group) if dist.is_available() and dist.is_initialized() else 1
+
+    def center_stats(self, X, labels):
+        n, d = X.shape
+        nbytes = lib().euc_center_stats_workspace_bytes(n, d, self.k)
+        if self._ws is None or self._ws.numel() < nbytes or self._ws.device != X.device:
+            self._ws = workspace(nbytes, X.device)
+        stats = torch.empty((self.k, d + 1), dtype=torch.float64, device=X.device)
+        check(lib().euc_center_stats(ptr(X), int(X.dtype == torch.float64), ptr(labels),
+                                     int(labels.dtype == torch.int64), n, d, self.k, ptr(stats),
+                                     ptr(self._ws), self._ws.numel(), stream_of(X)))
+        return stats
+
+    def finalize(self, stats, prev):
+        d = stats.size(1) - 1
+        out = torch.empty((self.k, d), dtype=prev.dtype, device=stats.device)
+        check(lib().euc_center_finalize(ptr(stats), d, self.k, ptr(out), int(prev.dtype == torch.float64),
+                                        ptr(prev), self.empty, stream_of(stats)))
+        return out
+
+    def step(self, X, C):
+        """One iteration on the local shard X; returns (new centers, labels int32,
+        flagged-pair count of this shard as a 0-d device tensor)."""
+        labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, labels_dtype=torch.int32, min_dist=False)
+        stats = self.center_stats(X, labels)
+        if self._world() > 1:
+            dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=self.group)
+        return self.finalize(stats, C), labels, cnt
+
+    def fit(self, X, C0, n_iter):
+        C = C0.contiguous()
+        labels = None
+        for _ in range(int(n_iter)):
+            C, labels, _ = self.step(X, C)
+        return C, labels
+
+
+def shard_rows(n, rank, world):
+    """Contiguous row range [lo, hi) of rank `rank` out of `world`."""
+    base, rem = divmod(n, world)
+    lo = rank * base + min(rank, rem)
+    return lo, lo + base + (1 if rank < rem else 0)

@@ -1,0 +1,241 @@
+/*
+ * euclid_b200.h -- C ABI of the B200 (sm_100a) k-means distance engine.
+ *
+ * Every function takes plain device pointers, element counts and a CUDA stream
+ * (passed as void*, NULL = legacy default stream).  No torch types cross this
+ * boundary.  Functions are asynchronous on `stream` unless stated otherwise and
+ * return an euc_status; euc_last_error() gives a readable message for the last
+ * failing call on the calling host thread.
+ *
+ * Scratch memory: each distance / center entry point takes a caller-owned device
+ * workspace (`ws`, `ws_bytes`).  Query the size with euc_workspace_bytes(); a
+ * smaller workspace is rejected with EUC_ERR_WORKSPACE.  The library itself
+ * never allocates device memory on these paths.
+ *
+ * Shapes follow the reference: P is n x dim (points, row-major, contiguous),
+ * C is m x dim (centers), D is n x m (row-major).  Index arithmetic is 64-bit
+ * throughout; unlike the reference there is no N*M <= 2^32 limit.
+ *
+ * Reference citations are file:line in inEXASCALE/euclid-cuda.
+ */
+#ifndef EUCLID_B200_H
+#define EUCLID_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EUC_API __attribute__((visibility("default")))
+#else
+#define EUC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+typedef enum {
+  EUC_OK = 0,
+  EUC_ERR_SHAPE = 1,       /* bad or mismatched sizes (reference: "Dimension mismatch", ...) */
+  EUC_ERR_DTYPE = 2,       /* unsupported element type for this entry point                  */
+  EUC_ERR_UNSUPPORTED = 3, /* argument value the operator does not support (e.g. tile_size)  */
+  EUC_ERR_LAUNCH = 4,      /* CUDA launch / runtime error                                     */
+  EUC_ERR_TIMEOUT = 5,     /* a bounded device-side wait expired; the kernel returned early   */
+  EUC_ERR_WORKSPACE = 6,   /* workspace missing or smaller than euc_workspace_bytes()         */
+  EUC_ERR_ARG = 7,         /* null pointer or invalid argument                                */
+  EUC_ERR_DEVICE = 8       /* current device is not sm_100                                    */
+} euc_status;
+
+EUC_API const char* euc_version(void);
+EUC_API const char* euc_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+EUC_API const char* euc_last_error(void);
+/* Synchronising check of the device-side error word: returns EUC_ERR_TIMEOUT if a
+ * bounded wait inside a kernel expired since the previous check (and clears it),
+ * EUC_OK otherwise. */
+EUC_API int euc_device_check(void);
+
+/* Operator identifiers, used by euc_workspace_bytes() and the generic entries. */
+typedef enum {
+  /* euclidean_cuda.cpp:26-32 */
+  EUC_OP_SINGLE = 0, EUC_OP_DOUBLE = 1,
+  /* euclidean_cuda_mix.cpp:13-83 */
+  EUC_OP_MIX_FP16_FP64 = 10, EUC_OP_MIX_BF16_FP64 = 11, EUC_OP_MIX_TF32_FP64 = 12,
+  EUC_OP_MIX_FP32_FP64 = 13, EUC_OP_MIX_FP16_FP16 = 14, EUC_OP_MIX_FP16_FP32 = 15,
+  EUC_OP_MIX_BF16_BF16 = 16, EUC_OP_MIX_BF16_FP32 = 17, EUC_OP_MIX_FP32_FP32 = 18,
+  /* euclidean_cuda_tiled.cpp:12-45 */
+  EUC_OP_TILED_FP16_FP64 = 20, EUC_OP_TILED_FP16_FP32 = 21, EUC_OP_TILED_BF16_FP64 = 22,
+  EUC_OP_TILED_BF16_FP32 = 23, EUC_OP_TILED_FP32_FP64 = 24, EUC_OP_TILED_FP32_FP32 = 25,
+  /* euclidean_cuda_tiled.cpp:51-62 */
+  EUC_OP_TC_FP16_FP64 = 30, EUC_OP_TC_FP16_FP32 = 31, EUC_OP_TC_BF16_FP64 = 32,
+  EUC_OP_TC_BF16_FP32 = 33,
+  /* euclidean_cuda_uniform.cpp:9-40 */
+  EUC_OP_UNI_FP16 = 40, EUC_OP_UNI_BF16 = 41, EUC_OP_UNI_TF32 = 42,
+  EUC_OP_UNI_FP16_DIRECT = 43, EUC_OP_UNI_BF16_DIRECT = 44, EUC_OP_UNI_TF32_DIRECT = 45,
+  EUC_OP_UNI_FP32_DIRECT = 46, EUC_OP_UNI_FP64_DIRECT = 47,
+  /* euclidean_cuda_advanced.cpp:10-27 */
+  EUC_OP_ADV_FP64_FP16 = 50, EUC_OP_ADV_FP64_BF16 = 51, EUC_OP_ADV_FP64_TF32 = 52,
+  EUC_OP_ADV_FP64_FP32_GEMM = 53,
+  /* center_kernels.cu:255-262 */
+  EUC_OP_CENTERS_FP32 = 60, EUC_OP_CENTERS_FP64 = 61
+} euc_op;
+
+/* Device workspace (bytes) needed by `op` at this size.  For the fused argmin
+ * entry (euc_argmin) pass the distance op it is built on. */
+EUC_API size_t euc_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim);
+EUC_API size_t euc_argmin_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim);
+
+/* Optional per-call timing of the dominant distance kernel (CUDA events on the
+ * launching stream).  euc_last_kernel_ms() synchronises on the stop event. */
+EUC_API void euc_set_kernel_timing(int enable);
+EUC_API float euc_last_kernel_ms(void);
+/* Name of the kernel that euc_last_kernel_ms() timed. */
+EUC_API const char* euc_last_kernel_name(void);
+
+/* ------------------------------------------------------- base op (fp32/fp64)
+ * pairwise_euclidean_single / _double, euclidean_kernels.cu:83,120
+ * (bound at euclidean_cuda.cpp:26,30).  D = max(|p|^2 - 2 p.c + |c|^2, 0). */
+EUC_API int euc_pairwise_single(const float* P, const float* C, int64_t n, int64_t m, int64_t dim,
+                        float* D, void* ws, size_t ws_bytes, void* stream);
+EUC_API int euc_pairwise_double(const double* P, const double* C, int64_t n, int64_t m, int64_t dim,
+                        double* D, void* ws, size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------ mixed precision + fallback
+ * One entry per pairwise_euclidean_<low>_<fallback> of euclidean_kernels_mix.cu.
+ * P, C are fp32; D is fp32 n x m.  `d_count` (nullable, device uint64) receives
+ * the number of pairs flagged by the cancellation test; it replaces the
+ * `_with_stats` twins (euclidean_kernels_mix.cu:713-912, 1099-1626), which read
+ * the same counter back to the host. */
+#define EUC_MIX_DECL(name)                                                                 \
+  EUC_API int name(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa, \
+           float* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream)
+EUC_MIX_DECL(euc_mix_fp16_fp64); /* euclidean_kernels_mix.cu:515  */
+EUC_MIX_DECL(euc_mix_bf16_fp64); /* euclidean_kernels_mix.cu:584  */
+EUC_MIX_DECL(euc_mix_tf32_fp64); /* euclidean_kernels_mix.cu:648  */
+EUC_MIX_DECL(euc_mix_fp32_fp64); /* euclidean_kernels_mix.cu:918  */
+EUC_MIX_DECL(euc_mix_fp16_fp16); /* euclidean_kernels_mix.cu:1041 */
+EUC_MIX_DECL(euc_mix_fp16_fp32); /* euclidean_kernels_mix.cu:1163 */
+EUC_MIX_DECL(euc_mix_bf16_bf16); /* euclidean_kernels_mix.cu:1284 */
+EUC_MIX_DECL(euc_mix_bf16_fp32); /* euclidean_kernels_mix.cu:1405 */
+EUC_MIX_DECL(euc_mix_fp32_fp32); /* euclidean_kernels_mix.cu:1525 */
+#undef EUC_MIX_DECL
+
+/* ---------------------------------------------------------- tiled operators
+ * pairwise_euclidean_tiled_<low>_<high>[_with_stats], euclidean_kernels_tiled.cu:440-528.
+ * tile_size must be 16 or 32 (<= 0 selects 32 for dim <= 128, else 16) and dim <= 512,
+ * as in euclidean_kernels_tiled.cu:331-336.  `d_tile_counts` (nullable, device int32,
+ * ceil(n/T)*ceil(m/T) entries, zeroed by the call) receives the per-tile flag counts
+ * in the reference's tile order (tile_i * ceil(m/T) + tile_j). */
+#define EUC_TILED_DECL(name)                                                                 \
+  EUC_API int name(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa,   \
+           int tile_size, float* D, int32_t* d_tile_counts, uint64_t* d_count, void* ws,     \
+           size_t ws_bytes, void* stream)
+EUC_TILED_DECL(euc_tiled_fp16_fp64); /* euclidean_kernels_tiled.cu:440 */
+EUC_TILED_DECL(euc_tiled_fp16_fp32); /* euclidean_kernels_tiled.cu:447 */
+EUC_TILED_DECL(euc_tiled_bf16_fp64); /* euclidean_kernels_tiled.cu:470 */
+EUC_TILED_DECL(euc_tiled_bf16_fp32); /* euclidean_kernels_tiled.cu:477 */
+EUC_TILED_DECL(euc_tiled_fp32_fp64); /* euclidean_kernels_tiled.cu:500 */
+EUC_TILED_DECL(euc_tiled_fp32_fp32); /* euclidean_kernels_tiled.cu:507 */
+#undef EUC_TILED_DECL
+
+/* pairwise_euclidean_tensorcore_<low>_<high>, euclidean_kernels_tiled_tc.cu:274-300.
+ * tile_size must be 32 (<= 0 selects 32) and dim % 16 == 0, as in
+ * euclidean_kernels_tiled_tc.cu:246-248. */
+#define EUC_TC_DECL(name)                                                                   \
+  EUC_API int name(const float* P, const float* C, int64_t n, int64_t m, int64_t dim, float kappa,  \
+           int tile_size, float* D, uint64_t* d_count, void* ws, size_t ws_bytes, void* stream)
+EUC_TC_DECL(euc_tensorcore_fp16_fp64); /* euclidean_kernels_tiled_tc.cu:274 */
+EUC_TC_DECL(euc_tensorcore_fp16_fp32); /* euclidean_kernels_tiled_tc.cu:281 */
+EUC_TC_DECL(euc_tensorcore_bf16_fp64); /* euclidean_kernels_tiled_tc.cu:288 */
+EUC_TC_DECL(euc_tensorcore_bf16_fp32); /* euclidean_kernels_tiled_tc.cu:295 */
+#undef EUC_TC_DECL
+
+/* -------------------------------------------------------- uniform precision
+ * pairwise_euclidean_uniform_*, euclidean_kernels_uniform.cu:138-532.  fp16/bf16
+ * tensors are passed as uint16_t bit patterns; D has the input's type. */
+EUC_API int euc_uniform_fp16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim,
+                     uint16_t* D, void* ws, size_t ws_bytes, void* stream);          /* :138 */
+EUC_API int euc_uniform_bf16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m, int64_t dim,
+                     uint16_t* D, void* ws, size_t ws_bytes, void* stream);          /* :177 */
+EUC_API int euc_uniform_tf32(const float* P, const float* C, int64_t n, int64_t m, int64_t dim,
+                     float* D, void* ws, size_t ws_bytes, void* stream);             /* :215 */
+EUC_API int euc_uniform_fp16_direct(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m,
+                            int64_t dim, uint16_t* D, void* stream);                  /* :288 */
+EUC_API int euc_uniform_bf16_direct(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m,
+                            int64_t dim, uint16_t* D, void* stream);                  /* :345 */
+EUC_API int euc_uniform_tf32_direct(const float* P, const float* C, int64_t n, int64_t m,
+                            int64_t dim, float* D, void* stream);                     /* :398 */
+EUC_API int euc_uniform_fp32_direct(const float* P, const float* C, int64_t n, int64_t m,
+                            int64_t dim, float* D, void* stream);                     /* :453 */
+EUC_API int euc_uniform_fp64_direct(const double* P, const double* C, int64_t n, int64_t m,
+                            int64_t dim, double* D, void* stream);                    /* :507 */
+
+/* ------------------------------------------------------- advanced operators
+ * euclidean_kernels_advanced.cu:225-453 (bound at euclidean_cuda_advanced.cpp:10-27). */
+EUC_API int euc_advanced_fp64_fp16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m,
+                           int64_t dim, float kappa, float* D, uint64_t* d_count, void* ws,
+                           size_t ws_bytes, void* stream);                           /* :225 */
+EUC_API int euc_advanced_fp64_bf16(const uint16_t* P, const uint16_t* C, int64_t n, int64_t m,
+                           int64_t dim, float kappa, float* D, uint64_t* d_count, void* ws,
+                           size_t ws_bytes, void* stream);                           /* :283 */
+EUC_API int euc_advanced_fp64_tf32(const float* P, const float* C, int64_t n, int64_t m,
+                           int64_t dim, float kappa, double* D, uint64_t* d_count, void* ws,
+                           size_t ws_bytes, void* stream);                           /* :341 */
+EUC_API int euc_advanced_fp64_fp32_gemm(const double* P, const double* C, int64_t n, int64_t m,
+                                int64_t dim, float kappa, double* D, uint64_t* d_count,
+                                void* ws, size_t ws_bytes, void* stream);            /* :398 */
+
+/* get_fallback_count_low / get_last_fallback_count (euclidean_kernels_mix.cu:1028,
+ * euclidean_kernels_advanced.cu:455): synchronous read of a device int32 counter. */
+EUC_API int euc_read_count_i32(const int32_t* d_counter, int32_t* host_out);
+/* Synchronous read of a device uint64 counter written by d_count above. */
+EUC_API int euc_read_count_u64(const uint64_t* d_counter, uint64_t* host_out);
+
+/* ---------------------------------------------------------- center update
+ * update_centers_fp32 / _fp64, center_kernels.cu:101-139 (bound at :255-262):
+ * centers[c] = mean of the rows of X whose label is c; labels outside [0, k) are
+ * ignored; an empty cluster's center is 0.  Sums are accumulated in fp64.
+ * `d_counts` (nullable, device int64[k]) receives the cluster sizes; the
+ * `_with_reinit` twins (center_kernels.cu:195-246) are composed from these counts
+ * and the caller's RNG by the binding layer. */
+EUC_API int euc_update_centers_fp32(const float* X, const int64_t* labels, int64_t n, int64_t dim,
+                            int64_t k, float* centers, int64_t* d_counts, void* ws,
+                            size_t ws_bytes, void* stream);
+EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int64_t n, int64_t dim,
+                            int64_t k, double* centers, int64_t* d_counts, void* ws,
+                            size_t ws_bytes, void* stream);
+
+/* ============================================================ new entries
+ * No counterpart in the reference: the k-means caller composes these instead of
+ * materialising D (SURVEY hot path: distances -> argmin -> center update). */
+
+/* Fused distance + row argmin for distance operator `op` (an EUC_OP_MIX_*,
+ * EUC_OP_TILED_*, EUC_OP_TC_*, EUC_OP_SINGLE or EUC_OP_DOUBLE id).  The row's
+ * label is the first index of the minimum of the row of D that `op` would have
+ * produced (flagged pairs take their recomputed value, as in the reference), i.e.
+ * torch.argmin(D, 1).  P/C element type follows `op` (fp64 for EUC_OP_DOUBLE,
+ * fp32 otherwise).  Outputs are nullable: labels (int64[n]), labels32 (int32[n]),
+ * min_dist (fp32[n]; for EUC_OP_DOUBLE fp64[n]). */
+EUC_API int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
+               float kappa, int64_t* labels, int32_t* labels32, void* min_dist,
+               uint64_t* d_count, void* ws, size_t ws_bytes, void* stream);
+
+/* Partial center statistics for data-parallel Lloyd iterations: for the n local
+ * rows, stats[c*(dim+1) + j] = sum of X[i, j] over rows with label c (j < dim) and
+ * stats[c*(dim+1) + dim] = number of such rows, all fp64 (exact integer counts).
+ * `x_is_f64` selects fp64 X (else fp32); labels are int32 (labels_are_i64 = 0)
+ * or int64.  One all-reduce(sum) of `stats` combines ranks. */
+EUC_API size_t euc_center_stats_workspace_bytes(int64_t n, int64_t dim, int64_t k);
+EUC_API int euc_center_stats(const void* X, int x_is_f64, const void* labels, int labels_are_i64,
+                     int64_t n, int64_t dim, int64_t k, double* stats, void* ws,
+                     size_t ws_bytes, void* stream);
+/* centers[c, j] = stats[c, j] / stats[c, dim]; an empty cluster becomes 0
+ * (empty_policy 0, the reference's behaviour) or keeps `prev` (empty_policy 1). */
+EUC_API int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* centers,
+                        int centers_are_f64, const void* prev, int empty_policy, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EUCLID_B200_H */
