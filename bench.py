@@ -255,7 +255,7 @@ def main():
 
     if a.workload == "c2":
         def step():
-            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, None, ptr(labels), None, ptr(cnt),
+            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, 0, None, ptr(labels), None, ptr(cnt),
                                ptr(ws), ws.numel(), sp))
         launches_per_step = 5  # prep P, prep C, dist_tc_kernel, recompute, labels
         work_units = 2.0 * n_local * k * d * world  # flop per step, all ranks
@@ -292,7 +292,7 @@ def main():
         if a.workload == "c2":
             step()
         else:
-            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, None, ptr(labels), None, ptr(cnt),
+            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, 0, None, ptr(labels), None, ptr(cnt),
                                ptr(ws), ws.numel(), sp))
         kms.append(L.euc_last_kernel_ms())
     L.euc_set_kernel_timing(0)

@@ -51,7 +51,7 @@ _SIGS = {
     "euc_read_count_u64": ([_V, _V], _I),
     "euc_update_centers_fp32": ([_V, _V, _I64, _I64, _I64, _V, _V, _V, _SZ, _V], _I),
     "euc_update_centers_fp64": ([_V, _V, _I64, _I64, _I64, _V, _V, _V, _SZ, _V], _I),
-    "euc_argmin": ([_I, _V, _V, _I64, _I64, _I64, _F, _V, _V, _V, _V, _V, _SZ, _V], _I),
+    "euc_argmin": ([_I, _V, _V, _I64, _I64, _I64, _F, _I, _V, _V, _V, _V, _V, _SZ, _V], _I),
     "euc_center_stats_workspace_bytes": ([_I64, _I64, _I64], _SZ),
     "euc_center_stats": ([_V, _I, _V, _I, _I64, _I64, _I64, _V, _V, _SZ, _V], _I),
     "euc_center_finalize": ([_V, _I64, _I64, _V, _I, _V, _I, _V], _I),

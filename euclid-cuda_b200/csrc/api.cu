@@ -119,7 +119,7 @@ void timing_end(cudaStream_t st) {
 static inline size_t al(size_t b) { return (b + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hdr, pp, cc, plow, clow, list, key, val64, idx64, total;
+  size_t hdr, pp, cc, plow, clow, clow_s, cc_s, perm, list, key, val64, idx64, total;
   unsigned long long cap;
   int ldlow;
 };
@@ -140,6 +140,11 @@ static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, boo
   if (is_tc(s)) {
     L.plow = off; off += al(static_cast<size_t>(n) * L.ldlow * es);
     L.clow = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
+    if (argmin && s->flag != FL_NONE) {  // norm-sorted centers for the fast argmin screen
+      L.clow_s = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
+      L.cc_s = off; off += al(static_cast<size_t>(m) * 4);
+      L.perm = off; off += al(static_cast<size_t>(m) * 4);
+    }
   }
   L.cap = 0;
   if (s->flag != FL_NONE) {
@@ -182,6 +187,7 @@ static float k_float(const OpSpec* s, float kappa, int64_t dim) {
 }
 
 struct RunOut {
+  bool exact = false;                // argmin mode: exact epilogue instead of the fast screen
   void* D = nullptr;                 // D mode
   int64_t* labels = nullptr;         // argmin mode
   int32_t* labels32 = nullptr;
@@ -236,6 +242,10 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.Plow = is_tc(s) ? w + L.plow : nullptr;
   j.Clow = is_tc(s) ? w + L.clow : nullptr;
   j.ldlow = L.ldlow;
+  j.fast_argmin = argmin && is_tc(s) && s->flag != FL_NONE && !o.exact;
+  j.Clow_sorted = L.clow_s ? w + L.clow_s : nullptr;
+  j.cc_sorted = L.cc_s ? reinterpret_cast<float*>(w + L.cc_s) : nullptr;
+  j.perm = L.perm ? reinterpret_cast<int*>(w + L.perm) : nullptr;
   j.row_key = (argmin && L.key) ? reinterpret_cast<unsigned long long*>(w + L.key) : nullptr;
   j.row_val64 = (argmin && L.val64) ? reinterpret_cast<double*>(w + L.val64) : nullptr;
   j.row_idx64 = (argmin && L.idx64) ? reinterpret_cast<long long*>(w + L.idx64) : nullptr;
@@ -249,6 +259,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   e = launch_prep(j, true, is_tc(s));
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
+  if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
   if (e != cudaSuccess) return cuda_fail(e, "prep");
   e = is_tc(s) ? launch_tc(j) : launch_simt(j);
   if (e != cudaSuccess) return cuda_fail(e, s->name);
@@ -271,7 +282,8 @@ static int run_named(int op, const void* P, const void* C, int64_t n, int64_t m,
                      const RunOut& o, void* ws, size_t ws_bytes, void* stream) {
   const OpSpec* s = find_op(op);
   if (!s) return fail(EUC_ERR_ARG, "unknown operator id");
-  if (!o.D) return fail(EUC_ERR_ARG, std::string(s->name) + ": null output D");
+  if (!o.D && n > 0 && m > 0) return fail(EUC_ERR_ARG, std::string(s->name) + ": null output D");
+  if (!o.D) return EUC_OK;  // empty output
   return run_distance(s, P, C, n, m, dim, kappa, o, ws, ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -550,7 +562,7 @@ int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* cente
 }
 
 // ------------------------------------------------------------------ fused argmin
-int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa,
+int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa, int exact,
                int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count, void* ws, size_t ws_bytes,
                void* stream) {
   const OpSpec* s = find_op(op);
@@ -561,6 +573,7 @@ int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64
   if (!allowed) return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) + ": no fused argmin form");
   if (m > 0xffffffffll) return fail(EUC_ERR_SHAPE, "too many centers");
   RunOut o;
+  o.exact = exact != 0;
   o.labels = labels;
   o.labels32 = labels32;
   o.min_dist = min_dist;

@@ -94,11 +94,17 @@ struct DistJob {
   void* Plow;                    // padded low-precision copies (tcgen05 path)
   void* Clow;
   int ldlow;                     // padded row length (elements)
+  // fast argmin: centers sorted by norm (stable), their norms and original indices
+  bool fast_argmin;
+  void* Clow_sorted;
+  float* cc_sorted;
+  int* perm;
   cudaStream_t stream;
 };
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_prep(const DistJob& j, bool points, bool make_low);
+cudaError_t launch_sort_centers(const DistJob& j);
 cudaError_t launch_tc(const DistJob& j);
 cudaError_t launch_simt(const DistJob& j);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,

@@ -176,4 +176,55 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
   return cudaErrorNotSupported;
 }
 
+// Stable sort of the centers by norm (ties kept in index order), for the fast argmin
+// screen: rank_j = #{i : key_i < key_j or (key_i == key_j and i < j)}, key = norm (NaN
+// as +inf).  Each thread ranks one center against all others staged through shared
+// memory, then moves its low-precision row, norm and original index to its rank.
+__global__ void __launch_bounds__(256) sort_centers_kernel(const float* __restrict__ cc, int m,
+                                                           const uint4* __restrict__ low, int row_u4,
+                                                           float* __restrict__ cc_s, int* __restrict__ perm,
+                                                           uint4* __restrict__ low_s) {
+  __shared__ float tile[1024];
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  float kj = 0.f;
+  if (j < m) {
+    kj = cc[j];
+    if (kj != kj) kj = __int_as_float(0x7f800000);
+  }
+  int rank = 0;
+  for (int base = 0; base < m; base += 1024) {
+    __syncthreads();
+    for (int t = threadIdx.x; t < 1024 && base + t < m; t += blockDim.x) {
+      float v = cc[base + t];
+      tile[t] = (v != v) ? __int_as_float(0x7f800000) : v;
+    }
+    __syncthreads();
+    const int lim = min(1024, m - base);
+    if (j < m) {
+      for (int t = 0; t < lim; ++t) {
+        const float ki = tile[t];
+        const int i = base + t;
+        rank += (ki < kj) || (ki == kj && i < j);
+      }
+    }
+  }
+  if (j < m) {
+    cc_s[rank] = cc[j];
+    perm[rank] = j;
+    const uint4* src = low + static_cast<int64_t>(j) * row_u4;
+    uint4* dst = low_s + static_cast<int64_t>(rank) * row_u4;
+    for (int t = 0; t < row_u4; ++t) dst[t] = src[t];
+  }
+}
+
+cudaError_t launch_sort_centers(const DistJob& j) {
+  const int es = (j.spec->gemm == G_TC_TF32) ? 4 : 2;
+  const int row_u4 = j.ldlow * es / 16;
+  const int m = static_cast<int>(j.m);
+  sort_centers_kernel<<<(m + 255) / 256, 256, 0, j.stream>>>(
+      static_cast<const float*>(j.cc), m, static_cast<const uint4*>(j.Clow), row_u4, j.cc_sorted, j.perm,
+      static_cast<uint4*>(j.Clow_sorted));
+  return cudaGetLastError();
+}
+
 }  // namespace euc

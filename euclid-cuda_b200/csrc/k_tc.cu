@@ -33,11 +33,13 @@ static __device__ int s_tc_err;
 
 constexpr int TC_BM = 128;
 constexpr int TC_STAGES = 4;
-constexpr int TC_EPI_WARPS = 4;
+constexpr int TC_EPI_WARPS = 8;  // two warps per TMEM lane quadrant, each owning half of the columns
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
 constexpr int TC_A_BYTES = TC_BM * 128;  // one K-block of A: 128 rows x 128 bytes
+constexpr int TC_BAR_BYTES = 256;        // mbarriers, TMEM slot, abort flag
+constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 3 * 128 * 4 + 2 * 2 * 128 * 4;  // per-warp staging + row merge
 
-enum TcMode { TM_ARGMIN = 0, TM_D_F32 = 1, TM_D_F16 = 2, TM_D_BF16 = 3 };
+enum TcMode { TM_ARGMIN = 0, TM_D_F32 = 1, TM_D_F16 = 2, TM_D_BF16 = 3, TM_ARGMIN_FAST = 4 };
 
 struct TcArgs {
   int64_t n, m;
@@ -47,8 +49,12 @@ struct TcArgs {
   int n_ct;     // center tiles
   int64_t n_rt; // row tiles
   const float* pp;
-  const float* cc;
+  const float* cc;    // center norms, in the (possibly sorted) order of the B operand
+  const int* perm;    // sorted position -> original center index (fast argmin), else null
   float K;
+  float omk;          // 1 - K (fast screen)
+  float margin;       // fast screen margin, relative to (pp + cc + bias)
+  float ovf;          // fast screen off when pp * max(cc) may overflow the rounded S
   void* D;
   unsigned long long* row_key;
   unsigned long long* list;
@@ -60,6 +66,22 @@ struct TcArgs {
   const float* P;  // fp32 originals (inline recompute when the list is full)
   const float* C;
 };
+
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// The reference's distance for one accumulator value: S rounded to the GEMM's
+// output precision, then max((pp - 2 s) + cc, 0) (form_mixed_and_list_*,
+// euclidean_kernels_mix.cu:203-204).
+template <int SROUND>
+__device__ __forceinline__ float exact_d(float s, float pp, float cc) {
+  if constexpr (SROUND == SR_F16) s = round_f16(s);
+  if constexpr (SROUND == SR_BF16) s = round_bf16(s);
+  return fmaxf(__fadd_rn(__fmaf_rn(-2.f, s, pp), cc), 0.f);
+}
 
 template <int KIND, int SROUND, int FLAG, int MODE, int REC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -76,8 +98,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* accf = empty + TC_STAGES;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* mfull = drain + 1;  // row merge: upper-half warps have published their row minima
+  uint64_t* mdone = mfull + 1;  // row merge: lower-half warps have consumed them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi = reinterpret_cast<float*>(smem + TC_STAGES * stage_bytes + TC_BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -93,6 +118,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&acce[s], TC_EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(mfull, TC_EPI_WARPS / 2);
+    mbar_init(mdone, TC_EPI_WARPS / 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -105,9 +132,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int64_t n_tiles = a.n_rt * a.n_ct;  // (row tile, center tile) pairs owned round-robin by row tile
-  (void)n_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -188,79 +212,156 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    constexpr bool ARGMIN = (MODE == TM_ARGMIN || MODE == TM_ARGMIN_FAST);
+    constexpr bool FAST = (MODE == TM_ARGMIN_FAST);
+    const int ew = warp - 2;             // 0..7
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;            // which half of the tile's columns
+    const int cols = bn >> 1;            // columns per warp: 32, 64 or 128
     const int row_local = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    float* cc_w = epi + ew * 3 * 128;    // this warp's columns: norms
+    float* ccb_w = cc_w + 128;           //                      norms + bias (fast screen)
+    int* perm_w = reinterpret_cast<int*>(ccb_w + 128);  //      original center index
+    float* mv = epi + TC_EPI_WARPS * 3 * 128;           // row merge: [2][128] minima
+    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 256);  //    [2][128] their columns
     const float K = a.K;
-    uint32_t acc_i = 0;
+    uint32_t acc_i = 0, rt_i = 0;
     bool ok = true;
-    for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x) {
+    for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
       const int64_t i = rt * TC_BM + row_local;
       const bool row_ok = i < a.n;
       const float pp = row_ok ? __ldg(a.pp + i) : 0.f;
-      unsigned long long best = ~0ull;
+      float bestv = __int_as_float(0x7f800000);
+      uint32_t besti = 0xffffffffu;
+      float bias = 0.f;
+      if constexpr (FAST) {
+        // warp-uniform bias making every screened value non-negative: x' = cc - 2 s + bias >= 0
+        const float ppf = (row_ok && pp < 3.0e38f) ? pp : 0.f;
+        const unsigned mx = __reduce_max_sync(0xffffffffu, __float_as_uint(ppf));
+        bias = __uint_as_float(mx) * 1.0625f + 1e-30f;
+      }
       for (int ct = 0; ct < a.n_ct; ++ct) {
         const uint32_t buf = acc_i & 1u, use = (acc_i >> 1) & 1u;
+        // stage this warp's columns of the center tile (norms, biased norms, original index)
+        const int64_t jw = static_cast<int64_t>(ct) * bn + half * cols;  // first column of this warp
+        for (int c = lane; c < cols; c += 32) {
+          const bool cv = jw + c < a.m;
+          const float ccv = cv ? __ldg(a.cc + jw + c) : 0.f;
+          cc_w[c] = ccv;
+          if constexpr (FAST) {
+            ccb_w[c] = cv ? __fadd_rn(ccv, bias) : 3.0e38f;
+            perm_w[c] = cv ? __ldg(a.perm + jw + c) : 0;
+          }
+        }
+        __syncwarp();
         if (!mbar_wait(&accf[buf], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        for (int ch = 0; ch < bn / 32; ++ch) {
+        bool lane_exact = true;
+        if constexpr (FAST) {
+          // fast screen only when S cannot overflow its rounded format and pp is finite
+          const int64_t remw = a.m - jw;
+          const int lastc = (int)(remw < cols ? remw : cols) - 1;
+          const float ccmax_t = lastc >= 0 ? cc_w[lastc] : 0.f;
+          lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        }
+        for (int ch = 0; ch < cols / 32; ++ch) {
           float v[32];
-          tmem_ld32(lane_addr + buf * static_cast<uint32_t>(bn) + ch * 32, v);
-          const int64_t j0 = static_cast<int64_t>(ct) * bn + ch * 32;
-          const bool full_chunk = (j0 + 32) <= a.m;
+          tmem_ld32(lane_addr + buf * static_cast<uint32_t>(bn) + half * cols + ch * 32, v);
+          const int c0 = ch * 32;
+          const int64_t j0 = jw + c0;
+          const int64_t remc = a.m - j0;
+          const int nvalid = remc <= 0 ? 0 : (remc >= 32 ? 32 : (int)remc);
+          const uint32_t colmask = !row_ok ? 0u : (nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u));
+          bool exact = true;
+          if constexpr (FAST) {
+            // keys: x' = cc + bias - 2 s with the low 5 mantissa bits replaced by the column
+            float km = 3.0e38f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int64_t j = j0 + e;
-            const bool valid = row_ok && (full_chunk || j < a.m);
-            const float cc = (full_chunk || j < a.m) ? __ldg(a.cc + j) : 0.f;
-            float s = v[e];
-            if constexpr (SROUND == SR_F16) s = round_f16(s);
-            if constexpr (SROUND == SR_BF16) s = round_bf16(s);
-            float d = __fadd_rn(__fmaf_rn(-2.f, s, pp), cc);
-            d = fmaxf(d, 0.f);
-            bool flag = false;
-            if constexpr (FLAG == FL_F32) flag = valid && (d <= __fmul_rn(K, __fadd_rn(pp, cc)));
-            if constexpr (MODE == TM_ARGMIN) {
-              if (valid && !flag) {
-                const unsigned long long key = make_key(d, static_cast<uint32_t>(j));
-                best = key < best ? key : best;
+            for (int e = 0; e < 32; e += 2) {
+              const float x0 = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
+              const float x1 = __fmaf_rn(-2.f, v[e + 1], ccb_w[c0 + e + 1]);
+              const float k0 = __uint_as_float((__float_as_uint(x0) & ~31u) | e);
+              const float k1 = __uint_as_float((__float_as_uint(x1) & ~31u) | (e + 1));
+              km = fmin3(km, k0, k1);
+            }
+            bool cand = lane_exact;
+            if constexpr (FLAG != FL_NONE) {
+              // no pair of this chunk can be flagged unless its smallest x' reaches
+              // max(cc+bias) - (1-K)(pp + min cc) (+ rounding margin); norms are sorted
+              const int lastv = max(0, min(31, nvalid - 1));
+              const float ccmin = cc_w[c0], ccbmax = ccb_w[c0 + lastv];
+              const float thr = ccbmax - a.omk * (pp + ccmin) + (pp + ccbmax) * a.margin;
+              cand = cand || (km <= thr);
+            }
+            exact = __any_sync(0xffffffffu, cand && row_ok);
+            if (!exact && row_ok) {
+              const uint32_t kb = __float_as_uint(km);
+              const float dv = __fadd_rn(__uint_as_float(kb & ~31u) - bias, pp);
+              if (dv < bestv) {
+                bestv = fmaxf(dv, 0.f);
+                besti = static_cast<uint32_t>(perm_w[c0 + (kb & 31u)]);
               }
             }
-            v[e] = d;
-            if constexpr (FLAG == FL_F32) {
-              const unsigned msk = __ballot_sync(0xffffffffu, flag);
-              if (msk) {
-                const int leader = __ffs(msk) - 1;
-                unsigned long long base = 0;
-                if (lane == leader) base = atomicAdd(a.count, static_cast<unsigned long long>(__popc(msk)));
-                base = __shfl_sync(0xffffffffu, base, leader);
-                if (flag) {
-                  const unsigned long long pos = base + __popc(msk & ((1u << lane) - 1u));
-                  if (pos < a.list_cap) {
-                    a.list[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(j);
-                  } else if constexpr (MODE == TM_ARGMIN) {
-                    // list full: recompute in place and fold into the row minimum
-                    const float dd = static_cast<float>(direct_dist<float, REC>(a.P + i * a.dim, a.C + j * a.dim, a.dim));
-                    const unsigned long long key = make_key(dd, static_cast<uint32_t>(j));
-                    best = key < best ? key : best;
+          }
+          if (exact) {
+            uint32_t fm = 0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float cc = cc_w[c0 + e];
+              const float d = exact_d<SROUND>(v[e], pp, cc);
+              bool fl = false;
+              if constexpr (FLAG == FL_F32) fl = d <= __fmul_rn(K, __fadd_rn(pp, cc));
+              if constexpr (ARGMIN) {
+                if (((colmask >> e) & 1u) && !fl) {
+                  if constexpr (FAST) {
+                    const uint32_t jo = static_cast<uint32_t>(perm_w[c0 + e]);
+                    if (d < bestv || (d == bestv && jo < besti)) { bestv = d; besti = jo; }
+                  } else {
+                    if (d < bestv) { bestv = d; besti = static_cast<uint32_t>(j0 + e); }
                   }
+                }
+              }
+              if (fl) fm |= 1u << e;
+              v[e] = d;
+            }
+            fm &= colmask;
+            if constexpr (FLAG == FL_F32) {
+              if (fm) {
+                // append the flagged pairs of this row chunk to the recompute list
+                unsigned long long pos = atomicAdd(a.count, static_cast<unsigned long long>(__popc(fm)));
+                while (fm) {
+                  const int e = __ffs(fm) - 1;
+                  fm &= fm - 1;
+                  const uint32_t jo = FAST ? static_cast<uint32_t>(perm_w[c0 + e]) : static_cast<uint32_t>(j0 + e);
+                  if (pos < a.list_cap) {
+                    a.list[pos] = (static_cast<unsigned long long>(i) << 32) | jo;
+                  } else if constexpr (ARGMIN) {
+                    // list full: recompute in place and fold into the row minimum
+                    const float dd = static_cast<float>(direct_dist<float, REC>(a.P + i * a.dim,
+                                                                               a.C + static_cast<int64_t>(jo) * a.dim,
+                                                                               a.dim));
+                    if (dd < bestv || (dd == bestv && jo < besti)) { bestv = dd; besti = jo; }
+                  }
+                  ++pos;
                   if (a.tile_counts != nullptr)
-                    atomicAdd(&a.tile_counts[(i / a.tile_T) * a.tiles_j + j / a.tile_T], 1);
+                    atomicAdd(&a.tile_counts[(i / a.tile_T) * a.tiles_j + static_cast<int64_t>(jo) / a.tile_T], 1);
                 }
               }
             }
           }
-          if constexpr (MODE != TM_ARGMIN) {
+          if constexpr (!ARGMIN) {
             if (row_ok) {
               if constexpr (MODE == TM_D_F32) {
                 float* drow = static_cast<float*>(a.D) + i * a.m + j0;
-                if (full_chunk && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
+                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
 #pragma unroll
                   for (int e = 0; e < 32; e += 4)
                     *reinterpret_cast<float4*>(drow + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
                 } else {
+#pragma unroll
                   for (int e = 0; e < 32; ++e)
-                    if (j0 + e < a.m) drow[e] = v[e];
+                    if (e < nvalid) drow[e] = v[e];
                 }
               } else {
                 // fp16 / bf16 output: D = round(d) (euclidean_kernels_uniform.cu:62,102)
@@ -273,7 +374,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                   else
                     hv[e] = __bfloat16_as_ushort(__float2bfloat16_rn(v[e]));
                 }
-                if (full_chunk && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
+                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
 #pragma unroll
                   for (int e = 0; e < 32; e += 8) {
                     uint4 w;
@@ -284,8 +385,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     *reinterpret_cast<uint4*>(drow + e) = w;
                   }
                 } else {
+#pragma unroll
                   for (int e = 0; e < 32; ++e)
-                    if (j0 + e < a.m) drow[e] = hv[e];
+                    if (e < nvalid) drow[e] = hv[e];
                 }
               }
             }
@@ -296,8 +398,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) mbar_arrive(&acce[buf]);
         ++acc_i;
       }
-      if constexpr (MODE == TM_ARGMIN) {
-        if (ok && row_ok) a.row_key[i] = best;
+      if constexpr (ARGMIN) {
+        if (!ok) break;
+        // merge the two column halves of each row: upper half publishes, lower half combines
+        const uint32_t par = rt_i & 1u;
+        if (half == 1) {
+          if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag)) { ok = false; break; }
+          mv[128 + row_local] = bestv;
+          mi[128 + row_local] = besti;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(mfull);
+        } else {
+          if (!mbar_wait(mfull, par, abort_flag)) { ok = false; break; }
+          const float ov = mv[128 + row_local];
+          const uint32_t oi = mi[128 + row_local];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(mdone);
+          if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
+          if (row_ok) a.row_key[i] = make_key(bestv, besti);
+        }
       }
     }
     if (!ok) {
@@ -350,7 +469,7 @@ static int pick_bn(int64_t m) {
 }
 
 size_t tc_smem_bytes(int bn) {
-  return 1024 /*alignment slack*/ + TC_STAGES * (TC_A_BYTES + bn * 128) + 256 /*barriers*/;
+  return 1024 /*alignment slack*/ + TC_STAGES * (TC_A_BYTES + bn * 128) + TC_BAR_BYTES + TC_EPI_BYTES;
 }
 
 template <int KIND, int SROUND, int FLAG, int MODE, int REC>
@@ -383,8 +502,13 @@ cudaError_t launch_tc(const DistJob& j) {
   a.n_ct = static_cast<int>((j.m + a.bn - 1) / a.bn);
   a.n_rt = (j.n + TC_BM - 1) / TC_BM;
   a.pp = static_cast<const float*>(j.pp);
-  a.cc = static_cast<const float*>(j.cc);
+  a.cc = static_cast<const float*>(j.fast_argmin ? j.cc_sorted : j.cc);
+  a.perm = j.fast_argmin ? j.perm : nullptr;
   a.K = j.kf;
+  a.omk = 1.f - j.kf;
+  // screen margin: the rounding of S to the GEMM's output format dominates
+  a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-20f);
+  a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
   a.D = j.D;
   a.row_key = j.row_key;
   a.list = j.list;
@@ -398,40 +522,47 @@ cudaError_t launch_tc(const DistJob& j) {
 
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TC_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tb, j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tb, j.fast_argmin ? j.Clow_sorted : j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1))
+    return cudaErrorInvalidValue;
 
   const bool argmin = (j.D == nullptr);
-  int mode = TM_ARGMIN;
+  int mode = j.fast_argmin ? TM_ARGMIN_FAST : TM_ARGMIN;
   if (!argmin) mode = (s->out == OUT_F16) ? TM_D_F16 : (s->out == OUT_BF16 ? TM_D_BF16 : TM_D_F32);
   const cudaStream_t st = j.stream;
 
-#define TC_CASE(KIND_, SR_, FL_, MODE_, REC_)                                                        \
-  if (kind == KIND_ && s->sround == SR_ && s->flag == FL_ && mode == MODE_ && (MODE_ != TM_ARGMIN || \
-                                                                             s->rec == REC_))       \
+#define TC_CASE1(KIND_, SR_, FL_, MODE_, REC_)                                                      \
+  if (kind == KIND_ && s->sround == SR_ && s->flag == FL_ && mode == MODE_ &&                        \
+      ((MODE_ != TM_ARGMIN && MODE_ != TM_ARGMIN_FAST) || s->rec == REC_))                           \
     return launch_tc_t<KIND_, SR_, FL_, MODE_, REC_>(ta, tb, a, st);
+#define TC_CASE(KIND_, SR_, FL_, MODE_, REC_) TC_CASE1(KIND_, SR_, FL_, MODE_, REC_)
+#define TC_CASE_A(KIND_, SR_, FL_, REC_)         \
+  TC_CASE1(KIND_, SR_, FL_, TM_ARGMIN, REC_)     \
+  TC_CASE1(KIND_, SR_, FL_, TM_ARGMIN_FAST, REC_)
 
   // fp16 operands
   TC_CASE(0, SR_F16, FL_F32, TM_D_F32, RC_NONE)      // mix fp16_*
   TC_CASE(0, SR_NONE, FL_F32, TM_D_F32, RC_NONE)     // tiled / tensorcore fp16_*
   TC_CASE(0, SR_F16, FL_NONE, TM_D_F16, RC_NONE)     // uniform fp16
-  TC_CASE(0, SR_F16, FL_F32, TM_ARGMIN, RC_F64)
-  TC_CASE(0, SR_F16, FL_F32, TM_ARGMIN, RC_F32)
-  TC_CASE(0, SR_F16, FL_F32, TM_ARGMIN, RC_F16_ARITH)
-  TC_CASE(0, SR_NONE, FL_F32, TM_ARGMIN, RC_F64)
-  TC_CASE(0, SR_NONE, FL_F32, TM_ARGMIN, RC_F32)
+  TC_CASE_A(0, SR_F16, FL_F32, RC_F64)
+  TC_CASE_A(0, SR_F16, FL_F32, RC_F32)
+  TC_CASE_A(0, SR_F16, FL_F32, RC_F16_ARITH)
+  TC_CASE_A(0, SR_NONE, FL_F32, RC_F64)
+  TC_CASE_A(0, SR_NONE, FL_F32, RC_F32)
   // bf16 operands
   TC_CASE(1, SR_BF16, FL_F32, TM_D_F32, RC_NONE)
   TC_CASE(1, SR_NONE, FL_F32, TM_D_F32, RC_NONE)
   TC_CASE(1, SR_BF16, FL_NONE, TM_D_BF16, RC_NONE)
-  TC_CASE(1, SR_BF16, FL_F32, TM_ARGMIN, RC_F64)
-  TC_CASE(1, SR_BF16, FL_F32, TM_ARGMIN, RC_F32)
-  TC_CASE(1, SR_BF16, FL_F32, TM_ARGMIN, RC_BF16_ARITH)
-  TC_CASE(1, SR_NONE, FL_F32, TM_ARGMIN, RC_F64)
-  TC_CASE(1, SR_NONE, FL_F32, TM_ARGMIN, RC_F32)
+  TC_CASE_A(1, SR_BF16, FL_F32, RC_F64)
+  TC_CASE_A(1, SR_BF16, FL_F32, RC_F32)
+  TC_CASE_A(1, SR_BF16, FL_F32, RC_BF16_ARITH)
+  TC_CASE_A(1, SR_NONE, FL_F32, RC_F64)
+  TC_CASE_A(1, SR_NONE, FL_F32, RC_F32)
   // tf32 operands
   TC_CASE(2, SR_NONE, FL_F32, TM_D_F32, RC_NONE)
-  TC_CASE(2, SR_NONE, FL_F32, TM_ARGMIN, RC_F64)
+  TC_CASE_A(2, SR_NONE, FL_F32, RC_F64)
 #undef TC_CASE
+#undef TC_CASE_A
+#undef TC_CASE1
   return cudaErrorNotSupported;
 }
 

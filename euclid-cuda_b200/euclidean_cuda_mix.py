@@ -19,9 +19,9 @@ def pairwise_euclidean_fp16_fp64_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("fp16_fp64", P, C, kappa, True)
 
 
-def pairwise_euclidean_fp16_fp64_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_fp16_fp64_argmin(P, C, kappa=5.0, exact=False):
     """Fused fp16_fp64 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("fp16_fp64", P, C, kappa)
+    return _ops.run_argmin("fp16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_bf16_fp64(P, C, kappa=5.0):
@@ -34,9 +34,9 @@ def pairwise_euclidean_bf16_fp64_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("bf16_fp64", P, C, kappa, True)
 
 
-def pairwise_euclidean_bf16_fp64_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_bf16_fp64_argmin(P, C, kappa=5.0, exact=False):
     """Fused bf16_fp64 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("bf16_fp64", P, C, kappa)
+    return _ops.run_argmin("bf16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tf32_fp64(P, C, kappa=5.0):
@@ -49,9 +49,9 @@ def pairwise_euclidean_tf32_fp64_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("tf32_fp64", P, C, kappa, True)
 
 
-def pairwise_euclidean_tf32_fp64_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_tf32_fp64_argmin(P, C, kappa=5.0, exact=False):
     """Fused tf32_fp64 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("tf32_fp64", P, C, kappa)
+    return _ops.run_argmin("tf32_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_fp32_fp64(P, C, kappa=5.0):
@@ -64,9 +64,9 @@ def pairwise_euclidean_fp32_fp64_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("fp32_fp64", P, C, kappa, True)
 
 
-def pairwise_euclidean_fp32_fp64_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_fp32_fp64_argmin(P, C, kappa=5.0, exact=False):
     """Fused fp32_fp64 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("fp32_fp64", P, C, kappa)
+    return _ops.run_argmin("fp32_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_fp16_fp16(P, C, kappa=5.0):
@@ -79,9 +79,9 @@ def pairwise_euclidean_fp16_fp16_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("fp16_fp16", P, C, kappa, True)
 
 
-def pairwise_euclidean_fp16_fp16_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_fp16_fp16_argmin(P, C, kappa=5.0, exact=False):
     """Fused fp16_fp16 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("fp16_fp16", P, C, kappa)
+    return _ops.run_argmin("fp16_fp16", P, C, kappa, exact)
 
 
 def pairwise_euclidean_fp16_fp32(P, C, kappa=5.0):
@@ -94,9 +94,9 @@ def pairwise_euclidean_fp16_fp32_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("fp16_fp32", P, C, kappa, True)
 
 
-def pairwise_euclidean_fp16_fp32_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_fp16_fp32_argmin(P, C, kappa=5.0, exact=False):
     """Fused fp16_fp32 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("fp16_fp32", P, C, kappa)
+    return _ops.run_argmin("fp16_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_bf16_bf16(P, C, kappa=5.0):
@@ -109,9 +109,9 @@ def pairwise_euclidean_bf16_bf16_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("bf16_bf16", P, C, kappa, True)
 
 
-def pairwise_euclidean_bf16_bf16_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_bf16_bf16_argmin(P, C, kappa=5.0, exact=False):
     """Fused bf16_bf16 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("bf16_bf16", P, C, kappa)
+    return _ops.run_argmin("bf16_bf16", P, C, kappa, exact)
 
 
 def pairwise_euclidean_bf16_fp32(P, C, kappa=5.0):
@@ -124,9 +124,9 @@ def pairwise_euclidean_bf16_fp32_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("bf16_fp32", P, C, kappa, True)
 
 
-def pairwise_euclidean_bf16_fp32_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_bf16_fp32_argmin(P, C, kappa=5.0, exact=False):
     """Fused bf16_fp32 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("bf16_fp32", P, C, kappa)
+    return _ops.run_argmin("bf16_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_fp32_fp32(P, C, kappa=5.0):
@@ -139,9 +139,9 @@ def pairwise_euclidean_fp32_fp32_with_stats(P, C, kappa=5.0):
     return _ops.run_mix("fp32_fp32", P, C, kappa, True)
 
 
-def pairwise_euclidean_fp32_fp32_argmin(P, C, kappa=5.0):
+def pairwise_euclidean_fp32_fp32_argmin(P, C, kappa=5.0, exact=False):
     """Fused fp32_fp32 distance + row argmin: (labels, min distance, flagged count tensor)."""
-    return _ops.run_argmin("fp32_fp32", P, C, kappa)
+    return _ops.run_argmin("fp32_fp32", P, C, kappa, exact)
 
 
 def get_fallback_count_low(list_count_tensor):

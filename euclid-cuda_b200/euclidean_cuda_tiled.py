@@ -20,9 +20,9 @@ def pairwise_euclidean_tiled_fp16_fp64_with_stats(P, C, kappa, tile_size=32):
     return _ops.run_tiled("fp16_fp64", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_fp16_fp64_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_fp16_fp64_argmin(P, C, kappa, exact=False):
     """Fused tiled_fp16_fp64 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_fp16_fp64", P, C, kappa)
+    return _ops.run_argmin("tiled_fp16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tiled_fp16_fp32(P, C, kappa, tile_size=32):
@@ -35,9 +35,9 @@ def pairwise_euclidean_tiled_fp16_fp32_with_stats(P, C, kappa, tile_size=32):
     return _ops.run_tiled("fp16_fp32", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_fp16_fp32_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_fp16_fp32_argmin(P, C, kappa, exact=False):
     """Fused tiled_fp16_fp32 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_fp16_fp32", P, C, kappa)
+    return _ops.run_argmin("tiled_fp16_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tiled_bf16_fp64(P, C, kappa, tile_size=32):
@@ -50,9 +50,9 @@ def pairwise_euclidean_tiled_bf16_fp64_with_stats(P, C, kappa, tile_size=32):
     return _ops.run_tiled("bf16_fp64", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_bf16_fp64_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_bf16_fp64_argmin(P, C, kappa, exact=False):
     """Fused tiled_bf16_fp64 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_bf16_fp64", P, C, kappa)
+    return _ops.run_argmin("tiled_bf16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tiled_bf16_fp32(P, C, kappa, tile_size=32):
@@ -65,9 +65,9 @@ def pairwise_euclidean_tiled_bf16_fp32_with_stats(P, C, kappa, tile_size=32):
     return _ops.run_tiled("bf16_fp32", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_bf16_fp32_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_bf16_fp32_argmin(P, C, kappa, exact=False):
     """Fused tiled_bf16_fp32 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_bf16_fp32", P, C, kappa)
+    return _ops.run_argmin("tiled_bf16_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tiled_fp32_fp64(P, C, kappa, tile_size=64):
@@ -80,9 +80,9 @@ def pairwise_euclidean_tiled_fp32_fp64_with_stats(P, C, kappa, tile_size=64):
     return _ops.run_tiled("fp32_fp64", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_fp32_fp64_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_fp32_fp64_argmin(P, C, kappa, exact=False):
     """Fused tiled_fp32_fp64 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_fp32_fp64", P, C, kappa)
+    return _ops.run_argmin("tiled_fp32_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tiled_fp32_fp32(P, C, kappa, tile_size=64):
@@ -95,9 +95,9 @@ def pairwise_euclidean_tiled_fp32_fp32_with_stats(P, C, kappa, tile_size=64):
     return _ops.run_tiled("fp32_fp32", P, C, kappa, tile_size, True)
 
 
-def pairwise_euclidean_tiled_fp32_fp32_argmin(P, C, kappa):
+def pairwise_euclidean_tiled_fp32_fp32_argmin(P, C, kappa, exact=False):
     """Fused tiled_fp32_fp32 distance + row argmin (new)."""
-    return _ops.run_argmin("tiled_fp32_fp32", P, C, kappa)
+    return _ops.run_argmin("tiled_fp32_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tensorcore_fp16_fp64(P, C, kappa, tile_size=64):
@@ -105,9 +105,9 @@ def pairwise_euclidean_tensorcore_fp16_fp64(P, C, kappa, tile_size=64):
     return _ops.run_tensorcore("fp16_fp64", P, C, kappa, tile_size)
 
 
-def pairwise_euclidean_tensorcore_fp16_fp64_argmin(P, C, kappa):
+def pairwise_euclidean_tensorcore_fp16_fp64_argmin(P, C, kappa, exact=False):
     """Fused tensorcore_fp16_fp64 distance + row argmin (new)."""
-    return _ops.run_argmin("tensorcore_fp16_fp64", P, C, kappa)
+    return _ops.run_argmin("tensorcore_fp16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tensorcore_fp16_fp32(P, C, kappa, tile_size=64):
@@ -115,9 +115,9 @@ def pairwise_euclidean_tensorcore_fp16_fp32(P, C, kappa, tile_size=64):
     return _ops.run_tensorcore("fp16_fp32", P, C, kappa, tile_size)
 
 
-def pairwise_euclidean_tensorcore_fp16_fp32_argmin(P, C, kappa):
+def pairwise_euclidean_tensorcore_fp16_fp32_argmin(P, C, kappa, exact=False):
     """Fused tensorcore_fp16_fp32 distance + row argmin (new)."""
-    return _ops.run_argmin("tensorcore_fp16_fp32", P, C, kappa)
+    return _ops.run_argmin("tensorcore_fp16_fp32", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tensorcore_bf16_fp64(P, C, kappa, tile_size=64):
@@ -125,9 +125,9 @@ def pairwise_euclidean_tensorcore_bf16_fp64(P, C, kappa, tile_size=64):
     return _ops.run_tensorcore("bf16_fp64", P, C, kappa, tile_size)
 
 
-def pairwise_euclidean_tensorcore_bf16_fp64_argmin(P, C, kappa):
+def pairwise_euclidean_tensorcore_bf16_fp64_argmin(P, C, kappa, exact=False):
     """Fused tensorcore_bf16_fp64 distance + row argmin (new)."""
-    return _ops.run_argmin("tensorcore_bf16_fp64", P, C, kappa)
+    return _ops.run_argmin("tensorcore_bf16_fp64", P, C, kappa, exact)
 
 
 def pairwise_euclidean_tensorcore_bf16_fp32(P, C, kappa, tile_size=64):
@@ -135,6 +135,6 @@ def pairwise_euclidean_tensorcore_bf16_fp32(P, C, kappa, tile_size=64):
     return _ops.run_tensorcore("bf16_fp32", P, C, kappa, tile_size)
 
 
-def pairwise_euclidean_tensorcore_bf16_fp32_argmin(P, C, kappa):
+def pairwise_euclidean_tensorcore_bf16_fp32_argmin(P, C, kappa, exact=False):
     """Fused tensorcore_bf16_fp32 distance + row argmin (new)."""
-    return _ops.run_argmin("tensorcore_bf16_fp32", P, C, kappa)
+    return _ops.run_argmin("tensorcore_bf16_fp32", P, C, kappa, exact)

@@ -211,14 +211,20 @@ EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int6
  * materialising D (SURVEY hot path: distances -> argmin -> center update). */
 
 /* Fused distance + row argmin for distance operator `op` (an EUC_OP_MIX_*,
- * EUC_OP_TILED_*, EUC_OP_TC_*, EUC_OP_SINGLE or EUC_OP_DOUBLE id).  The row's
- * label is the first index of the minimum of the row of D that `op` would have
- * produced (flagged pairs take their recomputed value, as in the reference), i.e.
- * torch.argmin(D, 1).  P/C element type follows `op` (fp64 for EUC_OP_DOUBLE,
- * fp32 otherwise).  Outputs are nullable: labels (int64[n]), labels32 (int32[n]),
- * min_dist (fp32[n]; for EUC_OP_DOUBLE fp64[n]). */
+ * EUC_OP_TILED_*, EUC_OP_TC_*, EUC_OP_SINGLE or EUC_OP_DOUBLE id), without
+ * materialising D.  Flagged pairs take their recomputed value, as in the reference.
+ *   exact != 0: every pair's distance is formed exactly as `op` forms D, and the label
+ *               is torch.argmin(D, 1) of that D (first index of the minimum).
+ *   exact == 0: tensor-core operators screen each 32-center chunk with one fused
+ *               multiply-add, a key and a 3-way min per pair, and evaluate the exact
+ *               path only where a pair could be flagged.  Labels equal the exact ones
+ *               whenever the row's top-two distance gap exceeds 2^-10 (|p|^2 + max|c|^2)
+ *               (2^-7 for bf16 S); min_dist then carries about 18 significant bits.
+ * P/C element type follows `op` (fp64 for EUC_OP_DOUBLE, fp32 otherwise).  Outputs
+ * are nullable: labels (int64[n]), labels32 (int32[n]), min_dist (fp32[n]; fp64[n]
+ * for EUC_OP_DOUBLE). */
 EUC_API int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
-               float kappa, int64_t* labels, int32_t* labels32, void* min_dist,
+               float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,
                uint64_t* d_count, void* ws, size_t ws_bytes, void* stream);
 
 /* Partial center statistics for data-parallel Lloyd iterations: for the n local

@@ -155,15 +155,20 @@ static double direct_one(int rec, int in_type, const void* P, const void* C, int
     }
     return acc;
   }
-  /* half / bfloat arithmetic: each operation exact in double, then one rounding */
-  double (*rr)(double) = (rec == 3) ? r_f16 : r_bf16;
+  /* half / bfloat arithmetic: each operation exact in double, then one rounding.
+   * rec 3/4: diff, square and sum each rounded; rec 5/6: the square and the sum
+   * fused into one rounding (what a contracted __hadd(acc, __hmul(d, d)) computes). */
+  double (*rr)(double) = (rec == 3 || rec == 5) ? r_f16 : r_bf16;
+  const int fused = (rec == 5 || rec == 6);
   double acc = 0.0;
   for (int64_t k = 0; k < d; ++k) {
     const double p = rr(in_val(in_type, P, i * d + k));
     const double c = rr(in_val(in_type, C, j * d + k));
     const double diff = rr(p - c);
-    const double sq = rr(diff * diff);
-    acc = rr(acc + sq);
+    if (fused)
+      acc = rr(fma(diff, diff, acc));
+    else
+      acc = rr(acc + rr(diff * diff));
   }
   return acc;
 }

@@ -125,7 +125,7 @@ def gemm_f64(A, B):
 
 
 # ------------------------------------------------------------------- direct
-REC = {"fp64": 1, "fp32": 2, "fp16": 3, "bf16": 4}
+REC = {"fp64": 1, "fp32": 2, "fp16": 3, "bf16": 4, "fp16_fused": 5, "bf16_fused": 6}
 IN = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.float64): 3}
 
 

@@ -66,8 +66,10 @@ def test_host_queries(lib):
     assert lib.euc_workspace_bytes(999, n, m, d) == 0
     lib.euc_argmin_workspace_bytes.restype = ctypes.c_size_t
     lib.euc_argmin_workspace_bytes.argtypes = lib.euc_workspace_bytes.argtypes
-    # the fused argmin adds one 64-bit row key per point
-    assert lib.euc_argmin_workspace_bytes(10, n, m, d) == ws + ((n * 8 + 255) // 256) * 256
+    # the fused argmin adds the norm-sorted centers (copy, norms, original index) and a
+    # 64-bit row key per point
+    al = lambda b: (b + 255) // 256 * 256
+    assert lib.euc_argmin_workspace_bytes(10, n, m, d) == ws + al(m * 128 * 2) + 2 * al(m * 4) + al(n * 8)
 
 
 def test_compute_entry_rejects_missing_device(lib):
@@ -78,6 +80,6 @@ def test_compute_entry_rejects_missing_device(lib):
     lib.euc_argmin.restype = ctypes.c_int
     lib.euc_last_error.restype = ctypes.c_char_p
     rc = lib.euc_argmin(15, None, None, ctypes.c_int64(10), ctypes.c_int64(10), ctypes.c_int64(4),
-                        ctypes.c_float(5.0), None, None, None, None, None, ctypes.c_size_t(0), None)
+                        ctypes.c_float(5.0), 0, None, None, None, None, None, ctypes.c_size_t(0), None)
     assert rc == 8
     assert b"sm_100" in lib.euc_last_error()

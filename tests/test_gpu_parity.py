@@ -115,15 +115,60 @@ def test_mix_argmin_vs_oracle(op, shape):
 
 
 def test_argmin_matches_engine_D():
-    """Fused argmin == argmin of the engine's own D (same kernels, same S)."""
+    """Exact fused argmin == argmin of the engine's own D (same kernels, same S); the
+    fast screen agrees wherever the top-two gap exceeds its stated bound."""
     P, C = data(1000, 300, 72, "blobs", seed=3)
-    for op in ("fp16_fp32", "bf16_fp64", "tf32_fp64"):
+    Pt, Ct = cuda(P), cuda(C)
+    for op in ("fp16_fp32", "bf16_fp64", "tf32_fp64", "fp16_fp16"):
         kappa = 5.0 if op != "bf16_fp64" else 0.05
-        D = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}")(cuda(P), cuda(C), kappa)
-        lab, md, _ = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")(cuda(P), cuda(C), kappa)
+        D = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}")(Pt, Ct, kappa)
+        lab, md, c1 = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")(Pt, Ct, kappa, exact=True)
         torch.testing.assert_close(lab, D.argmin(1), rtol=0, atol=0)
         torch.testing.assert_close(md, D.min(1).values, rtol=0, atol=0)
+        labf, mdf, c2 = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")(Pt, Ct, kappa)
+        assert int(c1.item()) == int(c2.item())
+        u = 2.0 ** -7 if op.startswith("bf16") else 2.0 ** -10
+        nrm = O.norms_f32(P, O.MIX[op][2]).astype(np.float64)
+        bound = torch.from_numpy(u * (nrm + O.norms_f32(C, O.MIX[op][2]).max())).to(DEV)
+        top2 = torch.topk(D, 2, dim=1, largest=False).values.double()
+        sure = (top2[:, 1] - top2[:, 0]) > bound
+        assert float(sure.double().mean()) > 0.9
+        assert bool((labf[sure] == lab[sure]).all())
+        assert bool(((mdf.double() - md.double()).abs() <= bound + 1e-5 * md.double()).all())
     device_check()
+
+
+@pytest.mark.parametrize("op", ["fp16_fp32", "bf16_fp32", "fp16_fp64"])
+def test_fast_argmin_c2_like(op):
+    """Fast screen at a C2-like shape (1024 centers, d=128) against the exact epilogue."""
+    g = torch.Generator(device=DEV).manual_seed(7)
+    P = torch.randn(65536, 128, generator=g, device=DEV)
+    C = torch.randn(1024, 128, generator=g, device=DEV)
+    P[:4096] = C[:4096 % 1024].repeat(4, 1)[:4096] + 1e-3 * P[:4096]  # exact neighbours -> flagged pairs
+    kappa = 5.0 if op.startswith("fp16") else 0.1
+    fn = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")
+    le, me, ce = fn(P, C, kappa, exact=True)
+    lf, mf, cf = fn(P, C, kappa)
+    assert int(ce.item()) == int(cf.item()) and int(cf.item()) >= 4096
+    agree = (le == lf).double().mean()
+    assert float(agree) > 0.999, float(agree)
+    assert bool((lf[:4096] == torch.arange(4096, device=DEV) % 1024).all())
+    device_check()
+
+
+@pytest.mark.parametrize("op,variants", [("fp16_fp16", ("fp16", "fp16_fused")), ("bf16_bf16", ("bf16", "bf16_fused"))])
+def test_half_arith_recompute_rounding(op, variants):
+    """With every pair flagged, D is entirely the half/bf16-arithmetic recompute; it must
+    equal one of the two rounding sequences bit for bit (the test reports which)."""
+    P, C = data(64, 48, 40, "gauss", seed=12)
+    D = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}")(cuda(P), cuda(C), 1.0e6).cpu().numpy()
+    ii, jj = np.nonzero(np.ones((64, 48), bool))
+    match = {}
+    for v in variants:
+        ref = O.direct_pairs(v, P, C, ii, jj).astype(np.float32).reshape(64, 48)
+        match[v] = float((ref == D).mean())
+    print(op, match)
+    assert max(match.values()) == 1.0, match
 
 
 TILED = ["fp16_fp64", "fp16_fp32", "bf16_fp64", "bf16_fp32", "fp32_fp64", "fp32_fp32"]
