@@ -179,6 +179,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c2", "lloyd"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
@@ -306,7 +307,50 @@ def main():
             "peak_source": f"{peak_src} bf16 dense burst"}
 
     # end to end through the public API, host buffers
+    if a.no_e2e:
+        e2e = None
+    else:
+        e2e = run_e2e(a, cfg, X, Cm, dev, st, barrier, max_over_ranks, world)
+    del X
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        v, cores, sample = cpu_baseline(k, d, seconds=a.cpu_seconds)
+        if a.workload == "lloyd":
+            v = v * 1e9 / (2.0 * n * k * d)
+            cu = "iter/s"
+        else:
+            cu = "GFLOP/s"
+        cpu = {"value": v, "unit": cu, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
+                "dtype": "fp16" if cfg["op"].startswith("fp16") else "bf16", "data": "synthetic",
+                "config": {"workload": "c2: distance+argmin n=2^20 x d=128, k=1024, fp16 GEMM + fp32 recompute, "
+                                       "kappa=5" if a.workload == "c2" else
+                           "c4: Lloyd n=2^24 x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
+                           "n_per_rank": n_local, "k": k, "d": d, "op": cfg["op"], "kappa": cfg["kappa"],
+                           "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
+                           "parallelism": f"dp{world}"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+                "gpu_launches": launches_per_step * a.steps, "flagged_last_step": int(cnt.item())}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(a, cfg, X, Cm, dev, st, barrier, max_over_ranks, world):
+    """The metric through the public API with pinned host buffers: every step copies X and
+    C host->device and the labels device->host inside the timed region."""
+    import torch
+
+    import _ops
     import euclidean_cuda_mix
+    n_local, d = X.shape
+    k = Cm.shape[0]
     Xh = X.cpu().pin_memory()
     Ch = Cm.cpu().pin_memory()
     out_h = torch.empty(n_local, dtype=torch.int64).pin_memory()
@@ -338,33 +382,7 @@ def main():
     if a.workload == "lloyd":
         e2e["note"] = "distance+argmin phase of one iteration through the public API"
 
-    cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        v, cores, sample = cpu_baseline(k, d, seconds=a.cpu_seconds)
-        if a.workload == "lloyd":
-            v = v * 1e9 / (2.0 * n * k * d)
-            cu = "iter/s"
-        else:
-            cu = "GFLOP/s"
-        cpu = {"value": v, "unit": cu, "cores": cores, "kind": "port", "sample": sample}
-
-    if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps,
-                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-                "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
-                "dtype": "fp16" if cfg["op"].startswith("fp16") else "bf16", "data": "synthetic",
-                "config": {"workload": "c2: distance+argmin n=2^20 x d=128, k=1024, fp16 GEMM + fp32 recompute, "
-                                       "kappa=5" if a.workload == "c2" else
-                           "c4: Lloyd n=2^24 x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
-                           "n_per_rank": n_local, "k": k, "d": d, "op": cfg["op"], "kappa": cfg["kappa"],
-                           "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
-                           "parallelism": f"dp{world}"},
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-                "gpu_launches": launches_per_step * a.steps, "flagged_last_step": int(cnt.item())}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return e2e
 
 
 if __name__ == "__main__":

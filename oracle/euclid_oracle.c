@@ -111,8 +111,10 @@ void orc_gemm_f64(const double* A, const double* B, int64_t n, int64_t m, int64_
  * rec:     1 fp64 fma   (direct_on_list_rowmajor, euclidean_kernels_mix.cu:156-177;
  *                        direct_on_list_fp16/_bf16/_fp64, euclidean_kernels_advanced.cu:148-220)
  *          2 fp32 fma   (direct_fp32_on_list, euclidean_kernels_mix.cu:481-504)
- *          3 fp16 arith (direct_fp16_on_list, euclidean_kernels_mix.cu:412-439: __hsub/__hmul/__hadd)
- *          4 bf16 arith (direct_bf16_on_list, euclidean_kernels_mix.cu:442-469) */
+ *          3 fp16 arith, every operation rounded (direct_fp16_on_list, euclidean_kernels_mix.cu:412-439)
+ *          4 bf16 arith, every operation rounded (direct_bf16_on_list, euclidean_kernels_mix.cu:442-469)
+ *          5, 6: as 3, 4 with the square and the sum rounded once -- the sequence the
+ *             reference's __hadd(acc, __hmul(diff, diff)) executes when built for sm_100 */
 static inline double h2d(uint16_t h) {
   const int s = h >> 15, e = (h >> 10) & 31, f = h & 1023;
   double v;

@@ -144,7 +144,7 @@ def test_fast_argmin_c2_like(op):
     g = torch.Generator(device=DEV).manual_seed(7)
     P = torch.randn(65536, 128, generator=g, device=DEV)
     C = torch.randn(1024, 128, generator=g, device=DEV)
-    P[:4096] = C[:4096 % 1024].repeat(4, 1)[:4096] + 1e-3 * P[:4096]  # exact neighbours -> flagged pairs
+    P[:4096] = C[torch.arange(4096, device=DEV) % 1024] + 1e-3 * P[:4096]  # near-duplicates -> flagged pairs
     kappa = 5.0 if op.startswith("fp16") else 0.1
     fn = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")
     le, me, ce = fn(P, C, kappa, exact=True)
