@@ -38,8 +38,12 @@ __global__ void __launch_bounds__(256) recompute_kernel(const RecArgs a) {
   const unsigned long long cnt = *a.count;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   const uint64_t t0 = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (cnt <= a.cap) {
-    for (uint64_t t = t0; t < cnt; t += stride) {
+  // argmin: the listed pairs always go through here (the distance epilogue folded the
+  // ones beyond the list's capacity in place); D: an overflowing list is ignored and
+  // the dense sweep below recomputes every flagged pair instead
+  if (ARGMIN || cnt <= a.cap) {
+    const unsigned long long nlist = cnt < a.cap ? cnt : a.cap;
+    for (uint64_t t = t0; t < nlist; t += stride) {
       const unsigned long long e = a.list[t];
       const int64_t i = static_cast<int64_t>(e >> 32);
       const int64_t j = static_cast<int64_t>(e & 0xffffffffull);

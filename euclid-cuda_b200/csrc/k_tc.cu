@@ -26,13 +26,13 @@
 #include "direct.cuh"
 
 #include <cudaTypedefs.h>
+#include <algorithm>
 
 namespace euc {
 
 static __device__ int s_tc_err;
 
 constexpr int TC_BM = 128;
-constexpr int TC_STAGES = 4;
 constexpr int TC_EPI_WARPS = 8;  // two warps per TMEM lane quadrant, each owning half of the columns
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
 constexpr int TC_A_BYTES = TC_BM * 128;  // one K-block of A: 128 rows x 128 bytes
@@ -46,6 +46,8 @@ struct TcArgs {
   int dim;
   int kblocks;  // K-blocks of 128 bytes
   int bn;
+  int nst;      // pipeline stages
+  int a_res;    // 1: the row tile's A stays resident (double-buffered); stages carry B only
   int n_ct;     // center tiles
   int64_t n_rt; // row tiles
   const float* pp;
@@ -67,12 +69,6 @@ struct TcArgs {
   const float* C;
 };
 
-__device__ __forceinline__ float fmin3(float a, float b, float c) {
-  float r;
-  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 // The reference's distance for one accumulator value: S rounded to the GEMM's
 // output precision, then max((pp - 2 s) + cc, 0) (form_mixed_and_list_*,
 // euclidean_kernels_mix.cu:203-204).
@@ -91,29 +87,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // 1024-byte alignment of every stage (required by the 128B swizzle atoms)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = a.bn;
+  const int NST = a.nst;
+  const bool a_res = a.a_res != 0;
   const uint32_t b_bytes = static_cast<uint32_t>(bn) * 128u;
-  const uint32_t stage_bytes = TC_A_BYTES + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * stage_bytes);
-  uint64_t* empty = full + TC_STAGES;
-  uint64_t* accf = empty + TC_STAGES;
+  // resident mode: [A buf 0 | A buf 1 | B stage 0..NST-1]; streaming mode: [A+B stage 0..NST-1]
+  const uint32_t a_bytes = static_cast<uint32_t>(a.kblocks) * TC_A_BYTES;
+  const uint32_t stage_bytes = a_res ? b_bytes : (TC_A_BYTES + b_bytes);
+  uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + NST * stage_bytes);
+  uint64_t* empty = full + NST;
+  uint64_t* afull = empty + NST;
+  uint64_t* aempty = afull + 2;
+  uint64_t* accf = aempty + 2;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
   uint64_t* mfull = drain + 1;  // row merge: upper-half warps have published their row minima
   uint64_t* mdone = mfull + 1;  // row merge: lower-half warps have consumed them
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi = reinterpret_cast<float*>(smem + TC_STAGES * stage_bytes + TC_BAR_BYTES);
+  float* epi = reinterpret_cast<float*>(stage_base + NST * stage_bytes + TC_BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t ncols = 2u * static_cast<uint32_t>(bn);  // power of two >= 128
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
       mbar_init(&accf[s], 1);
       mbar_init(&acce[s], TC_EPI_WARPS);
     }
@@ -136,22 +141,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t stage = 0, phase = 0;
-      uint32_t issued_mask = 0, last_phase = 0;
+      uint32_t stage = 0, phase = 0, rt_i = 0;
+      uint32_t issued_mask = 0, last_phase = 0, a_issued = 0, a_last = 0;
       bool ok = true;
       const int kelems = (KIND == 2) ? 32 : 64;  // elements per 128-byte K-block
-      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x) {
+      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+        const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
+        if (a_res) {
+          // the whole 128-row A tile once per row tile, into its own buffer
+          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&afull[abuf], a_bytes);
+          uint8_t* sA = smem + abuf * a_bytes;
+          for (int kb = 0; kb < a.kblocks; ++kb)
+            tma_load_2d(sA + kb * TC_A_BYTES, &tmA, &afull[abuf], kb * kelems, static_cast<int>(rt * TC_BM));
+          a_issued |= 1u << abuf;
+          a_last = (a_last & ~(1u << abuf)) | (ause << abuf);
+        }
         for (int ct = 0; ct < a.n_ct && ok; ++ct) {
           for (int kb = 0; kb < a.kblocks; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-            uint8_t* sA = smem + stage * stage_bytes;
-            uint8_t* sB = sA + TC_A_BYTES;
+            uint8_t* st = stage_base + stage * stage_bytes;
             mbar_arrive_expect_tx(&full[stage], stage_bytes);
-            tma_load_2d(sA, &tmA, &full[stage], kb * kelems, static_cast<int>(rt * TC_BM));
-            tma_load_2d(sB, &tmB, &full[stage], kb * kelems, ct * bn);
+            if (a_res) {
+              tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * bn);
+            } else {
+              tma_load_2d(st, &tmA, &full[stage], kb * kelems, static_cast<int>(rt * TC_BM));
+              tma_load_2d(st + TC_A_BYTES, &tmB, &full[stage], kb * kelems, ct * bn);
+            }
             issued_mask |= 1u << stage;
             last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
-            if (++stage == TC_STAGES) { stage = 0; phase ^= 1u; }
+            if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
           }
         }
       }
@@ -159,21 +178,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         *abort_flag = 1;
         atomicExch(&s_tc_err, DEV_TIMEOUT_PRODUCER);
       }
-      // Drain: every issued stage's last load must have landed before smem is released.
-      for (int s = 0; s < TC_STAGES; ++s)
-        if (issued_mask & (1u << s)) {
-          volatile int no_abort = 0;
-          mbar_wait(&full[s], (last_phase >> s) & 1u, &no_abort);
-        }
+      // Drain: every issued copy must have landed before shared memory is released.
+      volatile int no_abort = 0;
+      for (int s = 0; s < NST; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_phase >> s) & 1u, &no_abort);
+      for (int s = 0; s < 2; ++s)
+        if (a_issued & (1u << s)) mbar_wait(&afull[s], (a_last >> s) & 1u, &no_abort);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
       const uint32_t idesc = umma_idesc(fmt, TC_BM, static_cast<uint32_t>(bn));
-      uint32_t stage = 0, phase = 0, acc_i = 0;
+      uint32_t stage = 0, phase = 0, acc_i = 0, rt_i = 0;
       bool ok = true;
-      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x) {
+      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+        const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
+        const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
+        if (a_res) {
+          if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
+        }
         for (int ct = 0; ct < a.n_ct && ok; ++ct) {
           const uint32_t buf = acc_i & 1u, use = (acc_i >> 1) & 1u;
           if (!mbar_wait(&acce[buf], use ^ 1u, abort_flag)) { ok = false; break; }
@@ -182,8 +206,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int kb = 0; kb < a.kblocks; ++kb) {
             if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sA = smem_u32(smem + stage * stage_bytes);
-            const uint32_t sB = sA + TC_A_BYTES;
+            const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
+            const uint32_t sA = a_res ? sAres + kb * TC_A_BYTES : st;
+            const uint32_t sB = a_res ? st : st + TC_A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes = one 128-byte swizzle row
               const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
@@ -194,12 +219,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
             }
             umma_commit(&empty[stage]);
-            if (++stage == TC_STAGES) { stage = 0; phase ^= 1u; }
+            if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
           umma_commit(&accf[buf]);
           ++acc_i;
         }
+        if (a_res && ok) umma_commit(&aempty[abuf]);  // A buffer free once this row tile's MMAs retire
       }
       if (!ok) {
         *abort_flag = 1;
@@ -218,6 +244,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int q = warp & 3;              // TMEM lane quadrant this warp may access
     const int half = ew >> 2;            // which half of the tile's columns
     const int cols = bn >> 1;            // columns per warp: 32, 64 or 128
+    const int nch = cols >> 5;           // 32-column chunks per warp and tile
     const int row_local = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     float* cc_w = epi + ew * 3 * 128;    // this warp's columns: norms
@@ -226,8 +253,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     float* mv = epi + TC_EPI_WARPS * 3 * 128;           // row merge: [2][128] minima
     uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 256);  //    [2][128] their columns
     const float K = a.K;
+
+    // Center metadata of the next tile this warp will process is loaded one tile ahead
+    // (4 columns per lane at most), so the global-load latency overlaps the current tile.
+    float pf_cc[4];
+    int pf_perm[4];
+    auto prefetch = [&](int64_t rt_next, int ct_next) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        pf_cc[t] = 0.f;
+        pf_perm[t] = 0;
+      }
+      if (rt_next >= a.n_rt) return;
+      const int64_t jw = static_cast<int64_t>(ct_next) * bn + half * cols;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int c = lane + 32 * t;
+        if (c < cols && jw + c < a.m) {
+          pf_cc[t] = __ldg(a.cc + jw + c);
+          if constexpr (FAST) pf_perm[t] = __ldg(a.perm + jw + c);
+        }
+      }
+    };
+
     uint32_t acc_i = 0, rt_i = 0;
     bool ok = true;
+    prefetch(blockIdx.x, 0);
     for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
       const int64_t i = rt * TC_BM + row_local;
       const bool row_ok = i < a.n;
@@ -243,18 +294,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       for (int ct = 0; ct < a.n_ct; ++ct) {
         const uint32_t buf = acc_i & 1u, use = (acc_i >> 1) & 1u;
-        // stage this warp's columns of the center tile (norms, biased norms, original index)
         const int64_t jw = static_cast<int64_t>(ct) * bn + half * cols;  // first column of this warp
-        for (int c = lane; c < cols; c += 32) {
-          const bool cv = jw + c < a.m;
-          const float ccv = cv ? __ldg(a.cc + jw + c) : 0.f;
-          cc_w[c] = ccv;
-          if constexpr (FAST) {
-            ccb_w[c] = cv ? __fadd_rn(ccv, bias) : 3.0e38f;
-            perm_w[c] = cv ? __ldg(a.perm + jw + c) : 0;
+        // publish the prefetched metadata of this tile, then start fetching the next tile's
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int c = lane + 32 * t;
+          if (c < cols) {
+            const bool cv = jw + c < a.m;
+            cc_w[c] = pf_cc[t];
+            if constexpr (FAST) {
+              ccb_w[c] = cv ? __fadd_rn(pf_cc[t], bias) : 3.0e38f;
+              perm_w[c] = pf_perm[t];
+            }
           }
         }
         __syncwarp();
+        if (ct + 1 < a.n_ct)
+          prefetch(rt, ct + 1);
+        else
+          prefetch(rt + gridDim.x, 0);
         if (!mbar_wait(&accf[buf], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
         bool lane_exact = true;
@@ -265,9 +323,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const float ccmax_t = lastc >= 0 ? cc_w[lastc] : 0.f;
           lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
         }
-        for (int ch = 0; ch < cols / 32; ++ch) {
-          float v[32];
-          tmem_ld32(lane_addr + buf * static_cast<uint32_t>(bn) + half * cols + ch * 32, v);
+
+        // one 32-column chunk: screen (fast) and / or exact evaluation
+        auto process = [&](int ch, float (&v)[32]) {
           const int c0 = ch * 32;
           const int64_t j0 = jw + c0;
           const int64_t remc = a.m - j0;
@@ -275,16 +333,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t colmask = !row_ok ? 0u : (nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u));
           bool exact = true;
           if constexpr (FAST) {
-            // keys: x' = cc + bias - 2 s with the low 5 mantissa bits replaced by the column
-            float km = 3.0e38f;
+            // keys: x' = cc + bias - 2 s with the low 5 mantissa bits replaced by the column;
+            // their minimum by a depth-4 tree of 3-way mins
+            float kk[32];
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float x0 = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
-              const float x1 = __fmaf_rn(-2.f, v[e + 1], ccb_w[c0 + e + 1]);
-              const float k0 = __uint_as_float((__float_as_uint(x0) & ~31u) | e);
-              const float k1 = __uint_as_float((__float_as_uint(x1) & ~31u) | (e + 1));
-              km = fmin3(km, k0, k1);
+            for (int e = 0; e < 32; ++e) {
+              const float x = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
+              kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
             }
+            float t[11];
+#pragma unroll
+            for (int u = 0; u < 10; ++u) t[u] = fmin3(kk[3 * u], kk[3 * u + 1], kk[3 * u + 2]);
+            t[10] = fminf(kk[30], kk[31]);
+            const float km = fmin3(fmin3(t[0], t[1], t[2]), fmin3(t[3], t[4], t[5]),
+                                   fmin3(fmin3(t[6], t[7], t[8]), t[9], t[10]));
             bool cand = lane_exact;
             if constexpr (FLAG != FL_NONE) {
               // no pair of this chunk can be flagged unless its smallest x' reaches
@@ -392,6 +454,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               }
             }
           }
+        };
+
+        const uint32_t tbase = lane_addr + buf * static_cast<uint32_t>(bn) + half * cols;
+        for (int ch = 0; ch < nch; ch += 2) {
+          float va[32], vb[32];
+          if (ch + 1 < nch) {
+            tmem_ld64(tbase + ch * 32, va, vb);  // two chunks per TMEM round trip
+            process(ch, va);
+            process(ch + 1, vb);
+          } else {
+            tmem_ld32(tbase + ch * 32, va);
+            process(ch, va);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -468,15 +543,34 @@ static int pick_bn(int64_t m) {
   return 256;
 }
 
-size_t tc_smem_bytes(int bn) {
-  return 1024 /*alignment slack*/ + TC_STAGES * (TC_A_BYTES + bn * 128) + TC_BAR_BYTES + TC_EPI_BYTES;
+constexpr size_t TC_SMEM_LIMIT = 232448;  // 227 KiB opt-in per block on sm_100
+constexpr size_t TC_FIXED = 1024 /*alignment slack*/ + TC_BAR_BYTES + TC_EPI_BYTES;
+
+// Pick the pipeline: resident A (double-buffered) with as many B stages as fit, or,
+// when two A tiles do not fit next to 3 B stages, streaming (A + B) stages.
+static void pick_pipeline(int bn, int kblocks, int* nst, int* a_res) {
+  const size_t b = static_cast<size_t>(bn) * 128, abytes = static_cast<size_t>(kblocks) * TC_A_BYTES;
+  const size_t avail = TC_SMEM_LIMIT - TC_FIXED;
+  if (2 * abytes + 3 * b <= avail) {
+    *a_res = 1;
+    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / b));
+  } else {
+    *a_res = 0;
+    *nst = static_cast<int>(std::min<size_t>(8, avail / (TC_A_BYTES + b)));
+  }
+}
+
+size_t tc_smem_bytes(int bn, int kblocks, int nst, int a_res) {
+  const size_t b = static_cast<size_t>(bn) * 128;
+  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TC_A_BYTES + nst * b : nst * (TC_A_BYTES + b);
+  return TC_FIXED + body;
 }
 
 template <int KIND, int SROUND, int FLAG, int MODE, int REC>
 static cudaError_t launch_tc_t(const CUtensorMap& ta, const CUtensorMap& tb, const TcArgs& args,
                                cudaStream_t st) {
   auto kern = dist_tc_kernel<KIND, SROUND, FLAG, MODE, REC>;
-  const size_t smem = tc_smem_bytes(args.bn);
+  const size_t smem = tc_smem_bytes(args.bn, args.kblocks, args.nst, args.a_res);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int grid = num_sms();
@@ -501,6 +595,7 @@ cudaError_t launch_tc(const DistJob& j) {
   a.bn = pick_bn(j.m);
   a.n_ct = static_cast<int>((j.m + a.bn - 1) / a.bn);
   a.n_rt = (j.n + TC_BM - 1) / TC_BM;
+  pick_pipeline(a.bn, a.kblocks, &a.nst, &a.a_res);
   a.pp = static_cast<const float*>(j.pp);
   a.cc = static_cast<const float*>(j.fast_argmin ? j.cc_sorted : j.cc);
   a.perm = j.fast_argmin ? j.perm : nullptr;
