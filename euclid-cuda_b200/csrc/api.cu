@@ -68,6 +68,7 @@ static int fail(int status, const std::string& msg) {
   return status;
 }
 static int ok() { return EUC_OK; }
+int set_error(int status, const char* msg) { return fail(status, msg); }
 static int cuda_fail(cudaError_t e, const char* where) {
   return fail(EUC_ERR_LAUNCH, std::string(where) + ": " + cudaGetErrorString(e));
 }

@@ -130,6 +130,8 @@ void timing_end(cudaStream_t st);
 
 int num_sms();
 bool device_is_sm100();
+// records `msg` as the calling thread's euc_last_error() text and returns `status`
+int set_error(int status, const char* msg);
 int device_error_and_clear();
 
 }  // namespace euc

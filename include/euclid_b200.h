@@ -227,6 +227,19 @@ EUC_API int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t 
                float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,
                uint64_t* d_count, void* ws, size_t ws_bytes, void* stream);
 
+/* No counterpart in the reference.  euc_argmin without a workspace, for callers that
+ * cannot allocate device memory (a host binding with no device allocator, or a
+ * process whose memory pool already holds the device's memory): the scratch is one
+ * static device array of euc_argmin_noalloc_max_bytes() (32 MiB) per device; nothing
+ * is allocated.  A shape whose euc_argmin_workspace_bytes() exceeds that is rejected
+ * with EUC_ERR_WORKSPACE.  The first call on each device takes the array's address
+ * (with that device current) and should come before any stream capture.  Calls that
+ * overlap in time on one device race on the shared scratch. */
+EUC_API size_t euc_argmin_noalloc_max_bytes(void);
+EUC_API int euc_argmin_noalloc(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
+                       float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,
+                       uint64_t* d_count, void* stream);
+
 /* Partial center statistics for data-parallel Lloyd iterations: for the n local
  * rows, stats[c*(dim+1) + j] = sum of X[i, j] over rows with label c (j < dim) and
  * stats[c*(dim+1) + dim] = number of such rows, all fp64 (exact integer counts).
