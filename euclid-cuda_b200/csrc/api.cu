@@ -87,7 +87,11 @@ int num_sms() {
   return g_sms[dev];
 }
 int tc_error_and_clear();
-int device_error_and_clear() { return tc_error_and_clear(); }
+int tf_error_and_clear();
+int device_error_and_clear() {
+  const int a = tc_error_and_clear(), b = tf_error_and_clear();
+  return a ? a : b;
+}
 
 bool device_is_sm100() {
   int dev = 0, major = 0;
@@ -120,10 +124,12 @@ void timing_end(cudaStream_t st) {
 static inline size_t al(size_t b) { return (b + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hdr, pp, cc, plow, clow, clow_s, cc_s, perm, list, key, val64, idx64, total;
-  unsigned long long cap;
+  size_t hdr, pp, cc, plow, clow, clow_s, cc_s, perm, list, key, val64, idx64, rcnt, redo, clist, cs, total;
+  unsigned long long cap, ccap;
   int ldlow;
 };
+
+constexpr int kMaxRegions = 1024;  // CTAs of the fast argmin screen: at most one per SM
 
 static int low_esize(const OpSpec* s) { return s->gemm == G_TC_TF32 ? 4 : 2; }
 static bool is_tc(const OpSpec* s) { return s->gemm == G_TC_F16 || s->gemm == G_TC_BF16 || s->gemm == G_TC_TF32; }
@@ -142,9 +148,13 @@ static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, boo
     L.plow = off; off += al(static_cast<size_t>(n) * L.ldlow * es);
     L.clow = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
     if (argmin && s->flag != FL_NONE) {  // norm-sorted centers for the fast argmin screen
+      // norms and original indices padded to whole 256-center tiles (copied tile by tile)
+      const size_t mpad = static_cast<size_t>((m + 255) / 256) * 256;
       L.clow_s = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
-      L.cc_s = off; off += al(static_cast<size_t>(m) * 4);
-      L.perm = off; off += al(static_cast<size_t>(m) * 4);
+      L.cc_s = off; off += al(mpad * 4);
+      L.perm = off; off += al(mpad * 4);
+      L.rcnt = off; off += al(static_cast<size_t>(kMaxRegions) * 4);
+      L.redo = off; off += al(static_cast<size_t>(n));
     }
   }
   L.cap = 0;
@@ -156,6 +166,13 @@ static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, boo
     cap = std::min<unsigned long long>(cap, nm);
     L.cap = cap;
     L.list = off; off += al(cap * 8);
+    if (L.redo) {
+      // fast argmin lists candidate 32-center chunks with their accumulators: room for two per row
+      const unsigned long long chunks = static_cast<unsigned long long>(n) * static_cast<unsigned long long>((m + 31) / 32);
+      L.ccap = std::min<unsigned long long>(chunks, std::max<unsigned long long>(2ull * n, 1ull << 16));
+      L.clist = off; off += al(L.ccap * 8);
+      L.cs = off; off += al(L.ccap * 128);
+    }
   }
   if (argmin) {
     if (s->form == FM_F64 && s->flag == FL_NONE) {
@@ -243,16 +260,25 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.Plow = is_tc(s) ? w + L.plow : nullptr;
   j.Clow = is_tc(s) ? w + L.clow : nullptr;
   j.ldlow = L.ldlow;
-  j.fast_argmin = argmin && is_tc(s) && s->flag != FL_NONE && !o.exact;
+  // the screen bounds flagged pairs through 1 - K > 0
+  j.fast_argmin = argmin && is_tc(s) && s->flag != FL_NONE && !o.exact && j.kf < 1.f;
   j.Clow_sorted = L.clow_s ? w + L.clow_s : nullptr;
   j.cc_sorted = L.cc_s ? reinterpret_cast<float*>(w + L.cc_s) : nullptr;
   j.perm = L.perm ? reinterpret_cast<int*>(w + L.perm) : nullptr;
   j.row_key = (argmin && L.key) ? reinterpret_cast<unsigned long long*>(w + L.key) : nullptr;
   j.row_val64 = (argmin && L.val64) ? reinterpret_cast<double*>(w + L.val64) : nullptr;
   j.row_idx64 = (argmin && L.idx64) ? reinterpret_cast<long long*>(w + L.idx64) : nullptr;
+  j.chunk_list = L.clist ? reinterpret_cast<unsigned long long*>(w + L.clist) : nullptr;
+  j.chunk_s = L.cs ? reinterpret_cast<float*>(w + L.cs) : nullptr;
+  j.chunk_cap = L.ccap;
+  j.regions = j.fast_argmin ? tc_fast_regions(n) : 0;
+  j.region_cnt = L.rcnt ? reinterpret_cast<uint32_t*>(w + L.rcnt) : nullptr;
+  j.redo = L.redo ? w + L.redo : nullptr;
   j.stream = st;
+  if (j.fast_argmin && j.regions > kMaxRegions) return fail(EUC_ERR_UNSUPPORTED, "more SMs than list regions");
 
   cudaError_t e = cudaMemsetAsync(j.count, 0, 8, st);
+  if (e == cudaSuccess && j.fast_argmin) e = cudaMemsetAsync(j.redo, 0, static_cast<size_t>(n), st);
   if (e == cudaSuccess && o.tile_counts) {
     const int64_t nt = ((n + o.tile_T - 1) / o.tile_T) * j.tiles_j;
     e = cudaMemsetAsync(o.tile_counts, 0, static_cast<size_t>(nt) * 4, st);
@@ -262,9 +288,11 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
   if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
   if (e != cudaSuccess) return cuda_fail(e, "prep");
-  e = is_tc(s) ? launch_tc(j) : launch_simt(j);
+  e = j.fast_argmin ? launch_tc_fast(j) : (is_tc(s) ? launch_tc(j) : launch_simt(j));
   if (e != cudaSuccess) return cuda_fail(e, s->name);
-  e = launch_recompute(j);
+  if (j.fast_argmin) e = launch_eval_chunks(j);
+  if (e == cudaSuccess) e = launch_recompute(j);
+  if (e == cudaSuccess && j.fast_argmin) e = launch_redo_rows(j);
   if (e != cudaSuccess) return cuda_fail(e, "recompute");
   if (argmin) {
     if (j.row_key) {

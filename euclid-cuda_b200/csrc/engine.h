@@ -99,6 +99,15 @@ struct DistJob {
   void* Clow_sorted;
   float* cc_sorted;
   int* perm;
+  // fast argmin: candidate chunks, (row << 32 | first sorted column) entries and their
+  // 32 fp32 accumulator values, kept in one region of chunk_cap / regions entries per
+  // CTA of the screening kernel
+  unsigned long long* chunk_list;
+  float* chunk_s;
+  unsigned long long chunk_cap;
+  int regions;
+  uint32_t* region_cnt;          // entries per region (written by the screening kernel)
+  uint8_t* redo;                 // rows whose candidates did not fit: recomputed whole
   cudaStream_t stream;
 };
 
@@ -106,6 +115,14 @@ struct DistJob {
 cudaError_t launch_prep(const DistJob& j, bool points, bool make_low);
 cudaError_t launch_sort_centers(const DistJob& j);
 cudaError_t launch_tc(const DistJob& j);
+// fast argmin: screening kernel, exact evaluation of the candidate chunks (flagged pairs
+// go to the recompute list), and rows whose candidates did not fit
+cudaError_t launch_tc_fast(const DistJob& j);
+cudaError_t launch_eval_chunks(const DistJob& j);
+cudaError_t launch_redo_rows(const DistJob& j);
+int tc_fast_regions(int64_t n);  // CTAs (= list regions) of the screening kernel
+bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows, bool is_f32,
+                  bool is_bf16);
 cudaError_t launch_simt(const DistJob& j);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);

@@ -15,6 +15,8 @@
 #include "common.cuh"
 #include "engine.h"
 
+#include <type_traits>
+
 namespace euc {
 
 template <typename T> __device__ __forceinline__ double to_d(T x);
@@ -124,10 +126,109 @@ __global__ void __launch_bounds__(128) prep_rows_kernel(const TIN* __restrict__ 
   }
 }
 
+// fp32 rows with dim % 4 == 0 and 16-byte aligned rows: same results, vector traffic.
+// A half-warp reads one row's 64-column slab with 16-byte loads (two rows per load
+// instruction), writes the low copy straight from registers (8- or 16-byte stores,
+// coalesced) and parks the slab in shared memory, from where lane r folds row r into
+// its norm in column order.
+template <int NORM, int LOWT>
+__global__ void __launch_bounds__(128) prep_rows_v4_kernel(const float* __restrict__ X, int64_t rows, int dim,
+                                                           void* __restrict__ low, int ldl,
+                                                           float* __restrict__ norms) {
+  __shared__ float tile[4][32][65];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 4 + warp) * 32;
+  if (row0 >= rows) return;
+  float (*t)[65] = tile[warp];
+  const int half = lane >> 4, hl = lane & 15;
+  float acc = 0.f;
+  for (int c0 = 0; c0 < dim; c0 += 64) {
+    const int c = c0 + hl * 4;
+    const bool cok = c < dim;  // dim % 4 == 0: the whole vector is inside the row
+    float4 v[16];
+#pragma unroll
+    for (int it = 0; it < 16; ++it) {
+      const int64_t gr = row0 + it * 2 + half;
+      v[it] = (gr < rows && cok) ? __ldg(reinterpret_cast<const float4*>(X + gr * dim + c))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int it = 0; it < 16; ++it) {
+      const int r = it * 2 + half;
+      t[r][hl * 4 + 0] = v[it].x;
+      t[r][hl * 4 + 1] = v[it].y;
+      t[r][hl * 4 + 2] = v[it].z;
+      t[r][hl * 4 + 3] = v[it].w;
+      if constexpr (LOWT != 0) {
+        const int64_t gr = row0 + r;
+        if (gr < rows && c < ldl) {
+          if constexpr (LOWT == 1) {
+            const __half2 a = __floats2half2_rn(v[it].x, v[it].y), b = __floats2half2_rn(v[it].z, v[it].w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&a);
+            w.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(static_cast<__half*>(low) + gr * ldl + c) = w;
+          } else if constexpr (LOWT == 2) {
+            const __nv_bfloat162 a = __floats2bfloat162_rn(v[it].x, v[it].y);
+            const __nv_bfloat162 b = __floats2bfloat162_rn(v[it].z, v[it].w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&a);
+            w.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(low) + gr * ldl + c) = w;
+          } else {
+            uint4 w;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(w.x) : "f"(v[it].x));
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(w.y) : "f"(v[it].y));
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(w.z) : "f"(v[it].z));
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(w.w) : "f"(v[it].w));
+            *reinterpret_cast<uint4*>(static_cast<uint32_t*>(low) + gr * ldl + c) = w;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    const int cend = min(64, dim - c0);
+    for (int k = 0; k < cend; ++k) {
+      const float x = t[lane][k];
+      if constexpr (NORM == NM_LOW_F16) {
+        const float h = round_f16(x);
+        acc = __fmaf_rn(h, h, acc);
+      } else if constexpr (NORM == NM_LOW_BF16) {
+        const float h = round_bf16(x);
+        acc = __fmaf_rn(h, h, acc);
+      } else if constexpr (NORM == NM_F32_FMA) {
+        acc = __fmaf_rn(x, x, acc);
+      } else {
+        acc = __fadd_rn(acc, __fmul_rn(x, x));
+      }
+    }
+    __syncwarp();
+  }
+  const int64_t my_row = row0 + lane;
+  if (my_row < rows) {
+    if constexpr (NORM == NM_LOW_F16)
+      norms[my_row] = round_f16(acc);
+    else if constexpr (NORM == NM_LOW_BF16)
+      norms[my_row] = round_bf16(acc);
+    else
+      norms[my_row] = acc;
+  }
+}
+
 template <typename TIN, int NORM, int LOWT>
 static cudaError_t go(const void* X, int64_t rows, int dim, void* low, int ldl, void* norms, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const int64_t blocks = (rows + 127) / 128;
+  if constexpr (std::is_same<TIN, float>::value && NORM != NM_F64_FMA) {
+    // the vector kernel's low stores need 8 (fp16/bf16) or 16 (tf32) byte aligned rows
+    const bool vec_ok = (dim % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
+                        (LOWT == 0 || ((reinterpret_cast<uintptr_t>(low) % 16 == 0) && ldl % 4 == 0));
+    if (vec_ok) {
+      prep_rows_v4_kernel<NORM, LOWT><<<static_cast<unsigned>(blocks), 128, 0, st>>>(
+          static_cast<const float*>(X), rows, dim, low, ldl, static_cast<float*>(norms));
+      return cudaGetLastError();
+    }
+  }
   prep_rows_kernel<TIN, NORM, LOWT><<<static_cast<unsigned>(blocks), 128, 0, st>>>(
       static_cast<const TIN*>(X), rows, dim, low, ldl, norms);
   return cudaGetLastError();

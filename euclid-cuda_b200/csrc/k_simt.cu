@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(256) simt_dist_kernel(const SimtArgs a) {
             if (pos < a.cap) {
               a.list[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(j);
             } else if constexpr (MODE == SM_ARGMIN_KEY) {
-              const float dd = static_cast<float>(direct_dist<TIN, REC>(P + i * a.dim, C + j * a.dim, a.dim));
+              const float dd = static_cast<float>(direct_dist_scalar<TIN, REC>(P + i * a.dim, C + j * a.dim, a.dim));
               const unsigned long long key = make_key(dd, static_cast<uint32_t>(j));
               bkey[r] = key < bkey[r] ? key : bkey[r];
             }

@@ -69,16 +69,6 @@ struct TcArgs {
   const float* C;
 };
 
-// The reference's distance for one accumulator value: S rounded to the GEMM's
-// output precision, then max((pp - 2 s) + cc, 0) (form_mixed_and_list_*,
-// euclidean_kernels_mix.cu:203-204).
-template <int SROUND>
-__device__ __forceinline__ float exact_d(float s, float pp, float cc) {
-  if constexpr (SROUND == SR_F16) s = round_f16(s);
-  if constexpr (SROUND == SR_BF16) s = round_bf16(s);
-  return fmaxf(__fadd_rn(__fmaf_rn(-2.f, s, pp), cc), 0.f);
-}
-
 template <int KIND, int SROUND, int FLAG, int MODE, int REC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     dist_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -400,7 +390,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     a.list[pos] = (static_cast<unsigned long long>(i) << 32) | jo;
                   } else if constexpr (ARGMIN) {
                     // list full: recompute in place and fold into the row minimum
-                    const float dd = static_cast<float>(direct_dist<float, REC>(a.P + i * a.dim,
+                    const float dd = static_cast<float>(direct_dist_scalar<float, REC>(a.P + i * a.dim,
                                                                                a.C + static_cast<int64_t>(jo) * a.dim,
                                                                                a.dim));
                     if (dd < bestv || (dd == bestv && jo < besti)) { bestv = dd; besti = jo; }
@@ -521,7 +511,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // Row-major [rows x ld] matrix of `esize`-byte elements, box = 128 bytes x box_rows.
-static bool make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows,
+bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows,
                       bool is_f32, bool is_bf16) {
   auto enc = get_encode();
   if (!enc) return false;
@@ -616,8 +606,8 @@ cudaError_t launch_tc(const DistJob& j) {
   a.C = static_cast<const float*>(j.C);
 
   CUtensorMap ta, tb;
-  if (!make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TC_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tb, j.fast_argmin ? j.Clow_sorted : j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1))
+  if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TC_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (!tc_make_tmap(&tb, j.fast_argmin ? j.Clow_sorted : j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
 
   const bool argmin = (j.D == nullptr);

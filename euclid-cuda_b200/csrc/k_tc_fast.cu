@@ -1,0 +1,750 @@
+// Fused distance + argmin on the tensor cores, screening form (sm_100a).
+//
+// TMA -> 128B-swizzled smem -> tcgen05.mma -> TMEM, with an epilogue reduced to what
+// an argmin needs, so that it keeps pace with the tensor cores:
+//
+//  * a CTA owns 256 rows at a time (two M=128 accumulators that share each 128-center
+//    B tile, which halves the B traffic per MMA against 128-row tiles); the A rows stay
+//    resident in shared memory while the center tiles stream past;
+//  * TMEM holds four 128-column accumulators (row half h, tile parity b); each belongs
+//    to one group of 4 epilogue warps (one per TMEM lane quadrant), so a group has two
+//    tile times to drain its accumulator while the MMAs of the next tile proceed;
+//  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
+//    each center tile's norms and original indices into shared memory ahead of use;
+//  * per 32-column chunk an epilogue warp forms keys x' = cc + bias - 2 s (one FMA),
+//    replaces the low 5 mantissa bits with the column (one LOP3) and takes the minimum
+//    with a depth-4 tree of 3-way mins;
+//  * a chunk in which some pair could meet the cancellation test
+//        d <= K (pp + cc)  <=>  2 s >= (1 - K)(pp + cc)  (up to rounding margins)
+//    -- bounded with the chunk's smallest and largest norm, tight because norms are
+//    sorted -- is not resolved here: its (row, chunk) and its 32 fp32 accumulators are
+//    appended to a list that eval_chunks_kernel evaluates with the operator's exact
+//    arithmetic (the same rounded S, distance formula and cancellation test as the
+//    exact epilogue; flagged pairs go to the direct-recompute list);
+//  * every other chunk can hold no flagged pair and contributes its key minimum.
+//
+// Labels equal the exact epilogue's wherever the row's top-two distance gap exceeds
+// the screen's resolution (2^-10 (pp + max cc) for fp16 S, 2^-7 for bf16 S).  If the
+// candidate list is full, the row is marked for a complete exact redo.
+//
+// All waits are bounded (common.cuh); on expiry the CTA records an error, drains its
+// copies and MMAs, frees TMEM and returns.
+#include "common.cuh"
+#include "engine.h"
+#include "direct.cuh"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+
+namespace euc {
+
+static __device__ int s_tf_err;
+
+// A CTA tile is 256 rows (two M=128 accumulator halves h = 0, 1, sharing every B tile)
+// by 128 centers; TMEM holds 4 accumulators of 128 columns: (half h, tile parity b).
+constexpr int TF_BM = 256;
+constexpr int TF_BN = 128;
+constexpr int TF_EPI_WARPS = 16;  // 4 groups (h, b) x 4 TMEM lane quadrants
+constexpr int TF_THREADS = (2 + TF_EPI_WARPS) * 32;
+constexpr int TF_KB_BYTES = 128 * 128;  // one 128-row x 128-byte K block (A half or B tile)
+constexpr int TF_SLOTS = 4;             // center-metadata ring
+constexpr int TF_META_BYTES = TF_BN * 8;
+constexpr int TF_BAR_BYTES = 512;
+constexpr int TF_EPI_BYTES = TF_EPI_WARPS * TF_BN * 4 + TF_BM * 8;  // per-warp biased norms + row merge
+
+struct TfArgs {
+  int64_t n, m;
+  int kblocks, nst, a_res, n_ct;
+  int64_t n_rt;
+  const float* pp;
+  const float* ccs;   // norms, sorted, padded to whole 256-center tiles
+  const int* perm;    // sorted position -> original index, padded
+  float omk, margin, ovf;
+  unsigned long long* row_key;
+  unsigned long long* list;     // candidate chunks: region r = list + r * region_cap
+  float* sbuf;                  // their 32 accumulator values, same index
+  unsigned long long region_cap;
+  uint32_t* region_cnt;
+  uint8_t* redo;
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(TF_THREADS, 1)
+    dist_tc_fast_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const TfArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NST = a.nst;
+  const bool a_res = a.a_res != 0;
+  const int KB = a.kblocks;
+  const uint32_t a_bytes = static_cast<uint32_t>(2 * KB) * TF_KB_BYTES;   // both halves, all K blocks
+  const uint32_t stage_bytes = a_res ? TF_KB_BYTES : 3u * TF_KB_BYTES;    // B  |  A0 A1 B
+  uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
+  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x (128 norms, 128 indices)
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + TF_SLOTS * TF_META_BYTES);
+  uint64_t* empty = full + NST;
+  uint64_t* afull = empty + NST;
+  uint64_t* aempty = afull + 2;
+  uint64_t* accf = aempty + 2;   // per tile parity: both halves' accumulators are complete
+  uint64_t* acce = accf + 2;     // per tile parity: both halves' accumulators were read
+  uint64_t* metaf = acce + 2;
+  uint64_t* metae = metaf + TF_SLOTS;
+  uint64_t* drain = metae + TF_SLOTS;
+  uint64_t* mfull = drain + 1;   // row merge: parity-1 groups have published their row minima
+  uint64_t* mdone = mfull + 1;   // row merge: parity-0 groups have consumed them
+  unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lcount + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + TF_BAR_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kCols = 4 * TF_BN;  // 512
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+      mbar_init(&accf[s], 1);
+      mbar_init(&acce[s], TF_EPI_WARPS / 2);
+    }
+    for (int s = 0; s < TF_SLOTS; ++s) {
+      mbar_init(&metaf[s], 1);
+      mbar_init(&metae[s], TF_EPI_WARPS / 2);
+    }
+    mbar_init(drain, 1);
+    mbar_init(mfull, TF_EPI_WARPS / 2);
+    mbar_init(mdone, TF_EPI_WARPS / 2);
+    *lcount = 0;
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, rt_i = 0, t = 0;
+      uint32_t issued_mask = 0, last_phase = 0, a_issued = 0, a_last = 0, m_issued = 0, m_last = 0;
+      bool ok = true;
+      const int kelems = (KIND == 2) ? 32 : 64;
+      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+        const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
+        const int row0 = static_cast<int>(rt * TF_BM);
+        if (a_res) {
+          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&afull[abuf], a_bytes);
+          uint8_t* sA = smem + abuf * a_bytes;
+          for (int h = 0; h < 2; ++h)
+            for (int kb = 0; kb < KB; ++kb)
+              tma_load_2d(sA + (h * KB + kb) * TF_KB_BYTES, &tmA, &afull[abuf], kb * kelems, row0 + h * 128);
+          a_issued |= 1u << abuf;
+          a_last = (a_last & ~(1u << abuf)) | (ause << abuf);
+        }
+        for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
+          const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
+          if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag)) { ok = false; break; }
+          uint8_t* ms = meta + slot * TF_META_BYTES;
+          mbar_arrive_expect_tx(&metaf[slot], TF_META_BYTES);
+          bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
+          bulk_load_1d(ms + TF_BN * 4, a.perm + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
+          m_issued |= 1u << slot;
+          m_last = (m_last & ~(1u << slot)) | (su << slot);
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+            uint8_t* st = stage_base + stage * stage_bytes;
+            mbar_arrive_expect_tx(&full[stage], stage_bytes);
+            if (a_res) {
+              tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+            } else {
+              tma_load_2d(st, &tmA, &full[stage], kb * kelems, row0);
+              tma_load_2d(st + TF_KB_BYTES, &tmA, &full[stage], kb * kelems, row0 + 128);
+              tma_load_2d(st + 2 * TF_KB_BYTES, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+            }
+            issued_mask |= 1u << stage;
+            last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(&s_tf_err, DEV_TIMEOUT_PRODUCER);
+      }
+      volatile int no_abort = 0;
+      for (int s = 0; s < NST; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_phase >> s) & 1u, &no_abort);
+      for (int s = 0; s < 2; ++s)
+        if (a_issued & (1u << s)) mbar_wait(&afull[s], (a_last >> s) & 1u, &no_abort);
+      for (int s = 0; s < TF_SLOTS; ++s)
+        if (m_issued & (1u << s)) mbar_wait(&metaf[s], (m_last >> s) & 1u, &no_abort);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
+      constexpr uint32_t idesc = umma_idesc(fmt, 128, TF_BN);
+      uint32_t stage = 0, phase = 0, t = 0, rt_i = 0;
+      bool ok = true;
+      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+        const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
+        const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
+        if (a_res) {
+          if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
+        }
+        for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
+          const uint32_t b = t & 1u, use = (t >> 1) & 1u;
+          if (!mbar_wait(&acce[b], use ^ 1u, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
+            const uint32_t sB = a_res ? st : st + 2 * TF_KB_BYTES;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t sA = a_res ? sAres + (h * KB + kb) * TF_KB_BYTES : st + h * TF_KB_BYTES;
+              const uint32_t d_tmem = tmem_base + (2 * b + h) * TF_BN;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
+                const uint64_t bd = sw128_kmajor_desc(sB + kk * 32);
+                if constexpr (KIND == 2)
+                  umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+                else
+                  umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+              }
+            }
+            umma_commit(&empty[stage]);
+            if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          umma_commit(&accf[b]);
+        }
+        if (a_res && ok) umma_commit(&aempty[abuf]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(&s_tf_err, DEV_TIMEOUT_MMA);
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;            // 0..15
+    const int q = warp & 3;             // TMEM lane quadrant
+    const int g = ew >> 2;              // group: row half h = g & 1, tile parity b = g >> 1
+    const int h = g & 1;
+    const uint32_t b = static_cast<uint32_t>(g >> 1);
+    const int row_local = h * 128 + q * 32 + lane;
+    const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (2 * b + h) * TF_BN;
+    float* ccb_w = epi + ew * TF_BN;                           // this warp's tile columns: norm + bias
+    float* mv = epi + TF_EPI_WARPS * TF_BN;                    // row merge: [256] minima
+    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + TF_BM);    //            [256] their columns
+    unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
+    float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
+    uint32_t rt_i = 0, t = 0, uses = 0;
+    bool ok = true;
+    for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+      const int64_t i = rt * TF_BM + row_local;
+      const bool row_ok = i < a.n;
+      const float pp = row_ok ? __ldg(a.pp + i) : 0.f;
+      // warp-uniform bias making every key non-negative: x' = cc - 2 s + bias >= 0
+      const float ppf = (row_ok && pp < 3.0e38f) ? pp : 0.f;
+      const float bias = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ppf))) * 1.0625f + 1e-30f;
+      float bestv = __int_as_float(0x7f800000);
+      uint32_t besti = 0xffffffffu;
+      for (int ct = 0; ct < a.n_ct; ++ct, ++t) {
+        if ((t & 1u) != b) continue;  // the other parity's groups take this tile
+        const uint32_t use = uses & 1u;
+        ++uses;
+        const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
+        const int64_t jt = static_cast<int64_t>(ct) * TF_BN;  // first (sorted) column of the tile
+        if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
+        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES);
+        const int* mperm = reinterpret_cast<const int*>(meta + slot * TF_META_BYTES + TF_BN * 4);
+#pragma unroll
+        for (int c = lane; c < TF_BN; c += 32) ccb_w[c] = (jt + c < a.m) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
+        __syncwarp();
+        const int64_t remt = a.m - jt;
+        const int nvt = remt >= TF_BN ? TF_BN : static_cast<int>(remt);
+        const float ccmax_t = mcc[nvt - 1];
+        const bool lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+
+        auto chunk = [&](int ch, const float (&v)[32]) {
+          const int c0 = ch * 32;
+          const int64_t j0 = jt + c0;
+          const int64_t remc = a.m - j0;
+          const int nvalid = remc <= 0 ? 0 : (remc >= 32 ? 32 : static_cast<int>(remc));
+          float kk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
+            kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
+          }
+          float tt[11];
+#pragma unroll
+          for (int u = 0; u < 10; ++u) tt[u] = fmin3(kk[3 * u], kk[3 * u + 1], kk[3 * u + 2]);
+          tt[10] = fminf(kk[30], kk[31]);
+          const float km = fmin3(fmin3(tt[0], tt[1], tt[2]), fmin3(tt[3], tt[4], tt[5]),
+                                 fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
+          bool cand = false;
+          if (nvalid > 0 && row_ok) {
+            const float ccmin = mcc[c0], ccbmax = ccb_w[c0 + nvalid - 1];
+            const float thr = ccbmax - a.omk * (pp + ccmin) + (pp + ccbmax) * a.margin;
+            cand = lane_exact || km <= thr;
+            if (!cand) {
+              const uint32_t kb = __float_as_uint(km);
+              const float dv = __fadd_rn(__uint_as_float(kb & ~31u) - bias, pp);
+              if (dv < bestv) {
+                bestv = fmaxf(dv, 0.f);
+                besti = static_cast<uint32_t>(mperm[c0 + (kb & 31u)]);
+              }
+            }
+          }
+          // some pair of a candidate chunk may be flagged: the chunk and its accumulators
+          // go to this CTA's list region (warp-aggregated) for the exact second pass
+          const unsigned bal = __ballot_sync(0xffffffffu, cand);
+          if (bal) {
+            const int leader = __ffs(bal) - 1;
+            unsigned long long base = 0;
+            if (lane == leader) base = atomicAdd(lcount, static_cast<unsigned long long>(__popc(bal)));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (cand) {
+              const unsigned long long pos = base + __popc(bal & ((1u << lane) - 1u));
+              if (pos < a.region_cap) {
+                region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(j0);
+                float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+              } else {
+                a.redo[i] = 1;
+              }
+            }
+          }
+        };
+
+#pragma unroll 1
+        for (int ch = 0; ch < TF_BN / 32; ++ch) {
+          float va[32];
+          tmem_ld32(tmem_acc + ch * 32, va);
+          chunk(ch, va);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&acce[b]);
+          mbar_arrive(&metae[slot]);
+        }
+      }
+      if (!ok) break;
+      // merge the two tile parities of each row
+      const uint32_t par = rt_i & 1u;
+      if (b == 1) {
+        if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag)) { ok = false; break; }
+        mv[row_local] = bestv;
+        mi[row_local] = besti;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(mfull);
+      } else {
+        if (!mbar_wait(mfull, par, abort_flag)) { ok = false; break; }
+        const float ov = mv[row_local];
+        const uint32_t oi = mi[row_local];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(mdone);
+        if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
+        if (row_ok) a.row_key[i] = make_key(bestv, besti);
+      }
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      if (lane == 0) atomicExch(&s_tf_err, DEV_TIMEOUT_EPILOGUE);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    const unsigned long long c = *lcount;
+    a.region_cnt[blockIdx.x] = static_cast<uint32_t>(c < a.region_cap ? c : a.region_cap);
+  }
+  if (warp == 1) tmem_dealloc(tmem_base, kCols);
+}
+
+// ------------------------------------------------------------------ host side
+
+constexpr size_t TF_SMEM_LIMIT = 232448;
+constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
+
+// Resident A (two 256-row tiles, double-buffered) with B-only stages when that leaves
+// room for 3 stages, else streaming (A0 A1 B) stages.
+static void tf_pipeline(int kblocks, int* nst, int* a_res) {
+  const size_t abytes = static_cast<size_t>(2 * kblocks) * TF_KB_BYTES;
+  const size_t avail = TF_SMEM_LIMIT - TF_FIXED;
+  if (2 * abytes + 3 * TF_KB_BYTES <= avail) {
+    *a_res = 1;
+    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / TF_KB_BYTES));
+  } else {
+    *a_res = 0;
+    *nst = static_cast<int>(std::min<size_t>(8, avail / (3 * TF_KB_BYTES)));
+  }
+}
+
+static size_t tf_smem_bytes(int kblocks, int nst, int a_res) {
+  const size_t body = a_res ? 4 * static_cast<size_t>(kblocks) * TF_KB_BYTES + nst * TF_KB_BYTES
+                            : nst * 3 * static_cast<size_t>(TF_KB_BYTES);
+  return TF_FIXED + body;
+}
+
+int tc_fast_regions(int64_t n) {
+  const int64_t n_rt = (n + TF_BM - 1) / TF_BM;
+  int grid = num_sms();
+  if (static_cast<int64_t>(grid) > n_rt) grid = static_cast<int>(n_rt);
+  return grid < 1 ? 1 : grid;
+}
+
+template <int KIND>
+static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const TfArgs& args, int grid,
+                               cudaStream_t st) {
+  auto kern = dist_tc_fast_kernel<KIND>;
+  const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  timing_begin(st, "dist_tc_fast_kernel");
+  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, args);
+  e = cudaGetLastError();
+  timing_end(st);
+  return e;
+}
+
+static int low_kind(const OpSpec* s) { return (s->gemm == G_TC_F16) ? 0 : (s->gemm == G_TC_BF16 ? 1 : 2); }
+
+cudaError_t launch_tc_fast(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  const int kind = low_kind(s);
+  const int esize = (kind == 2) ? 4 : 2;
+  if (j.n > 0x7fffffffll - TF_BM) return cudaErrorInvalidValue;  // TMA row coordinates are 32-bit
+  TfArgs a{};
+  a.n = j.n;
+  a.m = j.m;
+  a.kblocks = static_cast<int>((static_cast<int64_t>(j.ldlow) * esize) / 128);
+  a.n_ct = static_cast<int>((j.m + TF_BN - 1) / TF_BN);
+  a.n_rt = (j.n + TF_BM - 1) / TF_BM;
+  tf_pipeline(a.kblocks, &a.nst, &a.a_res);
+  if (a.nst < 2) return cudaErrorInvalidValue;
+  a.pp = static_cast<const float*>(j.pp);
+  a.ccs = j.cc_sorted;
+  a.perm = j.perm;
+  a.omk = 1.f - j.kf;
+  // screen margin: the rounding of S to the GEMM's output format dominates
+  a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-20f);
+  a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
+  a.row_key = j.row_key;
+  a.list = j.chunk_list;
+  a.sbuf = j.chunk_s;
+  a.region_cap = j.chunk_cap / static_cast<unsigned long long>(j.regions);
+  a.region_cnt = j.region_cnt;
+  a.redo = j.redo;
+  const int grid = j.regions;
+  if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, 128, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
+    return cudaErrorInvalidValue;
+  if (kind == 0) return launch_tf_t<0>(ta, tb, a, grid, j.stream);
+  if (kind == 1) return launch_tf_t<1>(ta, tb, a, grid, j.stream);
+  return launch_tf_t<2>(ta, tb, a, grid, j.stream);
+}
+
+int tf_error_and_clear() {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, s_tf_err, sizeof(int));
+  if (v) cudaMemcpyToSymbol(s_tf_err, &z, sizeof(int));
+  return v;
+}
+
+template <int KIND>
+__device__ __forceinline__ float low_dot(const uint4* __restrict__ p, const uint4* __restrict__ c, int nvec) {
+  float acc = 0.f;
+  for (int v = 0; v < nvec; ++v) {
+    const uint4 xv = __ldg(p + v), yv = __ldg(c + v);
+    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ys[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if constexpr (KIND == 2) {
+        acc = __fmaf_rn(__uint_as_float(xs[w]), __uint_as_float(ys[w]), acc);
+      } else {
+        float2 fx, fy;
+        if constexpr (KIND == 0) {
+          fx = __half22float2(*reinterpret_cast<const __half2*>(&xs[w]));
+          fy = __half22float2(*reinterpret_cast<const __half2*>(&ys[w]));
+        } else {
+          fx = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[w]));
+          fy = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ys[w]));
+        }
+        acc = __fmaf_rn(fx.x, fy.x, acc);
+        acc = __fmaf_rn(fx.y, fy.y, acc);
+      }
+    }
+  }
+  return acc;
+}
+
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long k) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
+    k = t < k ? t : k;
+  }
+  return k;
+}
+
+// ================================================================ second pass
+//
+// Candidate chunks, evaluated with the operator's exact arithmetic on the stored MMA
+// accumulators: s rounded to the GEMM's output format, d = max((pp - 2 s) + cc, 0),
+// flagged when d <= K (pp + cc) (euclidean_kernels_mix.cu:203-211), exactly as the
+// exact epilogue forms them.  One warp per chunk, one lane per column.  Unflagged
+// pairs fold into the row's 64-bit key with one atomicMin per chunk; flagged pairs are
+// counted and appended (warp-buffered) to the direct-recompute list, which
+// recompute_kernel then folds in.  If that list is full the pair is recomputed here.
+
+struct EvArgs {
+  const unsigned long long* clist;
+  const float* sbuf;
+  unsigned long long region_cap;
+  const uint32_t* region_cnt;
+  const float* pp;
+  const float* cc_s;
+  const int* perm;
+  int64_t n, m;
+  float K;
+  const uint8_t* redo;
+  unsigned long long* row_key;
+  unsigned long long* count;
+  unsigned long long* list;
+  unsigned long long cap;
+  const float* P;
+  const float* C;
+  int dim;
+};
+
+constexpr int EV_BLOCKS_PER_REGION = 8;
+constexpr int EV_WBUF = 256;  // flagged pairs buffered per warp before one list reservation
+
+template <int REC>
+__device__ __noinline__ void fold_direct(const float* P, const float* C, int dim, unsigned long long* row_key,
+                                         int64_t i, uint32_t jo) {
+  const float d = static_cast<float>(direct_dist_scalar<float, REC>(P + i * dim, C + static_cast<int64_t>(jo) * dim, dim));
+  atomicMin(&row_key[i], make_key(d, jo));
+}
+
+template <int REC>
+__device__ __forceinline__ void flush_pairs(const EvArgs& a, unsigned long long* wbuf, int& wcnt, int lane) {
+  unsigned long long base = 0;
+  if (lane == 0) base = atomicAdd(a.count, static_cast<unsigned long long>(wcnt));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  for (int q = lane; q < wcnt; q += 32) {
+    const unsigned long long e = wbuf[q];
+    if (base + q < a.cap)
+      a.list[base + q] = e;
+    else
+      fold_direct<REC>(a.P, a.C, a.dim, a.row_key, static_cast<int64_t>(e >> 32),
+                       static_cast<uint32_t>(e & 0xffffffffull));
+  }
+  __syncwarp();
+  wcnt = 0;
+}
+
+template <int SROUND, int REC>
+__global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
+  __shared__ unsigned long long s_buf[8][EV_WBUF];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  unsigned long long* wbuf = s_buf[wib];
+  int wcnt = 0;
+  const int r = blockIdx.x / EV_BLOCKS_PER_REGION;
+  const unsigned wr = (blockIdx.x % EV_BLOCKS_PER_REGION) * 8 + wib;
+  constexpr unsigned kStride = EV_BLOCKS_PER_REGION * 8;
+  unsigned long long cnt = a.region_cnt[r];
+  if (cnt > a.region_cap) cnt = a.region_cap;
+  const unsigned long long rbase = static_cast<unsigned long long>(r) * a.region_cap;
+  for (unsigned long long t = wr; t < cnt; t += kStride) {
+    const unsigned long long e = a.clist[rbase + t];
+    const float s = a.sbuf[(rbase + t) * 32 + lane];
+    const int64_t i = static_cast<int64_t>(e >> 32);
+    const int64_t j = static_cast<int64_t>(e & 0xffffffffull) + lane;
+    if (i >= a.n || a.redo[i]) continue;  // warp-uniform; redo rows are evaluated whole
+    unsigned long long key = ~0ull;
+    bool fl = false;
+    uint32_t jo = 0;
+    if (j < a.m) {
+      const float pp = __ldg(a.pp + i), cc = __ldg(a.cc_s + j);
+      jo = static_cast<uint32_t>(__ldg(a.perm + j));
+      const float d = exact_d<SROUND>(s, pp, cc);
+      fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
+      if (!fl) key = make_key(d, jo);
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, fl);
+    if (bal) {
+      if (fl) wbuf[wcnt + __popc(bal & ((1u << lane) - 1u))] = (static_cast<unsigned long long>(i) << 32) | jo;
+      wcnt += __popc(bal);
+      __syncwarp();
+      if (wcnt > EV_WBUF - 32) flush_pairs<REC>(a, wbuf, wcnt, lane);
+    }
+    key = warp_min_u64(key);
+    if (lane == 0 && key != ~0ull) atomicMin(&a.row_key[i], key);
+  }
+  if (wcnt > 0) flush_pairs<REC>(a, wbuf, wcnt, lane);
+}
+
+// Rows whose candidates overflowed their region: every pair evaluated exactly, with
+// s summed in fp32 (sequential fused multiply-adds) over the rounded operands the MMA
+// consumed; flagged pairs take the direct distance here.
+
+struct RdArgs {
+  const void* Plow;
+  const void* Clow;   // original order
+  int nvec;           // 16-byte vectors per low row
+  const float* P;
+  const float* C;
+  int dim;
+  const float* pp;
+  const float* cc;
+  int64_t n, m;
+  float K;
+  const uint8_t* redo;
+  unsigned long long* row_key;
+  unsigned long long* count;
+};
+
+template <int KIND, int SROUND, int REC>
+__global__ void __launch_bounds__(256) redo_rows_kernel(const RdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  unsigned long long nfl = 0;
+  for (int64_t base = gw * 32; base < a.n; base += nw * 32) {
+    const int64_t ii = base + lane;
+    unsigned bal = __ballot_sync(0xffffffffu, ii < a.n && a.redo[ii] != 0);
+    while (bal) {
+      const int64_t i = base + (__ffs(bal) - 1);
+      bal &= bal - 1;
+      unsigned long long best = ~0ull;
+      const float pp = __ldg(a.pp + i);
+      for (int64_t j0 = 0; j0 < a.m; j0 += 32) {
+        const int64_t j = j0 + lane;
+        bool fl = false;
+        if (j < a.m) {
+          const float sv = low_dot<KIND>(static_cast<const uint4*>(a.Plow) + i * a.nvec,
+                                         static_cast<const uint4*>(a.Clow) + j * a.nvec, a.nvec);
+          const float cc = __ldg(a.cc + j);
+          float d = exact_d<SROUND>(sv, pp, cc);
+          fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
+          if (fl) d = static_cast<float>(direct_dist_scalar<float, REC>(a.P + i * a.dim, a.C + j * a.dim, a.dim));
+          const unsigned long long k = make_key(d, static_cast<uint32_t>(j));
+          best = k < best ? k : best;
+        }
+        nfl += __popc(__ballot_sync(0xffffffffu, fl));
+      }
+      best = warp_min_u64(best);
+      if (lane == 0) a.row_key[i] = best;
+    }
+  }
+  if (lane == 0 && nfl) atomicAdd(a.count, nfl);
+}
+
+#define FAST_REC_CASES(X)     \
+  X(0, SR_F16, RC_F64)        \
+  X(0, SR_F16, RC_F32)        \
+  X(0, SR_F16, RC_F16_ARITH)  \
+  X(0, SR_NONE, RC_F64)       \
+  X(0, SR_NONE, RC_F32)       \
+  X(1, SR_BF16, RC_F64)       \
+  X(1, SR_BF16, RC_F32)       \
+  X(1, SR_BF16, RC_BF16_ARITH)\
+  X(1, SR_NONE, RC_F64)       \
+  X(1, SR_NONE, RC_F32)       \
+  X(2, SR_NONE, RC_F64)
+
+cudaError_t launch_eval_chunks(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  const int kind = low_kind(s);
+  EvArgs a{};
+  a.clist = j.chunk_list;
+  a.sbuf = j.chunk_s;
+  a.region_cap = j.chunk_cap / static_cast<unsigned long long>(j.regions);
+  a.region_cnt = j.region_cnt;
+  a.pp = static_cast<const float*>(j.pp);
+  a.cc_s = j.cc_sorted;
+  a.perm = j.perm;
+  a.n = j.n;
+  a.m = j.m;
+  a.K = j.kf;
+  a.redo = j.redo;
+  a.row_key = j.row_key;
+  a.count = j.count;
+  a.list = j.list;
+  a.cap = j.list_cap;
+  a.P = static_cast<const float*>(j.P);
+  a.C = static_cast<const float*>(j.C);
+  a.dim = j.dim;
+  const unsigned grid = static_cast<unsigned>(j.regions * EV_BLOCKS_PER_REGION);
+#define EV_CASE(KIND_, SR_, REC_)                                         \
+  if (kind == KIND_ && s->sround == SR_ && s->rec == REC_) {              \
+    eval_chunks_kernel<SR_, REC_><<<grid, 256, 0, j.stream>>>(a);         \
+    return cudaGetLastError();                                            \
+  }
+  FAST_REC_CASES(EV_CASE)
+#undef EV_CASE
+  return cudaErrorNotSupported;
+}
+
+cudaError_t launch_redo_rows(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  const int kind = low_kind(s);
+  const int esize = (kind == 2) ? 4 : 2;
+  RdArgs a{};
+  a.Plow = j.Plow;
+  a.Clow = j.Clow;
+  a.nvec = static_cast<int>(static_cast<int64_t>(j.ldlow) * esize / 16);
+  a.P = static_cast<const float*>(j.P);
+  a.C = static_cast<const float*>(j.C);
+  a.dim = j.dim;
+  a.pp = static_cast<const float*>(j.pp);
+  a.cc = static_cast<const float*>(j.cc);
+  a.n = j.n;
+  a.m = j.m;
+  a.K = j.kf;
+  a.redo = j.redo;
+  a.row_key = j.row_key;
+  a.count = j.count;
+  const int64_t warps = (j.n + 31) / 32;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((warps + 7) / 8, static_cast<int64_t>(num_sms()) * 8));
+#define RD_CASE(KIND_, SR_, REC_)                                             \
+  if (kind == KIND_ && s->sround == SR_ && s->rec == REC_) {                  \
+    redo_rows_kernel<KIND_, SR_, REC_><<<blocks, 256, 0, j.stream>>>(a);      \
+    return cudaGetLastError();                                                \
+  }
+  FAST_REC_CASES(RD_CASE)
+#undef RD_CASE
+  return cudaErrorNotSupported;
+}
+
+}  // namespace euc

@@ -66,10 +66,14 @@ def test_host_queries(lib):
     assert lib.euc_workspace_bytes(999, n, m, d) == 0
     lib.euc_argmin_workspace_bytes.restype = ctypes.c_size_t
     lib.euc_argmin_workspace_bytes.argtypes = lib.euc_workspace_bytes.argtypes
-    # the fused argmin adds the norm-sorted centers (copy, norms, original index) and a
-    # 64-bit row key per point
+    # the fused argmin adds the norm-sorted centers (copy, and norms and original index
+    # padded to 256-center tiles), per-CTA list counts, a redo byte per point, the
+    # candidate-chunk list and a 64-bit row key per point
     al = lambda b: (b + 255) // 256 * 256
-    assert lib.euc_argmin_workspace_bytes(10, n, m, d) == ws + al(m * 128 * 2) + 2 * al(m * 4) + al(n * 8)
+    mpad = (m + 255) // 256 * 256
+    ccap = min(n * ((m + 31) // 32), max(2 * n, 1 << 16))  # candidate chunks: entry + 32 fp32 accumulators
+    assert lib.euc_argmin_workspace_bytes(10, n, m, d) == (ws + al(m * 128 * 2) + 2 * al(mpad * 4) + al(1024 * 4)
+                                                           + al(n) + al(ccap * 8) + al(ccap * 128) + al(n * 8))
 
 
 def test_compute_entry_rejects_missing_device(lib):

@@ -126,7 +126,7 @@ def test_argmin_matches_engine_D():
         torch.testing.assert_close(lab, D.argmin(1), rtol=0, atol=0)
         torch.testing.assert_close(md, D.min(1).values, rtol=0, atol=0)
         labf, mdf, c2 = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")(Pt, Ct, kappa)
-        assert int(c1.item()) == int(c2.item())
+        assert int(c1.item()) == int(c2.item())  # same accumulators, same cancellation test
         u = 2.0 ** -7 if op.startswith("bf16") else 2.0 ** -10
         nrm = O.norms_f32(P, O.MIX[op][2]).astype(np.float64)
         bound = torch.from_numpy(u * (nrm + O.norms_f32(C, O.MIX[op][2]).max())).to(DEV)
@@ -178,6 +178,28 @@ def test_flag_list_overflow():
         np.testing.assert_array_equal(lab.cpu().numpy(), O.argmin_first(Do))
         np.testing.assert_array_equal(md.cpu().numpy(), Do.min(1))
         assert int(c.item()) == cnt_o
+    device_check()
+
+
+def test_fast_argmin_region_overflow_redo():
+    """Cancellation-heavy input (every pair flagged, every chunk a candidate): the fast
+    path's candidate list overflows its per-CTA regions and the overflowing rows are
+    evaluated whole by the redo pass.  All distances are then direct fp32 values, so
+    labels, minima and counts equal the exact path's and the oracle's."""
+    rng = np.random.default_rng(5)
+    n, m, d = 4096, 2048, 64
+    C = (1000.0 + rng.normal(0, 0.1, (m, d))).astype(np.float32)
+    P = (C[rng.integers(0, m, n)] + rng.normal(0, 0.01, (n, d))).astype(np.float32)
+    Pt, Ct = cuda(P), cuda(C)
+    fn = euclidean_cuda_mix.pairwise_euclidean_fp16_fp32_argmin
+    le, me, ce = fn(Pt, Ct, 5.0, exact=True)
+    lf, mf, cf = fn(Pt, Ct, 5.0)
+    assert int(ce.item()) == n * m and int(cf.item()) == n * m
+    torch.testing.assert_close(lf, le, rtol=0, atol=0)
+    torch.testing.assert_close(mf, me, rtol=0, atol=0)
+    Do, _, cnt_o = O.mix("fp16_fp32", P, C, 5.0)
+    assert cnt_o == n * m
+    np.testing.assert_array_equal(lf.cpu().numpy(), O.argmin_first(Do))
     device_check()
 
 
