@@ -132,6 +132,20 @@ def cpu_baseline(k, d, seconds=10.0, rows=4096, seed=1):
     return flops / el / 1e9, used, f"{reps} x {rows} rows x {k} centers x {d} dims, fp64 ({el:.1f} s)"
 
 
+def count_launches(step, torch):
+    """Kernels of this library (namespace euc::) that one step launches, counted from the
+    CUDA activity trace of one untimed step."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        return sum(1 for ev in prof.events() if ev.device_type.name == "CUDA" and "euc::" in ev.name)
+    except Exception:
+        return None
+
+
 def run_reference(a):
     """--impl reference: the reference path's CPU implementation (the oracle port; the
     reference itself is CUDA-only) on the host cores, rank 0 only."""
@@ -258,7 +272,6 @@ def main():
         def step():
             check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, 0, None, ptr(labels), None, ptr(cnt),
                                ptr(ws), ws.numel(), sp))
-        launches_per_step = 5  # prep P, prep C, dist_tc_kernel, recompute, labels
         work_units = 2.0 * n_local * k * d * world  # flop per step, all ranks
     else:
         from kmeans import LloydKMeans
@@ -267,12 +280,12 @@ def main():
 
         def step():
             state["C"], _, _ = km.step(X, state["C"])
-        launches_per_step = 5 + 6  # argmin chain + (memset-free) stats: hist, scan, scatter, segsum, finalize (+memsets)
         work_units = 1.0  # one iteration (of the whole job) per step
 
     for _ in range(a.warmup):
         step()
     barrier()
+    launches_per_step = count_launches(step, torch)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         e0.record(st)
@@ -335,7 +348,8 @@ def main():
                            "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
                            "parallelism": f"dp{world}"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-                "gpu_launches": launches_per_step * a.steps, "flagged_last_step": int(cnt.item())}
+                "gpu_launches": None if launches_per_step is None else launches_per_step * a.steps,
+                "launches_per_step": launches_per_step, "flagged_last_step": int(cnt.item())}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

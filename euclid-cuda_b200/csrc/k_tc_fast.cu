@@ -10,7 +10,7 @@
 //    to one group of 4 epilogue warps (one per TMEM lane quadrant), so a group has two
 //    tile times to drain its accumulator while the MMAs of the next tile proceed;
 //  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
-//    each center tile's norms and original indices into shared memory ahead of use;
+//    each center tile's norms into shared memory ahead of use;
 //  * per 32-column chunk an epilogue warp forms keys x' = cc + bias - 2 s (one FMA),
 //    replaces the low 5 mantissa bits with the column (one LOP3) and takes the minimum
 //    with a depth-4 tree of 3-way mins;
@@ -48,7 +48,7 @@ constexpr int TF_EPI_WARPS = 16;  // 4 groups (h, b) x 4 TMEM lane quadrants
 constexpr int TF_THREADS = (2 + TF_EPI_WARPS) * 32;
 constexpr int TF_KB_BYTES = 128 * 128;  // one 128-row x 128-byte K block (A half or B tile)
 constexpr int TF_SLOTS = 4;             // center-metadata ring
-constexpr int TF_META_BYTES = TF_BN * 8;
+constexpr int TF_META_BYTES = TF_BN * 4;  // the tile's sorted center norms
 constexpr int TF_BAR_BYTES = 512;
 constexpr int TF_EPI_BYTES = TF_EPI_WARPS * TF_BN * 4 + TF_BM * 8;  // per-warp biased norms + row merge
 
@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const uint32_t a_bytes = static_cast<uint32_t>(2 * KB) * TF_KB_BYTES;   // both halves, all K blocks
   const uint32_t stage_bytes = a_res ? TF_KB_BYTES : 3u * TF_KB_BYTES;    // B  |  A0 A1 B
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
-  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x (128 norms, 128 indices)
+  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 128 sorted norms
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + TF_SLOTS * TF_META_BYTES);
   uint64_t* empty = full + NST;
   uint64_t* afull = empty + NST;
@@ -158,8 +158,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* ms = meta + slot * TF_META_BYTES;
           mbar_arrive_expect_tx(&metaf[slot], TF_META_BYTES);
-          bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
-          bulk_load_1d(ms + TF_BN * 4, a.perm + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
+          bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_META_BYTES, &metaf[slot]);
           m_issued |= 1u << slot;
           m_last = (m_last & ~(1u << slot)) | (su << slot);
           for (int kb = 0; kb < KB; ++kb) {
@@ -257,6 +256,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     uint32_t* mi = reinterpret_cast<uint32_t*>(mv + TF_BM);    //            [256] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
+    // screen threshold of a chunk: thr = U_c + pp (margin - (1 - K)), with
+    // U_c = max(cc + bias) (1 + margin) - (1 - K) min cc over the chunk
+    const float kv = a.margin - a.omk;
     uint32_t rt_i = 0, t = 0, uses = 0;
     bool ok = true;
     for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
@@ -266,8 +268,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       // warp-uniform bias making every key non-negative: x' = cc - 2 s + bias >= 0
       const float ppf = (row_ok && pp < 3.0e38f) ? pp : 0.f;
       const float bias = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ppf))) * 1.0625f + 1e-30f;
-      float bestv = __int_as_float(0x7f800000);
-      uint32_t besti = 0xffffffffu;
+      const float vlane = pp * kv;
+      // best screened key of the row: x' with its column in the low 5 bits, and the
+      // first sorted column of its chunk
+      float best_x = __int_as_float(0x7f800000);
+      int64_t best_j = 0;
       for (int ct = 0; ct < a.n_ct; ++ct, ++t) {
         if ((t & 1u) != b) continue;  // the other parity's groups take this tile
         const uint32_t use = uses & 1u;
@@ -276,27 +281,40 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const int64_t jt = static_cast<int64_t>(ct) * TF_BN;  // first (sorted) column of the tile
         if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
         const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES);
-        const int* mperm = reinterpret_cast<const int*>(meta + slot * TF_META_BYTES + TF_BN * 4);
-#pragma unroll
-        for (int c = lane; c < TF_BN; c += 32) ccb_w[c] = (jt + c < a.m) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
-        __syncwarp();
         const int64_t remt = a.m - jt;
         const int nvt = remt >= TF_BN ? TF_BN : static_cast<int>(remt);
+#pragma unroll
+        for (int c = lane; c < TF_BN; c += 32) ccb_w[c] = (c < nvt) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
+        float u_own = 0.f;  // lane L < 4: U of chunk L
+        if (lane < 4 && lane * 32 < nvt) {
+          const int last = min(lane * 32 + 31, nvt - 1);
+          const float ccbmax = __fadd_rn(mcc[last], bias);
+          u_own = ccbmax * (1.f + a.margin) - a.omk * mcc[lane * 32];
+        }
         const float ccmax_t = mcc[nvt - 1];
-        const bool lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        const bool lane_exact = row_ok && !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        const int nch = (nvt + 31) >> 5;
+        __syncwarp();
         if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
 
-        auto chunk = [&](int ch, const float (&v)[32]) {
-          const int c0 = ch * 32;
-          const int64_t j0 = jt + c0;
-          const int64_t remc = a.m - j0;
-          const int nvalid = remc <= 0 ? 0 : (remc >= 32 ? 32 : static_cast<int>(remc));
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ++ch) {
+          float v[32];
+          tmem_ld32(tmem_acc + ch * 32, v);
+          const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vlane;
+          const float4* cb4 = reinterpret_cast<const float4*>(ccb_w + ch * 32);
           float kk[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
-            kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 cb = cb4[q4];
+            const float c4[4] = {cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const int e = q4 * 4 + r;
+              const float x = __fmaf_rn(-2.f, v[e], c4[r]);
+              kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
+            }
           }
           float tt[11];
 #pragma unroll
@@ -304,19 +322,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           tt[10] = fminf(kk[30], kk[31]);
           const float km = fmin3(fmin3(tt[0], tt[1], tt[2]), fmin3(tt[3], tt[4], tt[5]),
                                  fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
-          bool cand = false;
-          if (nvalid > 0 && row_ok) {
-            const float ccmin = mcc[c0], ccbmax = ccb_w[c0 + nvalid - 1];
-            const float thr = ccbmax - a.omk * (pp + ccmin) + (pp + ccbmax) * a.margin;
-            cand = lane_exact || km <= thr;
-            if (!cand) {
-              const uint32_t kb = __float_as_uint(km);
-              const float dv = __fadd_rn(__uint_as_float(kb & ~31u) - bias, pp);
-              if (dv < bestv) {
-                bestv = fmaxf(dv, 0.f);
-                besti = static_cast<uint32_t>(mperm[c0 + (kb & 31u)]);
-              }
-            }
+          const int64_t j0 = jt + ch * 32;
+          const bool cand = row_ok && (lane_exact || km <= thr);
+          if (!cand && km < best_x) {
+            best_x = km;
+            best_j = j0;
           }
           // some pair of a candidate chunk may be flagged: the chunk and its accumulators
           // go to this CTA's list region (warp-aggregated) for the exact second pass
@@ -338,13 +348,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
               }
             }
           }
-        };
-
-#pragma unroll 1
-        for (int ch = 0; ch < TF_BN / 32; ++ch) {
-          float va[32];
-          tmem_ld32(tmem_acc + ch * 32, va);
-          chunk(ch, va);
         }
         tc_fence_before();
         __syncwarp();
@@ -354,6 +357,14 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
       }
       if (!ok) break;
+      // this group's screened minimum of the row: distance and original center index
+      float bestv = __int_as_float(0x7f800000);
+      uint32_t besti = 0xffffffffu;
+      if (row_ok && best_x < __int_as_float(0x7f800000)) {
+        const uint32_t kb = __float_as_uint(best_x);
+        bestv = fmaxf(__fadd_rn(__uint_as_float(kb & ~31u) - bias, pp), 0.f);
+        besti = static_cast<uint32_t>(__ldg(a.perm + best_j + (kb & 31u)));
+      }
       // merge the two tile parities of each row
       const uint32_t par = rt_i & 1u;
       if (b == 1) {
@@ -454,7 +465,7 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.perm = j.perm;
   a.omk = 1.f - j.kf;
   // screen margin: the rounding of S to the GEMM's output format dominates
-  a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-20f);
+  a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-16f);
   a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
   a.row_key = j.row_key;
   a.list = j.chunk_list;
