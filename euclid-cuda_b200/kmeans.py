@@ -58,10 +58,15 @@ class LloydKMeans:
                                         ptr(prev), self.empty, stream_of(stats)))
         return out
 
+    def assign(self, X, C):
+        """Labels (int32) of the local rows and the flagged-pair count (0-d tensor)."""
+        labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, labels_dtype=torch.int32, min_dist=False)
+        return labels, cnt
+
     def step(self, X, C):
         """One iteration on the local shard X; returns (new centers, labels int32,
         flagged-pair count of this shard as a 0-d device tensor)."""
-        labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, labels_dtype=torch.int32, min_dist=False)
+        labels, cnt = self.assign(X, C)
         stats = self.center_stats(X, labels)
         if self._world() > 1:
             dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=self.group)

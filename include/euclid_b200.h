@@ -208,7 +208,7 @@ EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int6
 
 /* ============================================================ new entries
  * No counterpart in the reference: the k-means caller composes these instead of
- * materialising D (SURVEY hot path: distances -> argmin -> center update). */
+ * materialising D (the Lloyd hot path: distances -> argmin -> center update). */
 
 /* Fused distance + row argmin for distance operator `op` (an EUC_OP_MIX_*,
  * EUC_OP_TILED_*, EUC_OP_TC_*, EUC_OP_SINGLE or EUC_OP_DOUBLE id), without

@@ -2,8 +2,8 @@
 
 This is part of the oracle: it compiles the UNMODIFIED sources of
 inEXASCALE/euclid-cuda, where they lie in the read-only reference checkout,
-into ``oracle/_ref/`` (git-ignored, but shipped to the GPU box with the rest of
-the tree).  The resulting modules are used by ``tests/golden/make_golden.py`` to
+into ``oracle/_ref/`` (git-ignored, but copied along with the rest of the tree).
+The resulting modules are used by ``tests/golden/make_golden.py`` to
 produce golden vectors on a B200 and by the GPU parity tests to compare against
 the reference kernels directly.  Nothing in the product imports them.
 

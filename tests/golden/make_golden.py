@@ -7,7 +7,7 @@ seeded inputs and stores inputs + outputs as small .npz files next to it.  The
 CPU oracle is checked against these files (tests/test_oracle_golden.py) and the
 engine against both.
 
-Usage (GPU box):  python tests/golden/make_golden.py [--out tests/golden]
+Usage (on a B200):  python tests/golden/make_golden.py [--out tests/golden]
 
 Shapes avoid the reference's known hazards: N and M are multiples of 32 for the
 tiled kernels (a partial tile reaches a divergent __syncthreads,

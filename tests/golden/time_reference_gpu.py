@@ -1,5 +1,5 @@
 """Time the REFERENCE's own CUDA operators (built by oracle/build_ref.py) on the bench
-workloads, on one B200, for the comparison table in BASELINE.md.
+workloads, on one B200 (the comparison numbers for the engine's own measurements).
 
     python tests/golden/time_reference_gpu.py [--iters 5]
 

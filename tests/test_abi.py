@@ -30,7 +30,7 @@ def lib():
 
 def test_header_declares_the_reference_surface():
     names = declared()
-    # one entry per reference operator family member (SURVEY 8b): 2 base + 9 mix + 6 tiled +
+    # one entry per reference operator family member: 2 base + 9 mix + 6 tiled +
     # 4 tensorcore + 8 uniform + 4 advanced + 2 centers, plus counter reads and new entries
     for fam, n in (("euc_mix_", 9), ("euc_tiled_", 6), ("euc_tensorcore_", 4), ("euc_uniform_", 8),
                    ("euc_advanced_", 4), ("euc_update_centers_", 2), ("euc_pairwise_", 2)):
