@@ -195,6 +195,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--rows", type=int, default=None,
+                    help="override the workload's row count (smaller cases for profiler captures)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":
@@ -230,7 +232,9 @@ def main():
 
     L = lib()
     st = torch.cuda.current_stream(dev)
-    cfg = C2 if a.workload == "c2" else LLOYD
+    cfg = dict(C2 if a.workload == "c2" else LLOYD)
+    if a.rows:
+        cfg["n"] = a.rows
     n, d, k = cfg["n"], cfg["d"], cfg["k"]
     if a.workload == "lloyd":
         from kmeans import shard_rows
@@ -314,7 +318,7 @@ def main():
     kernel_ms = statistics.mean(kms)
     flop_launch = 2.0 * n_local * k * d
     achieved = flop_launch / (kernel_ms / 1e3) / 1e12
-    traffic = traffic_from_profiles(kname, a.workload)
+    traffic = traffic_from_profiles(kname, a.workload) if not a.rows else None
     roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
             "frac": achieved / tc_peak, "traffic": traffic, "kernel": kname, "kernel_ms": kernel_ms,
             "peak_source": f"{peak_src} bf16 dense burst"}
@@ -341,9 +345,9 @@ def main():
                 "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
                 "dtype": "fp16" if cfg["op"].startswith("fp16") else "bf16", "data": "synthetic",
-                "config": {"workload": "c2: distance+argmin n=2^20 x d=128, k=1024, fp16 GEMM + fp32 recompute, "
+                "config": {"workload": f"c2: distance+argmin n={n} x d=128, k=1024, fp16 GEMM + fp32 recompute, "
                                        "kappa=5" if a.workload == "c2" else
-                           "c4: Lloyd n=2^24 x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
+                           f"c4: Lloyd n={n} x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
                            "n_per_rank": n_local, "k": k, "d": d, "op": cfg["op"], "kappa": cfg["kappa"],
                            "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
                            "parallelism": f"dp{world}"},
