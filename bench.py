@@ -51,13 +51,16 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def traffic_from_profiles(kernel, workload):
-    """Per-launch DRAM bytes of `kernel` recorded from an ncu capture under profiles/."""
+def traffic_from_profiles(kernel, workload, rows):
+    """Per-launch DRAM bytes of `kernel` recorded from an ncu capture under profiles/, for
+    a launch over `rows` rows (the recorded figure is for the workload's full row count;
+    every term of it is proportional to the rows a launch processes)."""
     path = os.path.join(REPO, "profiles", f"{kernel}_{workload}.md")
+    full = C2["n"] if workload == "c2" else LLOYD["n"]
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
+                return float(line.split(":", 1)[1].split()[0]) * rows / full
     except OSError:
         pass
     return None
@@ -318,7 +321,7 @@ def main():
     kernel_ms = statistics.mean(kms)
     flop_launch = 2.0 * n_local * k * d
     achieved = flop_launch / (kernel_ms / 1e3) / 1e12
-    traffic = traffic_from_profiles(kname, a.workload) if not a.rows else None
+    traffic = traffic_from_profiles(kname, a.workload, n_local) if not a.rows else None
     roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
             "frac": achieved / tc_peak, "traffic": traffic, "kernel": kname, "kernel_ms": kernel_ms,
             "peak_source": f"{peak_src} bf16 dense burst"}

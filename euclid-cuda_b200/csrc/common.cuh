@@ -77,7 +77,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------- TMA
-// 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+// 2-D tiled bulk tensor load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
   asm volatile(
