@@ -259,6 +259,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     // screen threshold of a chunk: thr = U_c + pp (margin - (1 - K)), with
     // U_c = max(cc + bias) (1 + margin) - (1 - K) min cc over the chunk
     const float kv = a.margin - a.omk;
+    // ~31 in a register the compiler cannot fold, so that the column insertion below is
+    // one three-input logic op per element
+    uint32_t kmask;
+    asm volatile("mov.b32 %0, %1;" : "=r"(kmask) : "r"(~31u));
+    const float kInf = __int_as_float(0x7f800000);
     uint32_t rt_i = 0, t = 0, uses = 0;
     bool ok = true;
     for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
@@ -271,8 +276,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const float vlane = pp * kv;
       // best screened key of the row: x' with its column in the low 5 bits, and the
       // first sorted column of its chunk
-      float best_x = __int_as_float(0x7f800000);
-      int64_t best_j = 0;
+      float best_x = kInf;
+      uint32_t best_c = 0;
       for (int ct = 0; ct < a.n_ct; ++ct, ++t) {
         if ((t & 1u) != b) continue;  // the other parity's groups take this tile
         const uint32_t use = uses & 1u;
@@ -292,19 +297,21 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           u_own = ccbmax * (1.f + a.margin) - a.omk * mcc[lane * 32];
         }
         const float ccmax_t = mcc[nvt - 1];
-        const bool lane_exact = row_ok && !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        const bool lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
+        // per-lane threshold offset (rows past n never list a chunk); rows whose S may
+        // overflow its rounded format (or whose norms are not finite) list every chunk
+        const float vl = row_ok ? vlane : -kInf;
+        const bool force = row_ok && lane_exact;
         const int nch = (nvt + 31) >> 5;
         __syncwarp();
         if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
 
-#pragma unroll 1
-        for (int ch = 0; ch < nch; ++ch) {
-          float v[32];
-          tmem_ld32(tmem_acc + ch * 32, v);
-          const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vlane;
+        // one 32-column chunk: keys in place (x' with the column in the low 5 bits), their
+        // minimum, the screen, the fold into the row's best key
+        auto proc = [&](float (&v)[32], int ch) {
+          const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vl;
           const float4* cb4 = reinterpret_cast<const float4*>(ccb_w + ch * 32);
-          float kk[32];
 #pragma unroll
           for (int q4 = 0; q4 < 8; ++q4) {
             const float4 cb = cb4[q4];
@@ -312,42 +319,57 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
               const int e = q4 * 4 + r;
-              const float x = __fmaf_rn(-2.f, v[e], c4[r]);
-              kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
+              uint32_t kb;
+              asm("lop3.b32 %0, %1, %2, %3, 0xEA;"
+                  : "=r"(kb)
+                  : "r"(__float_as_uint(__fmaf_rn(-2.f, v[e], c4[r]))), "r"(kmask), "r"(static_cast<uint32_t>(e)));
+              v[e] = __uint_as_float(kb);
             }
           }
           float tt[11];
 #pragma unroll
-          for (int u = 0; u < 10; ++u) tt[u] = fmin3(kk[3 * u], kk[3 * u + 1], kk[3 * u + 2]);
-          tt[10] = fminf(kk[30], kk[31]);
+          for (int u = 0; u < 10; ++u) tt[u] = fmin3(v[3 * u], v[3 * u + 1], v[3 * u + 2]);
+          tt[10] = fminf(v[30], v[31]);
           const float km = fmin3(fmin3(tt[0], tt[1], tt[2]), fmin3(tt[3], tt[4], tt[5]),
                                  fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
-          const int64_t j0 = jt + ch * 32;
-          const bool cand = row_ok && (lane_exact || km <= thr);
-          if (!cand && km < best_x) {
-            best_x = km;
-            best_j = j0;
+          const bool cand = force || km <= thr;
+          const float kf = cand ? kInf : km;
+          if (kf < best_x) {
+            best_x = kf;
+            best_c = static_cast<uint32_t>(jt) + ch * 32;
           }
           // some pair of a candidate chunk may be flagged: the chunk and its accumulators
-          // go to this CTA's list region (warp-aggregated) for the exact second pass
+          // (read again from TMEM) go to this CTA's list region for the exact second pass
           const unsigned bal = __ballot_sync(0xffffffffu, cand);
           if (bal) {
             const int leader = __ffs(bal) - 1;
             unsigned long long base = 0;
             if (lane == leader) base = atomicAdd(lcount, static_cast<unsigned long long>(__popc(bal)));
             base = __shfl_sync(0xffffffffu, base, leader);
-            if (cand) {
-              const unsigned long long pos = base + __popc(bal & ((1u << lane) - 1u));
-              if (pos < a.region_cap) {
-                region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(j0);
-                float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
+            const unsigned long long pos = base + __popc(bal & ((1u << lane) - 1u));
+            const bool store = cand && pos < a.region_cap;
+            if (cand && !store) a.redo[i] = 1;
+            if (store)
+              region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(jt + ch * 32);
+            float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
 #pragma unroll
-                for (int e = 0; e < 32; e += 4) dst[e / 4] = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-              } else {
-                a.redo[i] = 1;
+            for (int half = 0; half < 2; ++half) {
+              float raw[16];
+              tmem_ld16(tmem_acc + ch * 32 + half * 16, raw);  // whole warp: the load is .sync.aligned
+              if (store) {
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                  dst[(half * 16 + e) / 4] = make_float4(raw[e], raw[e + 1], raw[e + 2], raw[e + 3]);
               }
             }
           }
+        };
+
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ++ch) {
+          float v0[32];
+          tmem_ld32(tmem_acc + ch * 32, v0);
+          proc(v0, ch);
         }
         tc_fence_before();
         __syncwarp();
@@ -360,10 +382,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       // this group's screened minimum of the row: distance and original center index
       float bestv = __int_as_float(0x7f800000);
       uint32_t besti = 0xffffffffu;
-      if (row_ok && best_x < __int_as_float(0x7f800000)) {
+      if (row_ok && best_x < kInf) {
         const uint32_t kb = __float_as_uint(best_x);
         bestv = fmaxf(__fadd_rn(__uint_as_float(kb & ~31u) - bias, pp), 0.f);
-        besti = static_cast<uint32_t>(__ldg(a.perm + best_j + (kb & 31u)));
+        besti = static_cast<uint32_t>(__ldg(a.perm + static_cast<int64_t>(best_c) + (kb & 31u)));
       }
       // merge the two tile parities of each row
       const uint32_t par = rt_i & 1u;
