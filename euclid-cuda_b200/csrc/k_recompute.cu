@@ -13,6 +13,8 @@
 #include "engine.h"
 #include "direct.cuh"
 
+#include <type_traits>
+
 namespace euc {
 
 struct RecArgs {
@@ -75,6 +77,73 @@ __global__ void __launch_bounds__(256) recompute_kernel(const RecArgs a) {
   }
 }
 
+// Argmin mode with fp32 inputs, warp-cooperative: a warp takes 32 listed pairs and
+// stages their P and C rows through shared memory 32 dimensions at a time with coalesced
+// (16-byte) loads; each lane then runs its pair's sum in the same arithmetic and the
+// same k order as direct_dist.
+constexpr int RW_WARPS = 4;
+constexpr int RW_K = 32;
+
+template <int REC>
+__global__ void __launch_bounds__(RW_WARPS * 32) recompute_argmin_rows_kernel(const RecArgs a) {
+  __shared__ float sp[RW_WARPS][32][RW_K + 1];
+  __shared__ float sc[RW_WARPS][32][RW_K + 1];
+  const float* P = static_cast<const float*>(a.P);
+  const float* C = static_cast<const float*>(a.C);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const unsigned long long cnt = *a.count;
+  const unsigned long long nlist = cnt < a.cap ? cnt : a.cap;
+  const int dim = a.dim;
+  const bool vec = (dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(C)) % 16 == 0);
+  const uint64_t gw = static_cast<uint64_t>(blockIdx.x) * RW_WARPS + w;
+  const uint64_t nw = static_cast<uint64_t>(gridDim.x) * RW_WARPS;
+  for (uint64_t base = gw * 32; base < nlist; base += nw * 32) {
+    const uint64_t t = base + lane;
+    bool valid = t < nlist;
+    const unsigned long long e = valid ? a.list[t] : 0ull;
+    const long long i = static_cast<long long>(e >> 32);
+    const long long j = static_cast<long long>(e & 0xffffffffull);
+    valid = valid && i < a.n && j < a.m;
+    DirectAcc<REC> acc;
+    for (int k0 = 0; k0 < dim; k0 += RW_K) {
+      const int kn = min(RW_K, dim - k0);
+      if (vec) {
+        const int quarter = lane >> 3, c4 = (lane & 7) * 4;  // 8 lanes x 16 bytes per row slab
+#pragma unroll 4
+        for (int rr = 0; rr < 32; rr += 4) {
+          const int r = rr + quarter;
+          const long long ir = __shfl_sync(0xffffffffu, i, r);
+          const long long jr = __shfl_sync(0xffffffffu, j, r);
+          const bool vr = __shfl_sync(0xffffffffu, valid, r);
+          float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), cv = pv;
+          if (vr && c4 < kn) {
+            pv = __ldg(reinterpret_cast<const float4*>(P + ir * dim + k0 + c4));
+            cv = __ldg(reinterpret_cast<const float4*>(C + jr * dim + k0 + c4));
+          }
+          float* dp = &sp[w][r][c4];
+          float* dc = &sc[w][r][c4];
+          dp[0] = pv.x; dp[1] = pv.y; dp[2] = pv.z; dp[3] = pv.w;
+          dc[0] = cv.x; dc[1] = cv.y; dc[2] = cv.z; dc[3] = cv.w;
+        }
+      } else {
+        for (int r = 0; r < 32; ++r) {
+          const long long ir = __shfl_sync(0xffffffffu, i, r);
+          const long long jr = __shfl_sync(0xffffffffu, j, r);
+          const bool vr = __shfl_sync(0xffffffffu, valid, r);
+          for (int c = lane; c < kn; c += 32) {
+            sp[w][r][c] = vr ? __ldg(P + ir * dim + k0 + c) : 0.f;
+            sc[w][r][c] = vr ? __ldg(C + jr * dim + k0 + c) : 0.f;
+          }
+        }
+      }
+      __syncwarp();
+      for (int kk = 0; kk < kn; ++kk) acc.add(sp[w][lane][kk], sc[w][lane][kk]);
+      __syncwarp();
+    }
+    if (valid) atomicMin(&a.row_key[i], make_key(static_cast<float>(acc.get()), static_cast<uint32_t>(j)));
+  }
+}
+
 template <typename TIN, int REC, typename TOUT, int FLAG, bool ARGMIN>
 static cudaError_t go_rec(const DistJob& j) {
   RecArgs a{};
@@ -92,6 +161,10 @@ static cudaError_t go_rec(const DistJob& j) {
   a.cc = j.cc;
   a.kf = j.kf;
   a.kd = j.kd;
+  if constexpr (ARGMIN && std::is_same<TIN, float>::value) {
+    recompute_argmin_rows_kernel<REC><<<num_sms() * 8, RW_WARPS * 32, 0, j.stream>>>(a);
+    return cudaGetLastError();
+  }
   const int blocks = num_sms() * 8;
   recompute_kernel<TIN, REC, TOUT, FLAG, ARGMIN><<<blocks, 256, 0, j.stream>>>(a);
   return cudaGetLastError();

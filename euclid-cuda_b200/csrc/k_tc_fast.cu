@@ -618,31 +618,54 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   unsigned long long cnt = a.region_cnt[r];
   if (cnt > a.region_cap) cnt = a.region_cap;
   const unsigned long long rbase = static_cast<unsigned long long>(r) * a.region_cap;
-  for (unsigned long long t = wr; t < cnt; t += kStride) {
-    const unsigned long long e = a.clist[rbase + t];
-    const float s = a.sbuf[(rbase + t) * 32 + lane];
-    const int64_t i = static_cast<int64_t>(e >> 32);
-    const int64_t j = static_cast<int64_t>(e & 0xffffffffull) + lane;
-    if (i >= a.n || a.redo[i]) continue;  // warp-uniform; redo rows are evaluated whole
-    unsigned long long key = ~0ull;
-    bool fl = false;
-    uint32_t jo = 0;
-    if (j < a.m) {
-      const float pp = __ldg(a.pp + i), cc = __ldg(a.cc_s + j);
-      jo = static_cast<uint32_t>(__ldg(a.perm + j));
-      const float d = exact_d<SROUND>(s, pp, cc);
-      fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
-      if (!fl) key = make_key(d, jo);
+  // two entries per iteration: their loads are independent and issue together
+  constexpr int U = 2;
+  for (unsigned long long t0 = wr; t0 < cnt; t0 += kStride * U) {
+    unsigned long long e[U];
+    float sv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long t = t0 + u * kStride;
+      const bool in = t < cnt;
+      e[u] = in ? a.clist[rbase + t] : ~0ull;
+      sv[u] = in ? a.sbuf[(rbase + t) * 32 + lane] : 0.f;
     }
-    const unsigned bal = __ballot_sync(0xffffffffu, fl);
-    if (bal) {
-      if (fl) wbuf[wcnt + __popc(bal & ((1u << lane) - 1u))] = (static_cast<unsigned long long>(i) << 32) | jo;
-      wcnt += __popc(bal);
-      __syncwarp();
-      if (wcnt > EV_WBUF - 32) flush_pairs<REC>(a, wbuf, wcnt, lane);
+    int64_t i[U];
+    bool jv[U], skip[U];
+    float pp[U], cc[U];
+    uint32_t jo[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      i[u] = static_cast<int64_t>(e[u] >> 32);
+      const int64_t j = static_cast<int64_t>(e[u] & 0xffffffffull) + lane;
+      const bool iv = i[u] < a.n;
+      skip[u] = !iv || a.redo[iv ? i[u] : 0] != 0;  // redo rows are evaluated whole
+      jv[u] = iv && j < a.m;
+      pp[u] = iv ? __ldg(a.pp + i[u]) : 0.f;
+      cc[u] = jv[u] ? __ldg(a.cc_s + j) : 0.f;
+      jo[u] = jv[u] ? static_cast<uint32_t>(__ldg(a.perm + j)) : 0u;
     }
-    key = warp_min_u64(key);
-    if (lane == 0 && key != ~0ull) atomicMin(&a.row_key[i], key);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (skip[u]) continue;  // warp-uniform
+      const float d = exact_d<SROUND>(sv[u], pp[u], cc[u]);
+      const bool fl = jv[u] && d <= __fmul_rn(a.K, __fadd_rn(pp[u], cc[u]));
+      const unsigned bal = __ballot_sync(0xffffffffu, fl);
+      if (bal) {
+        if (fl) wbuf[wcnt + __popc(bal & ((1u << lane) - 1u))] = (static_cast<unsigned long long>(i[u]) << 32) | jo[u];
+        wcnt += __popc(bal);
+        __syncwarp();
+        if (wcnt > EV_WBUF - 32) flush_pairs<REC>(a, wbuf, wcnt, lane);
+      }
+      // row key of the chunk: smallest unflagged distance (d >= 0, so its bits order as
+      // unsigned), then the smallest original index among the columns that reach it
+      const uint32_t dbits = (jv[u] && !fl) ? __float_as_uint(d) : 0xffffffffu;
+      const uint32_t dmin = __reduce_min_sync(0xffffffffu, dbits);
+      if (dmin != 0xffffffffu) {
+        const uint32_t jmin = __reduce_min_sync(0xffffffffu, dbits == dmin ? jo[u] : 0xffffffffu);
+        if (lane == 0) atomicMin(&a.row_key[i[u]], (static_cast<unsigned long long>(dmin) << 32) | jmin);
+      }
+    }
   }
   if (wcnt > 0) flush_pairs<REC>(a, wbuf, wcnt, lane);
 }
