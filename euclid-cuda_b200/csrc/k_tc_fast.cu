@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
 
+        uint32_t cmask = 0;  // this lane's candidate chunks of the tile
         // one 32-column chunk: keys in place (x' with the column in the low 5 bits), their
         // minimum, the screen, the fold into the row's best key
         auto proc = [&](float (&v)[32], int ch) {
@@ -338,31 +339,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             best_x = kf;
             best_c = static_cast<uint32_t>(jt) + ch * 32;
           }
-          // some pair of a candidate chunk may be flagged: the chunk and its accumulators
-          // (read again from TMEM) go to this CTA's list region for the exact second pass
-          const unsigned bal = __ballot_sync(0xffffffffu, cand);
-          if (bal) {
-            const int leader = __ffs(bal) - 1;
-            unsigned long long base = 0;
-            if (lane == leader) base = atomicAdd(lcount, static_cast<unsigned long long>(__popc(bal)));
-            base = __shfl_sync(0xffffffffu, base, leader);
-            const unsigned long long pos = base + __popc(bal & ((1u << lane) - 1u));
-            const bool store = cand && pos < a.region_cap;
-            if (cand && !store) a.redo[i] = 1;
-            if (store)
-              region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(jt + ch * 32);
-            float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              float raw[16];
-              tmem_ld16(tmem_acc + ch * 32 + half * 16, raw);  // whole warp: the load is .sync.aligned
-              if (store) {
-#pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                  dst[(half * 16 + e) / 4] = make_float4(raw[e], raw[e + 1], raw[e + 2], raw[e + 3]);
-              }
-            }
-          }
+          cmask |= static_cast<uint32_t>(cand) << ch;
         };
 
 #pragma unroll 1
@@ -370,6 +347,45 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           float v0[32];
           tmem_ld32(tmem_acc + ch * 32, v0);
           proc(v0, ch);
+        }
+
+        // candidate chunks of this tile (some pair may be flagged): each goes, with its
+        // accumulators read again from TMEM, to this CTA's list region for the exact
+        // second pass; one shared-memory reservation per warp and tile
+        if (__any_sync(0xffffffffu, cmask != 0)) {
+          uint32_t bal[TF_BN / 32];
+          uint32_t total = 0;
+#pragma unroll
+          for (int ch = 0; ch < TF_BN / 32; ++ch) {
+            bal[ch] = __ballot_sync(0xffffffffu, (cmask >> ch) & 1u);
+            total += __popc(bal[ch]);
+          }
+          unsigned long long base = 0;
+          if (lane == 0) base = atomicAdd(lcount, static_cast<unsigned long long>(total));
+          base = __shfl_sync(0xffffffffu, base, 0);
+#pragma unroll
+          for (int ch = 0; ch < TF_BN / 32; ++ch) {
+            if (bal[ch]) {
+              const bool cand = (cmask >> ch) & 1u;
+              const unsigned long long pos = base + __popc(bal[ch] & ((1u << lane) - 1u));
+              base += __popc(bal[ch]);
+              const bool store = cand && pos < a.region_cap;
+              if (cand && !store) a.redo[i] = 1;
+              if (store)
+                region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(jt + ch * 32);
+              float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                float raw[16];
+                tmem_ld16(tmem_acc + ch * 32 + half * 16, raw);  // whole warp: the load is .sync.aligned
+                if (store) {
+#pragma unroll
+                  for (int e = 0; e < 16; e += 4)
+                    dst[(half * 16 + e) / 4] = make_float4(raw[e], raw[e + 1], raw[e + 2], raw[e + 3]);
+                }
+              }
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
