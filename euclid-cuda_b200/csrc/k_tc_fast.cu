@@ -3,12 +3,11 @@
 // TMA -> 128B-swizzled smem -> tcgen05.mma -> TMEM, with an epilogue reduced to what
 // an argmin needs, so that it keeps pace with the tensor cores:
 //
-//  * a CTA owns 256 rows at a time (two M=128 accumulators that share each 128-center
-//    B tile, which halves the B traffic per MMA against 128-row tiles); the A rows stay
-//    resident in shared memory while the center tiles stream past;
-//  * TMEM holds four 128-column accumulators (row half h, tile parity b); each belongs
-//    to one group of 4 epilogue warps (one per TMEM lane quadrant), so a group has two
-//    tile times to drain its accumulator while the MMAs of the next tile proceed;
+//  * a CTA owns 128 rows at a time (A resident in shared memory, double-buffered) while
+//    the 256-center tiles stream past, one M=128, N=256 MMA per K step;
+//  * TMEM holds two 256-column accumulators (tile parity b); the 16 epilogue warps form
+//    4 groups (b, column half), one warp per TMEM lane quadrant, so a group has two
+//    tile times to drain its half of an accumulator while the next tile's MMAs proceed;
 //  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
 //    each center tile's norms into shared memory ahead of use;
 //  * per 32-column chunk an epilogue warp forms keys x' = cc + bias - 2 s (one FMA),
@@ -40,17 +39,19 @@ namespace euc {
 
 static __device__ int s_tf_err;
 
-// A CTA tile is 256 rows (two M=128 accumulator halves h = 0, 1, sharing every B tile)
-// by 128 centers; TMEM holds 4 accumulators of 128 columns: (half h, tile parity b).
-constexpr int TF_BM = 256;
-constexpr int TF_BN = 128;
-constexpr int TF_EPI_WARPS = 16;  // 4 groups (h, b) x 4 TMEM lane quadrants
+// A CTA tile is 128 rows by 256 centers: one M=128, N=256 MMA per K step (on this part
+// an MMA instruction costs the same time for N = 128 and N = 256, so N = 256 doubles the
+// rate); TMEM holds 2 accumulators of 256 columns, one per tile parity b.
+constexpr int TF_BM = 128;
+constexpr int TF_BN = 256;
+constexpr int TF_EPI_WARPS = 16;  // 4 groups (b, column half) x 4 TMEM lane quadrants
 constexpr int TF_THREADS = (2 + TF_EPI_WARPS) * 32;
-constexpr int TF_KB_BYTES = 128 * 128;  // one 128-row x 128-byte K block (A half or B tile)
+constexpr int TF_A_KB = TF_BM * 128;  // one 128-row x 128-byte K block of A
+constexpr int TF_B_KB = TF_BN * 128;  // one 256-row x 128-byte K block of B
 constexpr int TF_SLOTS = 4;             // center-metadata ring
 constexpr int TF_META_BYTES = TF_BN * 4;  // the tile's sorted center norms
 constexpr int TF_BAR_BYTES = 512;
-constexpr int TF_EPI_BYTES = TF_EPI_WARPS * TF_BN * 4 + TF_BM * 8;  // per-warp biased norms + row merge
+constexpr int TF_EPI_BYTES = TF_EPI_WARPS * 128 * 4 + 2 * 4 * TF_BM * 4;  // per-warp biased norms + row merge
 
 struct TfArgs {
   int64_t n, m;
@@ -77,21 +78,21 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const int NST = a.nst;
   const bool a_res = a.a_res != 0;
   const int KB = a.kblocks;
-  const uint32_t a_bytes = static_cast<uint32_t>(2 * KB) * TF_KB_BYTES;   // both halves, all K blocks
-  const uint32_t stage_bytes = a_res ? TF_KB_BYTES : 3u * TF_KB_BYTES;    // B  |  A0 A1 B
+  const uint32_t a_bytes = static_cast<uint32_t>(KB) * TF_A_KB;                   // all K blocks of A
+  const uint32_t stage_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);  // B  |  A B
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
-  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 128 sorted norms
+  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 256 sorted norms
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + TF_SLOTS * TF_META_BYTES);
   uint64_t* empty = full + NST;
   uint64_t* afull = empty + NST;
   uint64_t* aempty = afull + 2;
-  uint64_t* accf = aempty + 2;   // per tile parity: both halves' accumulators are complete
-  uint64_t* acce = accf + 2;     // per tile parity: both halves' accumulators were read
+  uint64_t* accf = aempty + 2;   // per tile parity: the accumulator is complete
+  uint64_t* acce = accf + 2;     // per tile parity: the accumulator was read
   uint64_t* metaf = acce + 2;
   uint64_t* metae = metaf + TF_SLOTS;
   uint64_t* drain = metae + TF_SLOTS;
-  uint64_t* mfull = drain + 1;   // row merge: parity-1 groups have published their row minima
-  uint64_t* mdone = mfull + 1;   // row merge: parity-0 groups have consumed them
+  uint64_t* mfull = drain + 1;   // row merge: groups 1..3 have published their row minima
+  uint64_t* mdone = mfull + 1;   // row merge: group 0 has consumed them
   unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lcount + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr uint32_t kCols = 4 * TF_BN;  // 512
+  constexpr uint32_t kCols = 2 * TF_BN;  // 512
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -117,8 +118,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&metae[s], TF_EPI_WARPS / 2);
     }
     mbar_init(drain, 1);
-    mbar_init(mfull, TF_EPI_WARPS / 2);
-    mbar_init(mdone, TF_EPI_WARPS / 2);
+    mbar_init(mfull, TF_EPI_WARPS - 4);
+    mbar_init(mdone, 4);
     *lcount = 0;
     *abort_flag = 0;
     fence_mbar_init();
@@ -147,9 +148,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&afull[abuf], a_bytes);
           uint8_t* sA = smem + abuf * a_bytes;
-          for (int h = 0; h < 2; ++h)
-            for (int kb = 0; kb < KB; ++kb)
-              tma_load_2d(sA + (h * KB + kb) * TF_KB_BYTES, &tmA, &afull[abuf], kb * kelems, row0 + h * 128);
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(sA + kb * TF_A_KB, &tmA, &afull[abuf], kb * kelems, row0);
           a_issued |= 1u << abuf;
           a_last = (a_last & ~(1u << abuf)) | (ause << abuf);
         }
@@ -169,8 +169,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
               tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * TF_BN);
             } else {
               tma_load_2d(st, &tmA, &full[stage], kb * kelems, row0);
-              tma_load_2d(st + TF_KB_BYTES, &tmA, &full[stage], kb * kelems, row0 + 128);
-              tma_load_2d(st + 2 * TF_KB_BYTES, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+              tma_load_2d(st + TF_A_KB, &tmB, &full[stage], kb * kelems, ct * TF_BN);
             }
             issued_mask |= 1u << stage;
             last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
@@ -211,20 +210,17 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
-            const uint32_t sB = a_res ? st : st + 2 * TF_KB_BYTES;
+            const uint32_t sA = a_res ? sAres + kb * TF_A_KB : st;
+            const uint32_t sB = a_res ? st : st + TF_A_KB;
+            const uint32_t d_tmem = tmem_base + b * TF_BN;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t sA = a_res ? sAres + (h * KB + kb) * TF_KB_BYTES : st + h * TF_KB_BYTES;
-              const uint32_t d_tmem = tmem_base + (2 * b + h) * TF_BN;
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
-                const uint64_t bd = sw128_kmajor_desc(sB + kk * 32);
-                if constexpr (KIND == 2)
-                  umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-                else
-                  umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-              }
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
+              const uint64_t bd = sw128_kmajor_desc(sB + kk * 32);
+              if constexpr (KIND == 2)
+                umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+              else
+                umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
             }
             umma_commit(&empty[stage]);
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
@@ -246,14 +242,14 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;            // 0..15
     const int q = warp & 3;             // TMEM lane quadrant
-    const int g = ew >> 2;              // group: row half h = g & 1, tile parity b = g >> 1
-    const int h = g & 1;
+    const int g = ew >> 2;              // group: tile parity b = g >> 1, column half hc = g & 1
+    const int hc = g & 1;
     const uint32_t b = static_cast<uint32_t>(g >> 1);
-    const int row_local = h * 128 + q * 32 + lane;
-    const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (2 * b + h) * TF_BN;
-    float* ccb_w = epi + ew * TF_BN;                           // this warp's tile columns: norm + bias
-    float* mv = epi + TF_EPI_WARPS * TF_BN;                    // row merge: [256] minima
-    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + TF_BM);    //            [256] their columns
+    const int row_local = q * 32 + lane;
+    const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * TF_BN + hc * 128;
+    float* ccb_w = epi + ew * 128;                             // this warp's 128 columns: norm + bias
+    float* mv = epi + TF_EPI_WARPS * 128;                      // row merge: [4][128] minima
+    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 4 * TF_BM);  //          [4][128] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
     // screen threshold of a chunk: thr = U_c + pp (margin - (1 - K)), with
@@ -283,20 +279,20 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t use = uses & 1u;
         ++uses;
         const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
-        const int64_t jt = static_cast<int64_t>(ct) * TF_BN;  // first (sorted) column of the tile
+        const int64_t jt = static_cast<int64_t>(ct) * TF_BN + hc * 128;  // first (sorted) column of this warp
         if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
-        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES);
+        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES) + hc * 128;
         const int64_t remt = a.m - jt;
-        const int nvt = remt >= TF_BN ? TF_BN : static_cast<int>(remt);
+        const int nvt = remt <= 0 ? 0 : (remt >= 128 ? 128 : static_cast<int>(remt));
 #pragma unroll
-        for (int c = lane; c < TF_BN; c += 32) ccb_w[c] = (c < nvt) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
+        for (int c = lane; c < 128; c += 32) ccb_w[c] = (c < nvt) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
         float u_own = 0.f;  // lane L < 4: U of chunk L
         if (lane < 4 && lane * 32 < nvt) {
           const int last = min(lane * 32 + 31, nvt - 1);
           const float ccbmax = __fadd_rn(mcc[last], bias);
           u_own = ccbmax * (1.f + a.margin) - a.omk * mcc[lane * 32];
         }
-        const float ccmax_t = mcc[nvt - 1];
+        const float ccmax_t = nvt > 0 ? mcc[nvt - 1] : 0.f;
         const bool lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
         // per-lane threshold offset (rows past n never list a chunk); rows whose S may
         // overflow its rounded format (or whose norms are not finite) list every chunk
@@ -353,10 +349,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         // accumulators read again from TMEM, to this CTA's list region for the exact
         // second pass; one shared-memory reservation per warp and tile
         if (__any_sync(0xffffffffu, cmask != 0)) {
-          uint32_t bal[TF_BN / 32];
+          uint32_t bal[4];
           uint32_t total = 0;
 #pragma unroll
-          for (int ch = 0; ch < TF_BN / 32; ++ch) {
+          for (int ch = 0; ch < 4; ++ch) {
             bal[ch] = __ballot_sync(0xffffffffu, (cmask >> ch) & 1u);
             total += __popc(bal[ch]);
           }
@@ -364,7 +360,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (lane == 0) base = atomicAdd(lcount, static_cast<unsigned long long>(total));
           base = __shfl_sync(0xffffffffu, base, 0);
 #pragma unroll
-          for (int ch = 0; ch < TF_BN / 32; ++ch) {
+          for (int ch = 0; ch < 4; ++ch) {
             if (bal[ch]) {
               const bool cand = (cmask >> ch) & 1u;
               const unsigned long long pos = base + __popc(bal[ch] & ((1u << lane) - 1u));
@@ -403,21 +399,24 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         bestv = fmaxf(__fadd_rn(__uint_as_float(kb & ~31u) - bias, pp), 0.f);
         besti = static_cast<uint32_t>(__ldg(a.perm + static_cast<int64_t>(best_c) + (kb & 31u)));
       }
-      // merge the two tile parities of each row
+      // merge the four (parity, column half) partial minima of each row
       const uint32_t par = rt_i & 1u;
-      if (b == 1) {
+      if (g != 0) {
         if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag)) { ok = false; break; }
-        mv[row_local] = bestv;
-        mi[row_local] = besti;
+        mv[(g - 1) * TF_BM + row_local] = bestv;
+        mi[(g - 1) * TF_BM + row_local] = besti;
         __syncwarp();
         if (lane == 0) mbar_arrive(mfull);
       } else {
         if (!mbar_wait(mfull, par, abort_flag)) { ok = false; break; }
-        const float ov = mv[row_local];
-        const uint32_t oi = mi[row_local];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const float ov = mv[p * TF_BM + row_local];
+          const uint32_t oi = mi[p * TF_BM + row_local];
+          if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(mdone);
-        if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
         if (row_ok) a.row_key[i] = make_key(bestv, besti);
       }
     }
@@ -442,23 +441,23 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 constexpr size_t TF_SMEM_LIMIT = 232448;
 constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
 
-// Resident A (two 256-row tiles, double-buffered) with B-only stages when that leaves
-// room for 3 stages, else streaming (A0 A1 B) stages.
+// Resident A (the row tile, double-buffered) with B-only stages when that leaves room
+// for 3 stages, else streaming (A B) stages.
 static void tf_pipeline(int kblocks, int* nst, int* a_res) {
-  const size_t abytes = static_cast<size_t>(2 * kblocks) * TF_KB_BYTES;
+  const size_t abytes = static_cast<size_t>(kblocks) * TF_A_KB;
   const size_t avail = TF_SMEM_LIMIT - TF_FIXED;
-  if (2 * abytes + 3 * TF_KB_BYTES <= avail) {
+  if (2 * abytes + 3 * TF_B_KB <= avail) {
     *a_res = 1;
-    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / TF_KB_BYTES));
+    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / TF_B_KB));
   } else {
     *a_res = 0;
-    *nst = static_cast<int>(std::min<size_t>(8, avail / (3 * TF_KB_BYTES)));
+    *nst = static_cast<int>(std::min<size_t>(8, avail / (TF_A_KB + TF_B_KB)));
   }
 }
 
 static size_t tf_smem_bytes(int kblocks, int nst, int a_res) {
-  const size_t body = a_res ? 4 * static_cast<size_t>(kblocks) * TF_KB_BYTES + nst * TF_KB_BYTES
-                            : nst * 3 * static_cast<size_t>(TF_KB_BYTES);
+  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TF_A_KB + nst * static_cast<size_t>(TF_B_KB)
+                            : nst * static_cast<size_t>(TF_A_KB + TF_B_KB);
   return TF_FIXED + body;
 }
 
@@ -514,7 +513,7 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
-  if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, 128, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
   if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
   if (kind == 0) return launch_tf_t<0>(ta, tb, a, grid, j.stream);
