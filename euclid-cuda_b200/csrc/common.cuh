@@ -153,6 +153,17 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
 }
+// Same for a K-major operand with 32-byte rows stored with the 32-byte swizzle (8-row
+// atoms of 256 bytes): SBO = 256 >> 4, layout 6 = SWIZZLE_32B.
+__device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(256u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(6u) << 61;
+  return d;
+}
 // Instruction descriptor: fp32 accumulator, A/B format (0 f16, 1 bf16, 2 tf32),
 // both K-major, M x N tile.
 __host__ __device__ constexpr uint32_t umma_idesc(uint32_t ab_format, uint32_t M, uint32_t N) {

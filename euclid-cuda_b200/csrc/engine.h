@@ -108,6 +108,14 @@ struct DistJob {
   int regions;
   uint32_t* region_cnt;          // entries per region (written by the screening kernel)
   uint8_t* redo;                 // rows whose candidates did not fit: recomputed whole
+  // fast argmin: the MMA also adds (cc_j + B) / 2 per column through one extra K block
+  // (32-byte rows): a_aux = 128 rows of [2^E, 2^E, 2^E, 0...], b_aux (sorted) = the
+  // three-part split of (cc_j + B) / 2^(E+1); B = 1.0625 max pp keeps every value >= 0
+  void* a_aux;
+  void* b_aux_sorted;
+  unsigned int* ppmax_bits;      // max finite pp (bits), reduced on the device
+  float* aux_b;                  // B (device scalar)
+  int* aux_e;                    // E (device scalar)
   cudaStream_t stream;
 };
 
@@ -123,6 +131,10 @@ cudaError_t launch_redo_rows(const DistJob& j);
 int tc_fast_regions(int64_t n);  // CTAs (= list regions) of the screening kernel
 bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows, bool is_f32,
                   bool is_bf16);
+bool tc_make_tmap_sw32(CUtensorMap* map, const void* base, int64_t rows, int esize, int box_rows, bool is_f32,
+                       bool is_bf16);
+// fast argmin: B and E from max pp and max cc, the A-side extra K block
+cudaError_t launch_aux_params(const DistJob& j);
 cudaError_t launch_simt(const DistJob& j);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);

@@ -527,6 +527,23 @@ bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int 
   return r == CUDA_SUCCESS;
 }
 
+// Row-major [rows x (32 / esize)] matrix (32-byte rows), box = 32 bytes x box_rows,
+// 32-byte swizzle.
+bool tc_make_tmap_sw32(CUtensorMap* map, const void* base, int64_t rows, int esize, int box_rows, bool is_f32,
+                       bool is_bf16) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(32 / esize), static_cast<cuuint64_t>(rows)};
+  cuuint64_t gstride[1] = {32};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(32 / esize), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt = is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : (is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static int pick_bn(int64_t m) {
   if (m <= 64) return 64;
   if (m <= 128) return 128;

@@ -18,8 +18,8 @@
 //    -- bounded with the chunk's smallest and largest norm, tight because norms are
 //    sorted -- is not resolved here: its (row, chunk) and its 32 fp32 accumulators are
 //    appended to a list that eval_chunks_kernel evaluates with the operator's exact
-//    arithmetic (the same rounded S, distance formula and cancellation test as the
-//    exact epilogue; flagged pairs go to the direct-recompute list);
+//    arithmetic on s = y0 - y (the same rounding of S, distance formula and cancellation
+//    test as the exact epilogue; flagged pairs go to the direct-recompute list);
 //  * every other chunk can hold no flagged pair and contributes its key minimum.
 //
 // Labels equal the exact epilogue's wherever the row's top-two distance gap exceeds
@@ -49,9 +49,11 @@ constexpr int TF_THREADS = (2 + TF_EPI_WARPS) * 32;
 constexpr int TF_A_KB = TF_BM * 128;  // one 128-row x 128-byte K block of A
 constexpr int TF_B_KB = TF_BN * 128;  // one 256-row x 128-byte K block of B
 constexpr int TF_SLOTS = 4;             // center-metadata ring
-constexpr int TF_META_BYTES = TF_BN * 4;  // the tile's sorted center norms
+constexpr int TF_BAUX_BYTES = TF_BN * 32;  // the tile's extra-K rows (32 bytes each)
+constexpr int TF_META_BYTES = TF_BAUX_BYTES + TF_BN * 4;  // + the tile's sorted center norms
+constexpr int TF_AAUX_BYTES = TF_BM * 32;
 constexpr int TF_BAR_BYTES = 512;
-constexpr int TF_EPI_BYTES = TF_EPI_WARPS * 128 * 4 + 2 * 4 * TF_BM * 4;  // per-warp biased norms + row merge
+constexpr int TF_EPI_BYTES = 2 * 4 * TF_BM * 4;  // row merge
 
 struct TfArgs {
   int64_t n, m;
@@ -61,6 +63,7 @@ struct TfArgs {
   const float* ccs;   // norms, sorted, padded to whole 256-center tiles
   const int* perm;    // sorted position -> original index, padded
   float omk, margin, ovf;
+  const float* aux_b;           // B of the extra K block (device scalar)
   unsigned long long* row_key;
   unsigned long long* list;     // candidate chunks: region r = list + r * region_cap
   float* sbuf;                  // their 32 accumulator values, same index
@@ -72,6 +75,7 @@ struct TfArgs {
 template <int KIND>
 __global__ void __launch_bounds__(TF_THREADS, 1)
     dist_tc_fast_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmAaux, const __grid_constant__ CUtensorMap tmBaux,
                         const TfArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -81,8 +85,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const uint32_t a_bytes = static_cast<uint32_t>(KB) * TF_A_KB;                   // all K blocks of A
   const uint32_t stage_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);  // B  |  A B
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
-  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 256 sorted norms
-  uint64_t* full = reinterpret_cast<uint64_t*>(meta + TF_SLOTS * TF_META_BYTES);
+  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x (256 extra-K rows, 256 sorted norms)
+  uint8_t* aaux = meta + TF_SLOTS * TF_META_BYTES; // the A side of the extra K block (resident)
+  uint64_t* full = reinterpret_cast<uint64_t*>(aaux + TF_AAUX_BYTES);
   uint64_t* empty = full + NST;
   uint64_t* afull = empty + NST;
   uint64_t* aempty = afull + 2;
@@ -90,7 +95,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   uint64_t* acce = accf + 2;     // per tile parity: the accumulator was read
   uint64_t* metaf = acce + 2;
   uint64_t* metae = metaf + TF_SLOTS;
-  uint64_t* drain = metae + TF_SLOTS;
+  uint64_t* auxf = metae + TF_SLOTS;
+  uint64_t* drain = auxf + 1;
   uint64_t* mfull = drain + 1;   // row merge: groups 1..3 have published their row minima
   uint64_t* mdone = mfull + 1;   // row merge: group 0 has consumed them
   unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
@@ -117,6 +123,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&metaf[s], 1);
       mbar_init(&metae[s], TF_EPI_WARPS / 2);
     }
+    mbar_init(auxf, 1);
     mbar_init(drain, 1);
     mbar_init(mfull, TF_EPI_WARPS - 4);
     mbar_init(mdone, 4);
@@ -128,6 +135,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmAaux);
+    prefetch_tmap(&tmBaux);
   }
   tc_fence_before();
   __syncthreads();
@@ -141,6 +150,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       uint32_t issued_mask = 0, last_phase = 0, a_issued = 0, a_last = 0, m_issued = 0, m_last = 0;
       bool ok = true;
       const int kelems = (KIND == 2) ? 32 : 64;
+      mbar_arrive_expect_tx(auxf, TF_AAUX_BYTES);
+      tma_load_2d(aaux, &tmAaux, auxf, 0, 0);
       for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const int row0 = static_cast<int>(rt * TF_BM);
@@ -158,7 +169,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* ms = meta + slot * TF_META_BYTES;
           mbar_arrive_expect_tx(&metaf[slot], TF_META_BYTES);
-          bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_META_BYTES, &metaf[slot]);
+          tma_load_2d(ms, &tmBaux, &metaf[slot], 0, ct * TF_BN);
+          bulk_load_1d(ms + TF_BAUX_BYTES, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
           m_issued |= 1u << slot;
           m_last = (m_last & ~(1u << slot)) | (su << slot);
           for (int kb = 0; kb < KB; ++kb) {
@@ -188,6 +200,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         if (a_issued & (1u << s)) mbar_wait(&afull[s], (a_last >> s) & 1u, &no_abort);
       for (int s = 0; s < TF_SLOTS; ++s)
         if (m_issued & (1u << s)) mbar_wait(&metaf[s], (m_last >> s) & 1u, &no_abort);
+      mbar_wait(auxf, 0, &no_abort);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -195,7 +208,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
       constexpr uint32_t idesc = umma_idesc(fmt, 128, TF_BN);
       uint32_t stage = 0, phase = 0, t = 0, rt_i = 0;
-      bool ok = true;
+      bool ok = mbar_wait(auxf, 0, abort_flag);
+      const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux));
       for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
@@ -226,6 +240,17 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
+          // the extra K block: adds y0_j = (cc_j + B) / 2 to every row of column j
+          {
+            const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
+            if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t bd = sw32_kmajor_desc(smem_u32(meta + slot * TF_META_BYTES));
+            if constexpr (KIND == 2)
+              umma_tf32(tmem_base + b * TF_BN, aux_ad, bd, idesc, 1u);
+            else
+              umma_f16(tmem_base + b * TF_BN, aux_ad, bd, idesc, 1u);
+          }
           umma_commit(&accf[b]);
         }
         if (a_res && ok) umma_commit(&aempty[abuf]);
@@ -240,6 +265,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // The accumulators hold y = (cc + B) / 2 - s >= 0 (the extra K block adds the first
+    // term), so a chunk's smallest distance is its smallest y: keys are y with the
+    // column in the low 5 mantissa bits, reduced with 3-way mins.
     const int ew = warp - 2;            // 0..15
     const int q = warp & 3;             // TMEM lane quadrant
     const int g = ew >> 2;              // group: tile parity b = g >> 1, column half hc = g & 1
@@ -247,14 +275,17 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const uint32_t b = static_cast<uint32_t>(g >> 1);
     const int row_local = q * 32 + lane;
     const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * TF_BN + hc * 128;
-    float* ccb_w = epi + ew * 128;                             // this warp's 128 columns: norm + bias
-    float* mv = epi + TF_EPI_WARPS * 128;                      // row merge: [4][128] minima
-    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 4 * TF_BM);  //          [4][128] their columns
+    float* mv = epi;                                             // row merge: [4][128] minima
+    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 4 * TF_BM);  //            [4][128] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
-    // screen threshold of a chunk: thr = U_c + pp (margin - (1 - K)), with
-    // U_c = max(cc + bias) (1 + margin) - (1 - K) min cc over the chunk
-    const float kv = a.margin - a.omk;
+    const float B = __ldg(a.aux_b);
+    // screen: a pair can only be flagged (d <= K (pp + cc)) where
+    //   y <= (cc + B - (1 - K)(pp + cc)) / 2,
+    // so a chunk is a candidate when its smallest y <= thr = U_c + V, with
+    //   U_c = ((max cc + B)(1 + margin) - (1 - K) min cc) / 2 over the chunk,
+    //   V   = pp (margin - (1 - K)) / 2 per row
+    const float kv = 0.5f * (a.margin - a.omk);
     // ~31 in a register the compiler cannot fold, so that the column insertion below is
     // one three-input logic op per element
     uint32_t kmask;
@@ -266,13 +297,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const int64_t i = rt * TF_BM + row_local;
       const bool row_ok = i < a.n;
       const float pp = row_ok ? __ldg(a.pp + i) : 0.f;
-      // warp-uniform bias making every key non-negative: x' = cc - 2 s + bias >= 0
-      const float ppf = (row_ok && pp < 3.0e38f) ? pp : 0.f;
-      const float bias = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ppf))) * 1.0625f + 1e-30f;
       const float vlane = pp * kv;
-      // best screened key of the row: x' with its column in the low 5 bits, and the
-      // first sorted column of its chunk
-      float best_x = kInf;
+      // best screened key of the row: y with its column in the low 5 bits, and the first
+      // sorted column of its chunk
+      float best_y = kInf;
       uint32_t best_c = 0;
       for (int ct = 0; ct < a.n_ct; ++ct, ++t) {
         if ((t & 1u) != b) continue;  // the other parity's groups take this tile
@@ -281,47 +309,35 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
         const int64_t jt = static_cast<int64_t>(ct) * TF_BN + hc * 128;  // first (sorted) column of this warp
         if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
-        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES) + hc * 128;
+        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES + TF_BAUX_BYTES) + hc * 128;
         const int64_t remt = a.m - jt;
         const int nvt = remt <= 0 ? 0 : (remt >= 128 ? 128 : static_cast<int>(remt));
-#pragma unroll
-        for (int c = lane; c < 128; c += 32) ccb_w[c] = (c < nvt) ? __fadd_rn(mcc[c], bias) : 3.0e38f;
         float u_own = 0.f;  // lane L < 4: U of chunk L
         if (lane < 4 && lane * 32 < nvt) {
           const int last = min(lane * 32 + 31, nvt - 1);
-          const float ccbmax = __fadd_rn(mcc[last], bias);
-          u_own = ccbmax * (1.f + a.margin) - a.omk * mcc[lane * 32];
+          u_own = 0.5f * (__fadd_rn(mcc[last], B) * (1.f + a.margin) - a.omk * mcc[lane * 32]);
         }
         const float ccmax_t = nvt > 0 ? mcc[nvt - 1] : 0.f;
-        const bool lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
-        // per-lane threshold offset (rows past n never list a chunk); rows whose S may
-        // overflow its rounded format (or whose norms are not finite) list every chunk
-        const float vl = row_ok ? vlane : -kInf;
+        // rows whose S may overflow its rounded format, or whose norms (or this tile's)
+        // are not finite, list every chunk
+        const bool lane_exact = !(pp < 3.0e38f && ccmax_t < 3.0e38f && pp * ccmax_t <= a.ovf);
+        const float vl = row_ok ? vlane : -kInf;  // rows past n never list a chunk
         const bool force = row_ok && lane_exact;
         const int nch = (nvt + 31) >> 5;
-        __syncwarp();
         if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
 
         uint32_t cmask = 0;  // this lane's candidate chunks of the tile
-        // one 32-column chunk: keys in place (x' with the column in the low 5 bits), their
-        // minimum, the screen, the fold into the row's best key
-        auto proc = [&](float (&v)[32], int ch) {
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ++ch) {
+          float v[32];
+          tmem_ld32(tmem_acc + ch * 32, v);
           const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vl;
-          const float4* cb4 = reinterpret_cast<const float4*>(ccb_w + ch * 32);
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4) {
-            const float4 cb = cb4[q4];
-            const float c4[4] = {cb.x, cb.y, cb.z, cb.w};
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              const int e = q4 * 4 + r;
-              uint32_t kb;
-              asm("lop3.b32 %0, %1, %2, %3, 0xEA;"
-                  : "=r"(kb)
-                  : "r"(__float_as_uint(__fmaf_rn(-2.f, v[e], c4[r]))), "r"(kmask), "r"(static_cast<uint32_t>(e)));
-              v[e] = __uint_as_float(kb);
-            }
+          for (int e = 0; e < 32; ++e) {
+            uint32_t kb;
+            asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(kb) : "r"(__float_as_uint(v[e])), "r"(kmask), "r"(static_cast<uint32_t>(e)));
+            v[e] = __uint_as_float(kb);
           }
           float tt[11];
 #pragma unroll
@@ -331,22 +347,15 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
                                  fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
           const bool cand = force || km <= thr;
           const float kf = cand ? kInf : km;
-          if (kf < best_x) {
-            best_x = kf;
+          if (kf < best_y) {
+            best_y = kf;
             best_c = static_cast<uint32_t>(jt) + ch * 32;
           }
           cmask |= static_cast<uint32_t>(cand) << ch;
-        };
-
-#pragma unroll 1
-        for (int ch = 0; ch < nch; ++ch) {
-          float v0[32];
-          tmem_ld32(tmem_acc + ch * 32, v0);
-          proc(v0, ch);
         }
 
         // candidate chunks of this tile (some pair may be flagged): each goes, with its
-        // accumulators read again from TMEM, to this CTA's list region for the exact
+        // accumulators y (read again from TMEM), to this CTA's list region for the exact
         // second pass; one shared-memory reservation per warp and tile
         if (__any_sync(0xffffffffu, cmask != 0)) {
           uint32_t bal[4];
@@ -391,12 +400,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
       }
       if (!ok) break;
-      // this group's screened minimum of the row: distance and original center index
-      float bestv = __int_as_float(0x7f800000);
+      // this group's screened minimum of the row: distance d = 2 y - B + pp and original
+      // center index
+      float bestv = kInf;
       uint32_t besti = 0xffffffffu;
-      if (row_ok && best_x < kInf) {
-        const uint32_t kb = __float_as_uint(best_x);
-        bestv = fmaxf(__fadd_rn(__uint_as_float(kb & ~31u) - bias, pp), 0.f);
+      if (row_ok && best_y < kInf) {
+        const uint32_t kb = __float_as_uint(best_y);
+        bestv = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(kb & ~31u), -B), pp), 0.f);
         besti = static_cast<uint32_t>(__ldg(a.perm + static_cast<int64_t>(best_c) + (kb & 31u)));
       }
       // merge the four (parity, column half) partial minima of each row
@@ -439,7 +449,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // ------------------------------------------------------------------ host side
 
 constexpr size_t TF_SMEM_LIMIT = 232448;
-constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
+constexpr size_t TF_FIXED =
+    1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + TF_AAUX_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
 
 // Resident A (the row tile, double-buffered) with B-only stages when that leaves room
 // for 3 stages, else streaming (A B) stages.
@@ -469,14 +480,14 @@ int tc_fast_regions(int64_t n) {
 }
 
 template <int KIND>
-static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const TfArgs& args, int grid,
-                               cudaStream_t st) {
+static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& taa,
+                               const CUtensorMap& tba, const TfArgs& args, int grid, cudaStream_t st) {
   auto kern = dist_tc_fast_kernel<KIND>;
   const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   timing_begin(st, "dist_tc_fast_kernel");
-  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, args);
+  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, taa, tba, args);
   e = cudaGetLastError();
   timing_end(st);
   return e;
@@ -504,6 +515,7 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   // screen margin: the rounding of S to the GEMM's output format dominates
   a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-16f);
   a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
+  a.aux_b = j.aux_b;
   a.row_key = j.row_key;
   a.list = j.chunk_list;
   a.sbuf = j.chunk_s;
@@ -516,9 +528,13 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
   if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
-  if (kind == 0) return launch_tf_t<0>(ta, tb, a, grid, j.stream);
-  if (kind == 1) return launch_tf_t<1>(ta, tb, a, grid, j.stream);
-  return launch_tf_t<2>(ta, tb, a, grid, j.stream);
+  CUtensorMap taa, tba;
+  const int64_t mpad = (j.m + TF_BN - 1) / TF_BN * TF_BN;
+  if (!tc_make_tmap_sw32(&taa, j.a_aux, TF_BM, esize, TF_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (!tc_make_tmap_sw32(&tba, j.b_aux_sorted, mpad, esize, TF_BN, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  if (kind == 0) return launch_tf_t<0>(ta, tb, taa, tba, a, grid, j.stream);
+  if (kind == 1) return launch_tf_t<1>(ta, tb, taa, tba, a, grid, j.stream);
+  return launch_tf_t<2>(ta, tb, taa, tba, a, grid, j.stream);
 }
 
 int tf_error_and_clear() {
@@ -576,7 +592,8 @@ __device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long k)
 
 struct EvArgs {
   const unsigned long long* clist;
-  const float* sbuf;
+  const float* sbuf;            // the chunk's accumulators y = y0 - s, y0 = (cc + B) / 2 (0 for a non-finite cc)
+  const float* aux_b;
   unsigned long long region_cap;
   const uint32_t* region_cnt;
   const float* pp;
@@ -660,10 +677,12 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
       cc[u] = jv[u] ? __ldg(a.cc_s + j) : 0.f;
       jo[u] = jv[u] ? static_cast<uint32_t>(__ldg(a.perm + j)) : 0u;
     }
+    const float B = __ldg(a.aux_b);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (skip[u]) continue;  // warp-uniform
-      const float d = exact_d<SROUND>(sv[u], pp[u], cc[u]);
+      const float y0 = cc[u] < 3.0e38f ? 0.5f * __fadd_rn(cc[u], B) : 0.f;
+      const float d = exact_d<SROUND>(y0 - sv[u], pp[u], cc[u]);
       const bool fl = jv[u] && d <= __fmul_rn(a.K, __fadd_rn(pp[u], cc[u]));
       const unsigned bal = __ballot_sync(0xffffffffu, fl);
       if (bal) {
@@ -760,6 +779,7 @@ cudaError_t launch_eval_chunks(const DistJob& j) {
   EvArgs a{};
   a.clist = j.chunk_list;
   a.sbuf = j.chunk_s;
+  a.aux_b = j.aux_b;
   a.region_cap = j.chunk_cap / static_cast<unsigned long long>(j.regions);
   a.region_cnt = j.region_cnt;
   a.pp = static_cast<const float*>(j.pp);
