@@ -10,9 +10,11 @@
 //    tile times to drain its half of an accumulator while the next tile's MMAs proceed;
 //  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
 //    each center tile's norms into shared memory ahead of use;
-//  * per 32-column chunk an epilogue warp forms keys x' = cc + bias - 2 s (one FMA),
-//    replaces the low 5 mantissa bits with the column (one LOP3) and takes the minimum
-//    with a depth-4 tree of 3-way mins;
+//  * one extra 32-byte K block per tile adds y0_j = (cc_j + B)/2 to every accumulator of
+//    column j (B = 1.0625 max pp, centers stored negated), so the MMA yields
+//    y = y0 - s >= 0 directly; per 32-column chunk an epilogue warp replaces the low 5
+//    mantissa bits of y with the column (one LOP3) and takes the minimum with a
+//    depth-4 tree of 3-way mins;
 //  * a chunk in which some pair could meet the cancellation test
 //        d <= K (pp + cc)  <=>  2 s >= (1 - K)(pp + cc)  (up to rounding margins)
 //    -- bounded with the chunk's smallest and largest norm, tight because norms are
@@ -23,8 +25,9 @@
 //  * every other chunk can hold no flagged pair and contributes its key minimum.
 //
 // Labels equal the exact epilogue's wherever the row's top-two distance gap exceeds
-// the screen's resolution (2^-10 (pp + max cc) for fp16 S, 2^-7 for bf16 S).  If the
-// candidate list is full, the row is marked for a complete exact redo.
+// the screen's resolution: 2^-10 (pp + max cc) for fp16 S (2^-7 for bf16 S) plus the
+// key truncation, 2^-16 (max cc + B).  If the candidate list is full, the row is
+// marked for a complete exact redo.
 //
 // All waits are bounded (common.cuh); on expiry the CTA records an error, drains its
 // copies and MMAs, frees TMEM and returns.
