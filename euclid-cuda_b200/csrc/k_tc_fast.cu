@@ -653,8 +653,8 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   unsigned long long cnt = a.region_cnt[r];
   if (cnt > a.region_cap) cnt = a.region_cap;
   const unsigned long long rbase = static_cast<unsigned long long>(r) * a.region_cap;
-  // two entries per iteration: their loads are independent and issue together
-  constexpr int U = 2;
+  // four entries per iteration: their loads are independent and issue together
+  constexpr int U = 4;
   for (unsigned long long t0 = wr; t0 < cnt; t0 += kStride * U) {
     unsigned long long e[U];
     float sv[U];
