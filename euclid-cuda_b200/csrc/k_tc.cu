@@ -2,17 +2,20 @@
 //
 // One persistent CTA per SM walks 128-row tiles of the points.  For each row tile
 // it sweeps every center tile (bn = 64/128/256 centers):
-//   warp 0  : TMA producer, streams (A: 128 x 64 fp16/bf16 | 128 x 32 tf32) and
-//             (B: bn x same) K-blocks into a 4-stage ring of 128B-swizzled smem;
+//   warp 0  : TMA producer; the row tile's A K-blocks (128 x 64 fp16/bf16 | 128 x 32
+//             tf32) stay resident (double-buffered) when they fit, else A streams with
+//             B; B (bn x same) K-blocks stream through a ring of up to 8 stages of
+//             128B-swizzled smem;
 //   warp 1  : tcgen05.mma issuer (one elected lane), M=128 x N=bn x K=16|8 per
 //             instruction, fp32 accumulators double-buffered in TMEM (2*bn columns);
 //             also owns the TMEM allocation;
-//   warps 2-5: epilogue; each thread owns one TMEM lane = one point row.  It reads
-//             32 accumulator columns at a time (tcgen05.ld 32x32b.x32), applies the
+//   warps 2-9: epilogue, 2 per TMEM lane quadrant (each half of the tile's columns);
+//             each thread owns one TMEM lane = one point row.  It reads 32 or 64
+//             accumulator columns at a time (tcgen05.ld 32x32b), applies the
 //             reference's S rounding, forms d = max((pp - 2s) + cc, 0), runs the
 //             cancellation test d <= K (pp + cc) and either stores D or keeps the
-//             running (min, first index) of the row.  Flagged pairs are appended to
-//             a compact list with one atomic per warp (ballot + popc).
+//             running (min, first index) of the row (exact argmin).  Flagged pairs are
+//             appended to a compact list with one atomic per warp (ballot + popc).
 //
 // This replaces the reference's chain  cast -> norms -> cuBLAS GEMM (S in HBM) ->
 // form_mixed_and_list_* (euclidean_kernels_mix.cu:184-316, 322-407) and the WMMA
@@ -37,9 +40,9 @@ constexpr int TC_EPI_WARPS = 8;  // two warps per TMEM lane quadrant, each ownin
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
 constexpr int TC_A_BYTES = TC_BM * 128;  // one K-block of A: 128 rows x 128 bytes
 constexpr int TC_BAR_BYTES = 256;        // mbarriers, TMEM slot, abort flag
-constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 3 * 128 * 4 + 2 * 2 * 128 * 4;  // per-warp staging + row merge
+constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 128 * 4 + 2 * 2 * 128 * 4;  // per-warp center norms + row merge
 
-enum TcMode { TM_ARGMIN = 0, TM_D_F32 = 1, TM_D_F16 = 2, TM_D_BF16 = 3, TM_ARGMIN_FAST = 4 };
+enum TcMode { TM_ARGMIN = 0, TM_D_F32 = 1, TM_D_F16 = 2, TM_D_BF16 = 3 };
 
 struct TcArgs {
   int64_t n, m;
@@ -51,12 +54,8 @@ struct TcArgs {
   int n_ct;     // center tiles
   int64_t n_rt; // row tiles
   const float* pp;
-  const float* cc;    // center norms, in the (possibly sorted) order of the B operand
-  const int* perm;    // sorted position -> original center index (fast argmin), else null
+  const float* cc;    // center norms
   float K;
-  float omk;          // 1 - K (fast screen)
-  float margin;       // fast screen margin, relative to (pp + cc + bias)
-  float ovf;          // fast screen off when pp * max(cc) may overflow the rounded S
   void* D;
   unsigned long long* row_key;
   unsigned long long* list;
@@ -228,8 +227,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    constexpr bool ARGMIN = (MODE == TM_ARGMIN || MODE == TM_ARGMIN_FAST);
-    constexpr bool FAST = (MODE == TM_ARGMIN_FAST);
+    constexpr bool ARGMIN = (MODE == TM_ARGMIN);
     const int ew = warp - 2;             // 0..7
     const int q = warp & 3;              // TMEM lane quadrant this warp may access
     const int half = ew >> 2;            // which half of the tile's columns
@@ -237,32 +235,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int nch = cols >> 5;           // 32-column chunks per warp and tile
     const int row_local = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    float* cc_w = epi + ew * 3 * 128;    // this warp's columns: norms
-    float* ccb_w = cc_w + 128;           //                      norms + bias (fast screen)
-    int* perm_w = reinterpret_cast<int*>(ccb_w + 128);  //      original center index
-    float* mv = epi + TC_EPI_WARPS * 3 * 128;           // row merge: [2][128] minima
+    float* cc_w = epi + ew * 128;        // this warp's columns: norms
+    float* mv = epi + TC_EPI_WARPS * 128;               // row merge: [2][128] minima
     uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 256);  //    [2][128] their columns
     const float K = a.K;
 
     // Center metadata of the next tile this warp will process is loaded one tile ahead
     // (4 columns per lane at most), so the global-load latency overlaps the current tile.
     float pf_cc[4];
-    int pf_perm[4];
     auto prefetch = [&](int64_t rt_next, int ct_next) {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        pf_cc[t] = 0.f;
-        pf_perm[t] = 0;
-      }
+      for (int t = 0; t < 4; ++t) pf_cc[t] = 0.f;
       if (rt_next >= a.n_rt) return;
       const int64_t jw = static_cast<int64_t>(ct_next) * bn + half * cols;
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const int c = lane + 32 * t;
-        if (c < cols && jw + c < a.m) {
-          pf_cc[t] = __ldg(a.cc + jw + c);
-          if constexpr (FAST) pf_perm[t] = __ldg(a.perm + jw + c);
-        }
+        if (c < cols && jw + c < a.m) pf_cc[t] = __ldg(a.cc + jw + c);
       }
     };
 
@@ -275,13 +264,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const float pp = row_ok ? __ldg(a.pp + i) : 0.f;
       float bestv = __int_as_float(0x7f800000);
       uint32_t besti = 0xffffffffu;
-      float bias = 0.f;
-      if constexpr (FAST) {
-        // warp-uniform bias making every screened value non-negative: x' = cc - 2 s + bias >= 0
-        const float ppf = (row_ok && pp < 3.0e38f) ? pp : 0.f;
-        const unsigned mx = __reduce_max_sync(0xffffffffu, __float_as_uint(ppf));
-        bias = __uint_as_float(mx) * 1.0625f + 1e-30f;
-      }
       for (int ct = 0; ct < a.n_ct; ++ct) {
         const uint32_t buf = acc_i & 1u, use = (acc_i >> 1) & 1u;
         const int64_t jw = static_cast<int64_t>(ct) * bn + half * cols;  // first column of this warp
@@ -289,14 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int c = lane + 32 * t;
-          if (c < cols) {
-            const bool cv = jw + c < a.m;
-            cc_w[c] = pf_cc[t];
-            if constexpr (FAST) {
-              ccb_w[c] = cv ? __fadd_rn(pf_cc[t], bias) : 3.0e38f;
-              perm_w[c] = pf_perm[t];
-            }
-          }
+          if (c < cols) cc_w[c] = pf_cc[t];
         }
         __syncwarp();
         if (ct + 1 < a.n_ct)
@@ -305,58 +280,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           prefetch(rt + gridDim.x, 0);
         if (!mbar_wait(&accf[buf], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        bool lane_exact = true;
-        if constexpr (FAST) {
-          // fast screen only when S cannot overflow its rounded format and pp is finite
-          const int64_t remw = a.m - jw;
-          const int lastc = (int)(remw < cols ? remw : cols) - 1;
-          const float ccmax_t = lastc >= 0 ? cc_w[lastc] : 0.f;
-          lane_exact = !(pp < 3.0e38f && pp * ccmax_t <= a.ovf && bias < 3.0e38f);
-        }
 
-        // one 32-column chunk: screen (fast) and / or exact evaluation
+        // one 32-column chunk: the reference's form and flag per pair
         auto process = [&](int ch, float (&v)[32]) {
           const int c0 = ch * 32;
           const int64_t j0 = jw + c0;
           const int64_t remc = a.m - j0;
           const int nvalid = remc <= 0 ? 0 : (remc >= 32 ? 32 : (int)remc);
           const uint32_t colmask = !row_ok ? 0u : (nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u));
-          bool exact = true;
-          if constexpr (FAST) {
-            // keys: x' = cc + bias - 2 s with the low 5 mantissa bits replaced by the column;
-            // their minimum by a depth-4 tree of 3-way mins
-            float kk[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = __fmaf_rn(-2.f, v[e], ccb_w[c0 + e]);
-              kk[e] = __uint_as_float((__float_as_uint(x) & ~31u) | static_cast<uint32_t>(e));
-            }
-            float t[11];
-#pragma unroll
-            for (int u = 0; u < 10; ++u) t[u] = fmin3(kk[3 * u], kk[3 * u + 1], kk[3 * u + 2]);
-            t[10] = fminf(kk[30], kk[31]);
-            const float km = fmin3(fmin3(t[0], t[1], t[2]), fmin3(t[3], t[4], t[5]),
-                                   fmin3(fmin3(t[6], t[7], t[8]), t[9], t[10]));
-            bool cand = lane_exact;
-            if constexpr (FLAG != FL_NONE) {
-              // no pair of this chunk can be flagged unless its smallest x' reaches
-              // max(cc+bias) - (1-K)(pp + min cc) (+ rounding margin); norms are sorted
-              const int lastv = max(0, min(31, nvalid - 1));
-              const float ccmin = cc_w[c0], ccbmax = ccb_w[c0 + lastv];
-              const float thr = ccbmax - a.omk * (pp + ccmin) + (pp + ccbmax) * a.margin;
-              cand = cand || (km <= thr);
-            }
-            exact = __any_sync(0xffffffffu, cand && row_ok);
-            if (!exact && row_ok) {
-              const uint32_t kb = __float_as_uint(km);
-              const float dv = __fadd_rn(__uint_as_float(kb & ~31u) - bias, pp);
-              if (dv < bestv) {
-                bestv = fmaxf(dv, 0.f);
-                besti = static_cast<uint32_t>(perm_w[c0 + (kb & 31u)]);
-              }
-            }
-          }
-          if (exact) {
+          {
             uint32_t fm = 0;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -366,12 +298,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               if constexpr (FLAG == FL_F32) fl = d <= __fmul_rn(K, __fadd_rn(pp, cc));
               if constexpr (ARGMIN) {
                 if (((colmask >> e) & 1u) && !fl) {
-                  if constexpr (FAST) {
-                    const uint32_t jo = static_cast<uint32_t>(perm_w[c0 + e]);
-                    if (d < bestv || (d == bestv && jo < besti)) { bestv = d; besti = jo; }
-                  } else {
-                    if (d < bestv) { bestv = d; besti = static_cast<uint32_t>(j0 + e); }
-                  }
+                  if (d < bestv) { bestv = d; besti = static_cast<uint32_t>(j0 + e); }
                 }
               }
               if (fl) fm |= 1u << e;
@@ -385,7 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 while (fm) {
                   const int e = __ffs(fm) - 1;
                   fm &= fm - 1;
-                  const uint32_t jo = FAST ? static_cast<uint32_t>(perm_w[c0 + e]) : static_cast<uint32_t>(j0 + e);
+                  const uint32_t jo = static_cast<uint32_t>(j0 + e);
                   if (pos < a.list_cap) {
                     a.list[pos] = (static_cast<unsigned long long>(i) << 32) | jo;
                   } else if constexpr (ARGMIN) {
@@ -604,13 +531,8 @@ cudaError_t launch_tc(const DistJob& j) {
   a.n_rt = (j.n + TC_BM - 1) / TC_BM;
   pick_pipeline(a.bn, a.kblocks, &a.nst, &a.a_res);
   a.pp = static_cast<const float*>(j.pp);
-  a.cc = static_cast<const float*>(j.fast_argmin ? j.cc_sorted : j.cc);
-  a.perm = j.fast_argmin ? j.perm : nullptr;
+  a.cc = static_cast<const float*>(j.cc);
   a.K = j.kf;
-  a.omk = 1.f - j.kf;
-  // screen margin: the rounding of S to the GEMM's output format dominates
-  a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-20f);
-  a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
   a.D = j.D;
   a.row_key = j.row_key;
   a.list = j.list;
@@ -624,22 +546,20 @@ cudaError_t launch_tc(const DistJob& j) {
 
   CUtensorMap ta, tb;
   if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TC_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-  if (!tc_make_tmap(&tb, j.fast_argmin ? j.Clow_sorted : j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1))
+  if (!tc_make_tmap(&tb, j.Clow, j.m, j.ldlow, esize, a.bn, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
 
   const bool argmin = (j.D == nullptr);
-  int mode = j.fast_argmin ? TM_ARGMIN_FAST : TM_ARGMIN;
+  int mode = TM_ARGMIN;
   if (!argmin) mode = (s->out == OUT_F16) ? TM_D_F16 : (s->out == OUT_BF16 ? TM_D_BF16 : TM_D_F32);
   const cudaStream_t st = j.stream;
 
 #define TC_CASE1(KIND_, SR_, FL_, MODE_, REC_)                                                      \
   if (kind == KIND_ && s->sround == SR_ && s->flag == FL_ && mode == MODE_ &&                        \
-      ((MODE_ != TM_ARGMIN && MODE_ != TM_ARGMIN_FAST) || s->rec == REC_))                           \
+      (MODE_ != TM_ARGMIN || s->rec == REC_))                                                         \
     return launch_tc_t<KIND_, SR_, FL_, MODE_, REC_>(ta, tb, a, st);
 #define TC_CASE(KIND_, SR_, FL_, MODE_, REC_) TC_CASE1(KIND_, SR_, FL_, MODE_, REC_)
-#define TC_CASE_A(KIND_, SR_, FL_, REC_)         \
-  TC_CASE1(KIND_, SR_, FL_, TM_ARGMIN, REC_)     \
-  TC_CASE1(KIND_, SR_, FL_, TM_ARGMIN_FAST, REC_)
+#define TC_CASE_A(KIND_, SR_, FL_, REC_) TC_CASE1(KIND_, SR_, FL_, TM_ARGMIN, REC_)
 
   // fp16 operands
   TC_CASE(0, SR_F16, FL_F32, TM_D_F32, RC_NONE)      // mix fp16_*
