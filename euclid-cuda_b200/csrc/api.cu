@@ -124,7 +124,7 @@ void timing_end(cudaStream_t st) {
 static inline size_t al(size_t b) { return (b + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hdr, pp, cc, plow, clow, clow_s, cc_s, perm, list, key, val64, idx64, rcnt, redo, clist, cs, aaux, baux, total;
+  size_t hdr, pp, cc, plow, clow, clow_s, cc_s, perm, list, key, val64, idx64, rcnt, redo, clist, cs, baux, total;
   unsigned long long cap, ccap;
   int ldlow;
 };
@@ -155,8 +155,7 @@ static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, boo
       L.perm = off; off += al(mpad * 4);
       L.rcnt = off; off += al(static_cast<size_t>(kMaxRegions) * 4);
       L.redo = off; off += al(static_cast<size_t>(n));
-      L.aaux = off; off += al(128 * 32);   // extra K block of the screening MMA: 32 bytes per row
-      L.baux = off; off += al(mpad * 32);
+      L.baux = off; off += al(mpad * 32);  // extra K block of the screening MMA: 32 bytes per center
     }
   }
   L.cap = 0;
@@ -274,27 +273,24 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.chunk_s = L.cs ? reinterpret_cast<float*>(w + L.cs) : nullptr;
   j.chunk_cap = L.ccap;
   j.regions = j.fast_argmin ? tc_fast_regions(n) : 0;
-  j.a_aux = L.aaux ? w + L.aaux : nullptr;
   j.b_aux_sorted = L.baux ? w + L.baux : nullptr;
-  j.ppmax_bits = reinterpret_cast<unsigned int*>(w + L.hdr + 8);
-  j.aux_b = reinterpret_cast<float*>(w + L.hdr + 12);
   j.aux_e = reinterpret_cast<int*>(w + L.hdr + 16);
   j.region_cnt = L.rcnt ? reinterpret_cast<uint32_t*>(w + L.rcnt) : nullptr;
   j.redo = L.redo ? w + L.redo : nullptr;
   j.stream = st;
   if (j.fast_argmin && j.regions > kMaxRegions) return fail(EUC_ERR_UNSUPPORTED, "more SMs than list regions");
+  // the screening kernel prepares the points itself where it can (no low-precision copy)
+  j.fused_rows = j.fast_argmin && tc_fast_can_fuse_rows(j);
 
   cudaError_t e = cudaMemsetAsync(j.count, 0, 8, st);
   if (e == cudaSuccess && j.fast_argmin) e = cudaMemsetAsync(j.redo, 0, static_cast<size_t>(n), st);
-  if (e == cudaSuccess && j.fast_argmin) e = cudaMemsetAsync(j.ppmax_bits, 0, 4, st);
   if (e == cudaSuccess && o.tile_counts) {
     const int64_t nt = ((n + o.tile_T - 1) / o.tile_T) * j.tiles_j;
     e = cudaMemsetAsync(o.tile_counts, 0, static_cast<size_t>(nt) * 4, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "memset");
-  e = launch_prep(j, true, is_tc(s));
+  if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
-  if (e == cudaSuccess && j.fast_argmin) e = launch_aux_params(j);
   if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
   if (e != cudaSuccess) return cuda_fail(e, "prep");
   e = j.fast_argmin ? launch_tc_fast(j) : (is_tc(s) ? launch_tc(j) : launch_simt(j));

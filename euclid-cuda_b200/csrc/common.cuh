@@ -18,6 +18,7 @@ enum DevErr : int {
   DEV_TIMEOUT_MMA = 2,
   DEV_TIMEOUT_EPILOGUE = 3,
   DEV_BAD_TMEM = 4,
+  DEV_TIMEOUT_ROWS = 5,
 };
 
 // A wait that has not completed after this many nanoseconds is treated as a hang:
@@ -93,6 +94,11 @@ __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, u
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+// Hint: bring a global range into L2 (16-byte aligned, size % 16 == 0); nothing waits on it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes)
+               : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -108,14 +108,14 @@ struct DistJob {
   int regions;
   uint32_t* region_cnt;          // entries per region (written by the screening kernel)
   uint8_t* redo;                 // rows whose candidates did not fit: recomputed whole
-  // fast argmin: the MMA also adds (cc_j + B) / 2 per column through one extra K block
-  // (32-byte rows): a_aux = 128 rows of [2^E, 2^E, 2^E, 0...], b_aux (sorted) = the
-  // three-part split of (cc_j + B) / 2^(E+1); B = 1.0625 max pp keeps every value >= 0
-  void* a_aux;
+  // fast argmin: the MMA also adds (cc_j + Br_i) / 2 to pair (i, j) through one extra
+  // K block (32-byte rows, aux.cuh); b_aux holds the sorted centers' rows, the point
+  // rows are built in the screening kernel from pp
   void* b_aux_sorted;
-  unsigned int* ppmax_bits;      // max finite pp (bits), reduced on the device
-  float* aux_b;                  // B (device scalar)
   int* aux_e;                    // E (device scalar)
+  // fast argmin: the screening kernel reads the fp32 points itself (rounding, norms and
+  // the extra-K rows in shared memory) instead of a prepared low-precision copy
+  bool fused_rows;
   cudaStream_t stream;
 };
 
@@ -133,8 +133,8 @@ bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int 
                   bool is_bf16);
 bool tc_make_tmap_sw32(CUtensorMap* map, const void* base, int64_t rows, int esize, int box_rows, bool is_f32,
                        bool is_bf16);
-// fast argmin: B and E from max pp and max cc, the A-side extra K block
-cudaError_t launch_aux_params(const DistJob& j);
+// whether the screening kernel can prepare the points itself for this job
+bool tc_fast_can_fuse_rows(const DistJob& j);
 cudaError_t launch_simt(const DistJob& j);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);

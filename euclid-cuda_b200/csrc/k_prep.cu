@@ -14,6 +14,7 @@
 // row r's slab into its running norm and the slab is written back out as the low copy.
 #include "common.cuh"
 #include "engine.h"
+#include "aux.cuh"
 
 #include <type_traits>
 #include <algorithm>
@@ -278,174 +279,85 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
   return cudaErrorNotSupported;
 }
 
-// Stable sort of the centers by norm (ties kept in index order), for the fast argmin
-// screen: rank_j = #{i : key_i < key_j or (key_i == key_j and i < j)}, key = norm (NaN
-// as +inf).  Each thread ranks one center against all others staged through shared
-// memory, then moves its low-precision row, norm and original index to its rank.
-// ------------------------------------------------ fast argmin: the extra K block
-// The screening MMA adds y0_j = (cc_j + B) / 2 to every accumulator of column j through
-// one extra 32-byte K block: A side 2^E in its first three entries, B side the value
-// split in three parts of the operand type (each part the rounding of what the earlier
-// parts left), scaled by 2^-E so that it fits fp16's range.  Products of the parts with
-// 2^E are exact, so the MMA adds y0_j to within the type's precision cubed.
-
-__global__ void max_finite_kernel(const float* __restrict__ v, int64_t n, unsigned int* __restrict__ out) {
-  float mx = 0.f;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float x = v[i];
-    if (x < 3.0e38f && x > mx) mx = x;  // skips inf and NaN
-  }
-  const unsigned int m = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));  // non-negative: bits order as values
-  if ((threadIdx.x & 31) == 0) atomicMax(out, m);
-}
-
-template <int KIND> __device__ __forceinline__ uint32_t low_bits(float v);
-template <> __device__ __forceinline__ uint32_t low_bits<0>(float v) { return __half_as_ushort(__float2half_rn(v)); }
-template <> __device__ __forceinline__ uint32_t low_bits<1>(float v) {
-  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
-}
-template <> __device__ __forceinline__ uint32_t low_bits<2>(float v) {
-  uint32_t b;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b) : "f"(v));
-  return b;
-}
-template <int KIND> __device__ __forceinline__ float low_value(uint32_t b);
-template <> __device__ __forceinline__ float low_value<0>(uint32_t b) {
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
-}
-template <> __device__ __forceinline__ float low_value<1>(uint32_t b) {
-  return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b)));
-}
-template <> __device__ __forceinline__ float low_value<2>(uint32_t b) { return __uint_as_float(b); }
-
-// 32 bytes of an extra-K row: three parts of v, then zeros
-template <int KIND> __device__ __forceinline__ void aux_row(float v, uint4* dst) {
-  uint32_t p[3];
-  float r = v;
-#pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    p[k] = low_bits<KIND>(r);
-    r = r - low_value<KIND>(p[k]);
-  }
-  uint4 lo, hi = make_uint4(0u, 0u, 0u, 0u);
-  if constexpr (KIND == 2) {
-    lo = make_uint4(p[0], p[1], p[2], 0u);
-  } else {
-    lo = make_uint4(p[0] | (p[1] << 16), p[2], 0u, 0u);
-  }
-  dst[0] = lo;
-  dst[1] = hi;
-}
-
+// ------------------------------------------------ fast argmin: sorted centers
+// Stable rank sort of the centers by norm (ties kept in index order, NaN as +inf):
+// rank_j = #{i : key_i < key_j or (key_i == key_j and i < j)}.  One warp per center,
+// its lanes counting over the norms staged in shared memory.  Every block also reduces
+// the largest finite norm (all blocks see all norms, so they agree) and derives E of the
+// extra K block (aux.cuh).  Sorted position r receives the norm, the original index, the
+// low-precision row NEGATED (the screening MMA forms y0 - s) and the center's extra-K
+// row [c0, c1, c2, 2^E, 2^E, 2^E] (all zero for a norm that is not finite); the padded
+// positions m .. mpad-1 get +inf in c0, so their keys never win.
 template <int KIND>
-__global__ void __launch_bounds__(256) aux_params_kernel(const float* __restrict__ cc, int m,
-                                                          const unsigned int* __restrict__ ppmax_bits,
-                                                          float* __restrict__ aux_b, int* __restrict__ aux_e,
-                                                          uint4* __restrict__ a_aux) {
-  __shared__ unsigned int s_max;
-  __shared__ int s_e;
-  if (threadIdx.x == 0) s_max = 0u;
-  __syncthreads();
-  float mc = 0.f;
-  for (int j = threadIdx.x; j < m; j += blockDim.x) {
-    const float c = cc[j];
-    if (c < 3.0e38f && c > mc) mc = c;
-  }
-  const unsigned int wm = __reduce_max_sync(0xffffffffu, __float_as_uint(mc));
-  if ((threadIdx.x & 31) == 0) atomicMax(&s_max, wm);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const float B = __uint_as_float(*ppmax_bits) * 1.0625f + 1e-30f;
-    int e = 0;
-    if (KIND == 0) {  // fp16 parts must stay below its largest finite value
-      const float top = 0.5f * (__uint_as_float(s_max) + B);
-      while (e < 120 && top > ldexpf(32768.f, e)) ++e;
-    }
-    *aux_b = B;
-    *aux_e = e;
-    s_e = e;
-  }
-  __syncthreads();
-  const float a = ldexpf(1.f, s_e);
-  for (int r = threadIdx.x; r < 128; r += blockDim.x) {
-    uint4 lo, hi = make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t ab = low_bits<KIND>(a);
-    if constexpr (KIND == 2) {
-      lo = make_uint4(ab, ab, ab, 0u);
-    } else {
-      lo = make_uint4(ab | (ab << 16), ab, 0u, 0u);
-    }
-    a_aux[2 * r] = lo;
-    a_aux[2 * r + 1] = hi;
-  }
-}
-
-cudaError_t launch_aux_params(const DistJob& j) {
-  const int kind = (j.spec->gemm == G_TC_F16) ? 0 : (j.spec->gemm == G_TC_BF16 ? 1 : 2);
-  const int blocks = static_cast<int>(std::min<int64_t>((j.n + 255) / 256, static_cast<int64_t>(num_sms()) * 4));
-  max_finite_kernel<<<blocks, 256, 0, j.stream>>>(static_cast<const float*>(j.pp), j.n, j.ppmax_bits);
-  const float* cc = static_cast<const float*>(j.cc);
-  const int m = static_cast<int>(j.m);
-  uint4* aa = static_cast<uint4*>(j.a_aux);
-  if (kind == 0) aux_params_kernel<0><<<1, 256, 0, j.stream>>>(cc, m, j.ppmax_bits, j.aux_b, j.aux_e, aa);
-  else if (kind == 1) aux_params_kernel<1><<<1, 256, 0, j.stream>>>(cc, m, j.ppmax_bits, j.aux_b, j.aux_e, aa);
-  else aux_params_kernel<2><<<1, 256, 0, j.stream>>>(cc, m, j.ppmax_bits, j.aux_b, j.aux_e, aa);
-  return cudaGetLastError();
-}
-
-// Stable rank sort of the centers by norm (NaN last).  Sorted position r receives the
-// norm, the original index, the low-precision row NEGATED (the screening MMA forms
-// y0 - s) and the extra-K row of y0 = (cc + B) / 2 (zero for a norm that is not finite).
-template <int KIND>
-__global__ void __launch_bounds__(256) sort_centers_kernel(const float* __restrict__ cc, int m,
+__global__ void __launch_bounds__(256) sort_centers_kernel(const float* __restrict__ cc, int m, int mpad,
                                                            const uint4* __restrict__ low, int row_u4,
                                                            float* __restrict__ cc_s, int* __restrict__ perm,
-                                                           uint4* __restrict__ low_s, const float* __restrict__ aux_b,
-                                                           const int* __restrict__ aux_e, uint4* __restrict__ b_aux) {
-  __shared__ float tile[1024];
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+                                                           uint4* __restrict__ low_s, int* __restrict__ aux_e,
+                                                           uint4* __restrict__ b_aux) {
+  constexpr int SLAB = 2048;
+  __shared__ float tile[SLAB];
+  __shared__ unsigned int s_max;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x * 8 + warp;
+  const float kInf = __int_as_float(0x7f800000);
   float kj = 0.f;
   if (j < m) {
     kj = cc[j];
-    if (kj != kj) kj = __int_as_float(0x7f800000);
+    if (kj != kj) kj = kInf;
   }
+  if (threadIdx.x == 0) s_max = 0u;
   int rank = 0;
-  for (int base = 0; base < m; base += 1024) {
+  float mc = 0.f;
+  for (int base = 0; base < m; base += SLAB) {
     __syncthreads();
-    for (int t = threadIdx.x; t < 1024 && base + t < m; t += blockDim.x) {
-      float v = cc[base + t];
-      tile[t] = (v != v) ? __int_as_float(0x7f800000) : v;
+    for (int t = threadIdx.x; t < SLAB && base + t < m; t += blockDim.x) {
+      const float v = cc[base + t];
+      if (v < 3.0e38f && v > mc) mc = v;  // skips inf and NaN
+      tile[t] = (v != v) ? kInf : v;
     }
     __syncthreads();
-    const int lim = min(1024, m - base);
+    const int lim = min(SLAB, m - base);
     if (j < m) {
-      for (int t = 0; t < lim; ++t) {
+      for (int t = lane; t < lim; t += 32) {
         const float ki = tile[t];
         const int i = base + t;
         rank += (ki < kj) || (ki == kj && i < j);
       }
     }
   }
-  // padded positions m .. 255 of the last tile: y0 = +inf, so their keys never win
-  if (j >= m && j < ((m + 255) & ~255)) {
+  rank = __reduce_add_sync(0xffffffffu, rank);
+  const unsigned int wm = __reduce_max_sync(0xffffffffu, __float_as_uint(mc));  // non-negative: bits order as values
+  if (lane == 0) atomicMax(&s_max, wm);
+  __syncthreads();
+  const int E = aux_exponent<KIND>(__uint_as_float(s_max));
+  if (blockIdx.x == 0 && threadIdx.x == 0) *aux_e = E;
+  if (j >= m && j < mpad && lane == 0) {
     const uint32_t inf_bits = (KIND == 2) ? 0x7f800000u : (KIND == 1 ? 0x7f80u : 0x7c00u);
     b_aux[2 * static_cast<int64_t>(j)] = make_uint4(inf_bits, 0u, 0u, 0u);
     b_aux[2 * static_cast<int64_t>(j) + 1] = make_uint4(0u, 0u, 0u, 0u);
   }
   if (j < m) {
     const float c = cc[j];
-    cc_s[rank] = c;
-    perm[rank] = j;
     const uint4* src = low + static_cast<int64_t>(j) * row_u4;
     uint4* dst = low_s + static_cast<int64_t>(rank) * row_u4;
     const uint32_t neg = (KIND == 2) ? 0x80000000u : 0x80008000u;
-    for (int t = 0; t < row_u4; ++t) {
+    for (int t = lane; t < row_u4; t += 32) {
       const uint4 w = src[t];
       dst[t] = make_uint4(w.x ^ neg, w.y ^ neg, w.z ^ neg, w.w ^ neg);
     }
-    const float y0 = c < 3.0e38f ? ldexpf(0.5f * (c + *aux_b), -*aux_e) : 0.f;
-    aux_row<KIND>(y0, b_aux + 2 * static_cast<int64_t>(rank));
+    if (lane == 0) {
+      cc_s[rank] = c;
+      perm[rank] = j;
+      uint32_t e[6] = {0u, 0u, 0u, 0u, 0u, 0u};
+      if (c < 3.0e38f && E < kAuxNoScreen) {
+        split3<KIND>(ldexpf(0.5f * c, -E), e);
+        e[3] = e[4] = e[5] = low_bits<KIND>(ldexpf(1.f, E));
+      }
+      uint4 lo, hi;
+      aux_pack<KIND>(e, lo, hi);
+      b_aux[2 * static_cast<int64_t>(rank)] = lo;
+      b_aux[2 * static_cast<int64_t>(rank) + 1] = hi;
+    }
   }
 }
 
@@ -454,17 +366,18 @@ cudaError_t launch_sort_centers(const DistJob& j) {
   const int es = (kind == 2) ? 4 : 2;
   const int row_u4 = j.ldlow * es / 16;
   const int m = static_cast<int>(j.m);
-  const unsigned grid = static_cast<unsigned>((m + 255) / 256);  // also covers the padded positions
+  const int mpad = (m + 255) & ~255;
+  const unsigned grid = static_cast<unsigned>(mpad / 8);  // one warp per sorted position, padding included
   const float* cc = static_cast<const float*>(j.cc);
   const uint4* low = static_cast<const uint4*>(j.Clow);
   uint4* low_s = static_cast<uint4*>(j.Clow_sorted);
   uint4* ba = static_cast<uint4*>(j.b_aux_sorted);
   if (kind == 0)
-    sort_centers_kernel<0><<<grid, 256, 0, j.stream>>>(cc, m, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_b, j.aux_e, ba);
+    sort_centers_kernel<0><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
   else if (kind == 1)
-    sort_centers_kernel<1><<<grid, 256, 0, j.stream>>>(cc, m, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_b, j.aux_e, ba);
+    sort_centers_kernel<1><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
   else
-    sort_centers_kernel<2><<<grid, 256, 0, j.stream>>>(cc, m, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_b, j.aux_e, ba);
+    sort_centers_kernel<2><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
   return cudaGetLastError();
 }
 

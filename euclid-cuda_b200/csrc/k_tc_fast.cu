@@ -10,11 +10,15 @@
 //    tile times to drain its half of an accumulator while the next tile's MMAs proceed;
 //  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
 //    each center tile's norms into shared memory ahead of use;
-//  * one extra 32-byte K block per tile adds y0_j = (cc_j + B)/2 to every accumulator of
-//    column j (B = 1.0625 max pp, centers stored negated), so the MMA yields
+//  * one extra 32-byte K block (aux.cuh) adds y0 = (cc_j + Br_i)/2 to the accumulator of
+//    pair (i, j) (Br_i = 1.0625 pp_i, centers stored negated), so the MMA yields
 //    y = y0 - s >= 0 directly; per 32-column chunk an epilogue warp replaces the low 5
 //    mantissa bits of y with the column (one LOP3) and takes the minimum with a
 //    depth-4 tree of 3-way mins;
+//  * two row warps build each row tile's extra-K rows and its norms; for the fp16/bf16
+//    operators whose norms are those of the rounded values they also read the fp32
+//    points themselves (FUSED): round, accumulate the norm in dimension order and write
+//    the 128B-swizzled A tile, so the points are never staged in HBM;
 //  * a chunk in which some pair could meet the cancellation test
 //        d <= K (pp + cc)  <=>  2 s >= (1 - K)(pp + cc)  (up to rounding margins)
 //    -- bounded with the chunk's smallest and largest norm, tight because norms are
@@ -26,14 +30,15 @@
 //
 // Labels equal the exact epilogue's wherever the row's top-two distance gap exceeds
 // the screen's resolution: 2^-10 (pp + max cc) for fp16 S (2^-7 for bf16 S) plus the
-// key truncation, 2^-16 (max cc + B).  If the candidate list is full, the row is
-// marked for a complete exact redo.
+// key truncation, 2^-16 (max cc + Br).  If the candidate list is full, or the row's
+// norm does not fit the extra K block, the row is marked for a complete exact redo.
 //
 // All waits are bounded (common.cuh); on expiry the CTA records an error, drains its
 // copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
 #include "engine.h"
 #include "direct.cuh"
+#include "aux.cuh"
 
 #include <cudaTypedefs.h>
 #include <algorithm>
@@ -48,13 +53,16 @@ static __device__ int s_tf_err;
 constexpr int TF_BM = 128;
 constexpr int TF_BN = 256;
 constexpr int TF_EPI_WARPS = 16;  // 4 groups (b, column half) x 4 TMEM lane quadrants
-constexpr int TF_THREADS = (2 + TF_EPI_WARPS) * 32;
+constexpr int TF_ROW_WARPS = 2;   // row preparation: one thread per two rows of the tile
+constexpr int TF_ROW_THREADS = TF_ROW_WARPS * 32;
+constexpr int TF_THREADS = (2 + TF_EPI_WARPS + TF_ROW_WARPS) * 32;
 constexpr int TF_A_KB = TF_BM * 128;  // one 128-row x 128-byte K block of A
 constexpr int TF_B_KB = TF_BN * 128;  // one 256-row x 128-byte K block of B
 constexpr int TF_SLOTS = 4;             // center-metadata ring
 constexpr int TF_BAUX_BYTES = TF_BN * 32;  // the tile's extra-K rows (32 bytes each)
 constexpr int TF_META_BYTES = TF_BAUX_BYTES + TF_BN * 4;  // + the tile's sorted center norms
-constexpr int TF_AAUX_BYTES = TF_BM * 32;
+constexpr int TF_AAUX_BYTES = TF_BM * 32;       // per A buffer: the rows' extra-K rows
+constexpr int TF_ROWBUF_BYTES = 2 * TF_BM * 4;  // per A buffer: pp and Br of each row
 constexpr int TF_BAR_BYTES = 512;
 constexpr int TF_EPI_BYTES = 2 * 4 * TF_BM * 4;  // row merge
 
@@ -62,11 +70,13 @@ struct TfArgs {
   int64_t n, m;
   int kblocks, nst, a_res, n_ct;
   int64_t n_rt;
-  const float* pp;
+  float* pp;          // point norms (written here with FUSED)
+  const float* X;     // FUSED: the fp32 points, dim % 4 == 0, 16-byte aligned
+  int dim;
   const float* ccs;   // norms, sorted, padded to whole 256-center tiles
   const int* perm;    // sorted position -> original index, padded
   float omk, margin, ovf;
-  const float* aux_b;           // B of the extra K block (device scalar)
+  const int* aux_e;             // E of the extra K block (device scalar)
   unsigned long long* row_key;
   unsigned long long* list;     // candidate chunks: region r = list + r * region_cap
   float* sbuf;                  // their 32 accumulator values, same index
@@ -75,11 +85,61 @@ struct TfArgs {
   uint8_t* redo;
 };
 
+// FUSED row preparation of one point row: its fp32 values rounded to the operand type
+// (fp16 / bf16, round to nearest even) into the A buffer, K-major with the 128-byte
+// swizzle the MMA descriptor names (16-byte chunk q of row r in K block kb at
+// kb * 16K + (r / 8) * 1024 + (r % 8) * 128 + ((q ^ r % 8) * 16)), and its norm: fused
+// multiply-adds of the rounded values in dimension order, rounded to the operand type
+// (the NM_LOW_F16 / NM_LOW_BF16 recipes of the standalone preparation).  Rows past n and
+// dimensions past dim are zeros.
 template <int KIND>
+__device__ __forceinline__ float fused_row(const float* __restrict__ xr, int dim, int kblocks, uint8_t* sA, int r,
+                                           bool valid) {
+  static_assert(KIND == 0 || KIND == 1, "fp16 / bf16 operands");
+  float acc = 0.f;
+  uint8_t* rowp = sA + (r >> 3) * 1024 + (r & 7) * 128;
+  const int sw = r & 7;
+  const int d4 = valid ? (dim >> 2) : 0;
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  for (int kb = 0; kb < kblocks; ++kb) {
+    float4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int q = kb * 16 + u;
+      v[u] = q < d4 ? __ldg(x4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint8_t* kp = rowp + kb * TF_A_KB;
+#pragma unroll
+    for (int u = 0; u < 16; u += 2) {
+      const float x[8] = {v[u].x, v[u].y, v[u].z, v[u].w, v[u + 1].x, v[u + 1].y, v[u + 1].z, v[u + 1].w};
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float lo, hi;
+        if constexpr (KIND == 0) {
+          const __half2 t = __floats2half2_rn(x[2 * h], x[2 * h + 1]);
+          w[h] = *reinterpret_cast<const uint32_t*>(&t);
+          lo = __low2float(t);
+          hi = __high2float(t);
+        } else {
+          const __nv_bfloat162 t = __floats2bfloat162_rn(x[2 * h], x[2 * h + 1]);
+          w[h] = *reinterpret_cast<const uint32_t*>(&t);
+          lo = __low2float(t);
+          hi = __high2float(t);
+        }
+        acc = __fmaf_rn(lo, lo, acc);
+        acc = __fmaf_rn(hi, hi, acc);
+      }
+      *reinterpret_cast<uint4*>(kp + (((u >> 1) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  return KIND == 0 ? round_f16(acc) : round_bf16(acc);
+}
+
+template <int KIND, bool FUSED>
 __global__ void __launch_bounds__(TF_THREADS, 1)
     dist_tc_fast_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmAaux, const __grid_constant__ CUtensorMap tmBaux,
-                        const TfArgs a) {
+                        const __grid_constant__ CUtensorMap tmBaux, const TfArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = a.nst;
@@ -89,8 +149,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const uint32_t stage_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);  // B  |  A B
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
   uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x (256 extra-K rows, 256 sorted norms)
-  uint8_t* aaux = meta + TF_SLOTS * TF_META_BYTES; // the A side of the extra K block (resident)
-  uint64_t* full = reinterpret_cast<uint64_t*>(aaux + TF_AAUX_BYTES);
+  uint8_t* aaux = meta + TF_SLOTS * TF_META_BYTES; // per A buffer: the A side of the extra K block
+  float* rowbuf = reinterpret_cast<float*>(aaux + 2 * TF_AAUX_BYTES);  // per A buffer: pp[128], Br[128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(rowbuf) + 2 * TF_ROWBUF_BYTES);
   uint64_t* empty = full + NST;
   uint64_t* afull = empty + NST;
   uint64_t* aempty = afull + 2;
@@ -98,8 +159,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   uint64_t* acce = accf + 2;     // per tile parity: the accumulator was read
   uint64_t* metaf = acce + 2;
   uint64_t* metae = metaf + TF_SLOTS;
-  uint64_t* auxf = metae + TF_SLOTS;
-  uint64_t* drain = auxf + 1;
+  uint64_t* pempty = metae + TF_SLOTS;  // per A buffer: every epilogue warp has read its rows' pp, Br
+  uint64_t* drain = pempty + 2;
   uint64_t* mfull = drain + 1;   // row merge: groups 1..3 have published their row minima
   uint64_t* mdone = mfull + 1;   // row merge: group 0 has consumed them
   unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
@@ -116,9 +177,12 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    // afull: the row warps' arrivals, plus the producer's A copy when A comes by TMA
+    const uint32_t afull_count = TF_ROW_THREADS + ((!FUSED && a_res) ? 1u : 0u);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&afull[s], 1);
+      mbar_init(&afull[s], afull_count);
       mbar_init(&aempty[s], 1);
+      mbar_init(&pempty[s], TF_EPI_WARPS);
       mbar_init(&accf[s], 1);
       mbar_init(&acce[s], TF_EPI_WARPS / 2);
     }
@@ -126,7 +190,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&metaf[s], 1);
       mbar_init(&metae[s], TF_EPI_WARPS / 2);
     }
-    mbar_init(auxf, 1);
     mbar_init(drain, 1);
     mbar_init(mfull, TF_EPI_WARPS - 4);
     mbar_init(mdone, 4);
@@ -136,9 +199,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tmA);
+    if (!FUSED) prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    prefetch_tmap(&tmAaux);
     prefetch_tmap(&tmBaux);
   }
   tc_fence_before();
@@ -153,12 +215,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       uint32_t issued_mask = 0, last_phase = 0, a_issued = 0, a_last = 0, m_issued = 0, m_last = 0;
       bool ok = true;
       const int kelems = (KIND == 2) ? 32 : 64;
-      mbar_arrive_expect_tx(auxf, TF_AAUX_BYTES);
-      tma_load_2d(aaux, &tmAaux, auxf, 0, 0);
       for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const int row0 = static_cast<int>(rt * TF_BM);
-        if (a_res) {
+        if (!FUSED && a_res) {
           if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&afull[abuf], a_bytes);
           uint8_t* sA = smem + abuf * a_bytes;
@@ -203,7 +263,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         if (a_issued & (1u << s)) mbar_wait(&afull[s], (a_last >> s) & 1u, &no_abort);
       for (int s = 0; s < TF_SLOTS; ++s)
         if (m_issued & (1u << s)) mbar_wait(&metaf[s], (m_last >> s) & 1u, &no_abort);
-      mbar_wait(auxf, 0, &no_abort);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -211,14 +270,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
       constexpr uint32_t idesc = umma_idesc(fmt, 128, TF_BN);
       uint32_t stage = 0, phase = 0, t = 0, rt_i = 0;
-      bool ok = mbar_wait(auxf, 0, abort_flag);
-      const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux));
+      bool ok = true;
       for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
-        if (a_res) {
-          if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
-        }
+        const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux + abuf * TF_AAUX_BYTES));
+        // the row tile's extra-K rows (and its resident A)
+        if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
         for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
           const uint32_t b = t & 1u, use = (t >> 1) & 1u;
           if (!mbar_wait(&acce[b], use ^ 1u, abort_flag)) { ok = false; break; }
@@ -256,7 +314,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           }
           umma_commit(&accf[b]);
         }
-        if (a_res && ok) umma_commit(&aempty[abuf]);
+        if (ok) umma_commit(&aempty[abuf]);
       }
       if (!ok) {
         *abort_flag = 1;
@@ -266,11 +324,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort);
     }
-  } else {
+  } else if (warp < 2 + TF_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
-    // The accumulators hold y = (cc + B) / 2 - s >= 0 (the extra K block adds the first
-    // term), so a chunk's smallest distance is its smallest y: keys are y with the
-    // column in the low 5 mantissa bits, reduced with 3-way mins.
+    // The accumulators hold y = (cc + Br) / 2 - s >= 0 (the extra K block adds the first
+    // term), so a row's smallest distance in a chunk is its smallest y: keys are y with
+    // the column in the low 5 mantissa bits, reduced with 3-way mins.
     const int ew = warp - 2;            // 0..15
     const int q = warp & 3;             // TMEM lane quadrant
     const int g = ew >> 2;              // group: tile parity b = g >> 1, column half hc = g & 1
@@ -282,13 +340,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 4 * TF_BM);  //            [4][128] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
-    const float B = __ldg(a.aux_b);
     // screen: a pair can only be flagged (d <= K (pp + cc)) where
-    //   y <= (cc + B - (1 - K)(pp + cc)) / 2,
+    //   y <= (cc + Br - (1 - K)(pp + cc)) / 2,
     // so a chunk is a candidate when its smallest y <= thr = U_c + V, with
-    //   U_c = ((max cc + B)(1 + margin) - (1 - K) min cc) / 2 over the chunk,
-    //   V   = pp (margin - (1 - K)) / 2 per row
-    const float kv = 0.5f * (a.margin - a.omk);
+    //   U_c = (max cc (1 + margin) - (1 - K) min cc) / 2 over the chunk,
+    //   V   = (Br (1 + margin) + pp (margin - (1 - K))) / 2 per row
     // ~31 in a register the compiler cannot fold, so that the column insertion below is
     // one three-input logic op per element
     uint32_t kmask;
@@ -298,9 +354,15 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     bool ok = true;
     for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
       const int64_t i = rt * TF_BM + row_local;
-      const bool row_ok = i < a.n;
-      const float pp = row_ok ? __ldg(a.pp + i) : 0.f;
-      const float vlane = pp * kv;
+      // the row's norm and Br from the row warps (Br NaN: past n, or redone whole)
+      const uint32_t abuf = rt_i & 1u;
+      if (!mbar_wait(&afull[abuf], (rt_i >> 1) & 1u, abort_flag)) { ok = false; break; }
+      const float pp = rowbuf[abuf * 2 * TF_BM + row_local];
+      const float br = rowbuf[abuf * 2 * TF_BM + TF_BM + row_local];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[abuf]);
+      const bool row_ok = i < a.n && br == br;
+      const float vlane = 0.5f * __fmaf_rn(br, 1.f + a.margin, pp * (a.margin - a.omk));
       // best screened key of the row: y with its column in the low 5 bits, and the first
       // sorted column of its chunk
       float best_y = kInf;
@@ -318,7 +380,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         float u_own = 0.f;  // lane L < 4: U of chunk L
         if (lane < 4 && lane * 32 < nvt) {
           const int last = min(lane * 32 + 31, nvt - 1);
-          u_own = 0.5f * (__fadd_rn(mcc[last], B) * (1.f + a.margin) - a.omk * mcc[lane * 32]);
+          u_own = 0.5f * (mcc[last] * (1.f + a.margin) - a.omk * mcc[lane * 32]);
         }
         const float ccmax_t = nvt > 0 ? mcc[nvt - 1] : 0.f;
         // rows whose S may overflow its rounded format, or whose norms (or this tile's)
@@ -403,13 +465,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
       }
       if (!ok) break;
-      // this group's screened minimum of the row: distance d = 2 y - B + pp and original
+      // this group's screened minimum of the row: distance d = 2 y - Br + pp and original
       // center index
       float bestv = kInf;
       uint32_t besti = 0xffffffffu;
       if (row_ok && best_y < kInf) {
         const uint32_t kb = __float_as_uint(best_y);
-        bestv = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(kb & ~31u), -B), pp), 0.f);
+        bestv = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(kb & ~31u), -br), pp), 0.f);
         besti = static_cast<uint32_t>(__ldg(a.perm + static_cast<int64_t>(best_c) + (kb & 31u)));
       }
       // merge the four (parity, column half) partial minima of each row
@@ -437,6 +499,78 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       *abort_flag = 1;
       if (lane == 0) atomicExch(&s_tf_err, DEV_TIMEOUT_EPILOGUE);
     }
+  } else {
+    // ------------------------------------------------------------ row preparation
+    // Thread c owns rows c and c + 64 of each row tile: their pp and Br for the epilogue
+    // and their extra-K rows [2^E, 2^E, 2^E, parts of Br / 2 * 2^-E] for the MMA; with
+    // FUSED also the rows of A and pp itself.  A row whose norm is not finite or does
+    // not fit the extra K block gets a zero row term and is marked for the exact redo.
+    const int c = threadIdx.x - (2 + TF_EPI_WARPS) * 32;
+    const int E = __ldg(a.aux_e);
+    const bool screen = E < kAuxNoScreen;
+    const float sc = screen ? ldexpf(1.f, -E) : 0.f;
+    const uint32_t te = screen ? low_bits<KIND>(ldexpf(1.f, E)) : 0u;
+    const float kNaN = __int_as_float(0x7fc00000);
+    uint32_t rt_i = 0;
+    bool ok = true;
+    for (int64_t rt = blockIdx.x; rt < a.n_rt; rt += gridDim.x, ++rt_i) {
+      const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
+      // the MMAs of the buffer's previous row tile are done, and the epilogue has read
+      // its pp and Br
+      if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag) || !mbar_wait(&pempty[abuf], ause ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if constexpr (FUSED) {
+        // this CTA's next row tile into L2 while this one is read
+        const int64_t nrt = rt + gridDim.x;
+        if (c == 0 && nrt < a.n_rt) {
+          const int64_t r0 = nrt * TF_BM;
+          const int64_t rows = (a.n - r0) < TF_BM ? (a.n - r0) : TF_BM;
+          const uint64_t bytes = static_cast<uint64_t>(rows) * static_cast<uint64_t>(a.dim) * 4u;
+          const char* src = reinterpret_cast<const char*>(a.X + r0 * a.dim);
+          for (uint64_t off = 0; off < bytes; off += 32768u)
+            bulk_prefetch_l2(src + off, static_cast<uint32_t>(bytes - off < 32768u ? bytes - off : 32768u));
+        }
+      }
+      float* rb = rowbuf + abuf * 2 * TF_BM;
+      uint8_t* ax = aaux + abuf * TF_AAUX_BYTES;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const int r = c + 64 * h;
+        const int64_t i = rt * TF_BM + r;
+        const bool valid = i < a.n;
+        float pp;
+        if constexpr (FUSED) {
+          pp = fused_row<KIND>(a.X + (valid ? i : 0) * a.dim, a.dim, KB, smem + abuf * a_bytes, r, valid);
+          if (valid) a.pp[i] = pp;
+        } else {
+          pp = valid ? __ldg(a.pp + i) : 0.f;
+        }
+        const float br = __fmul_rn(pp, kAuxRowScale);
+        const float w = 0.5f * br * sc;
+        const bool fits = screen && br < 3.0e38f && (KIND != 0 || w < 32768.f);
+        if (valid && !fits) a.redo[i] = 1;
+        const bool use = valid && fits;
+        rb[r] = pp;
+        rb[TF_BM + r] = use ? br : kNaN;
+        uint32_t e[6] = {te, te, te, 0u, 0u, 0u};
+        if (use) split3<KIND>(w, e + 3);
+        uint4 lo, hi;
+        aux_pack<KIND>(e, lo, hi);
+        // 32-byte rows with the 32-byte swizzle: 16-byte chunk q of row r at chunk
+        // q ^ ((r / 4) % 2)
+        const int sw = (r >> 2) & 1;
+        *reinterpret_cast<uint4*>(ax + r * 32 + (sw << 4)) = lo;
+        *reinterpret_cast<uint4*>(ax + r * 32 + ((sw ^ 1) << 4)) = hi;
+      }
+      fence_async_shared();  // the MMA reads A and the extra-K rows through the async proxy
+      mbar_arrive(&afull[abuf]);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      if (c == 0) atomicExch(&s_tf_err, DEV_TIMEOUT_ROWS);
+    }
   }
 
   tc_fence_before();
@@ -452,8 +586,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 // ------------------------------------------------------------------ host side
 
 constexpr size_t TF_SMEM_LIMIT = 232448;
-constexpr size_t TF_FIXED =
-    1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + TF_AAUX_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
+constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + 2 * TF_AAUX_BYTES +
+                            2 * TF_ROWBUF_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
 
 // Resident A (the row tile, double-buffered) with B-only stages when that leaves room
 // for 3 stages, else streaming (A B) stages.
@@ -482,21 +616,39 @@ int tc_fast_regions(int64_t n) {
   return grid < 1 ? 1 : grid;
 }
 
-template <int KIND>
-static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& taa,
-                               const CUtensorMap& tba, const TfArgs& args, int grid, cudaStream_t st) {
-  auto kern = dist_tc_fast_kernel<KIND>;
+template <int KIND, bool FUSED>
+static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tba,
+                               const TfArgs& args, int grid, cudaStream_t st) {
+  auto kern = dist_tc_fast_kernel<KIND, FUSED>;
   const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   timing_begin(st, "dist_tc_fast_kernel");
-  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, taa, tba, args);
+  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, tba, args);
   e = cudaGetLastError();
   timing_end(st);
   return e;
 }
 
 static int low_kind(const OpSpec* s) { return (s->gemm == G_TC_F16) ? 0 : (s->gemm == G_TC_BF16 ? 1 : 2); }
+
+static int tf_kblocks(const DistJob& j) {
+  const int esize = (low_kind(j.spec) == 2) ? 4 : 2;
+  return static_cast<int>((static_cast<int64_t>(j.ldlow) * esize) / 128);
+}
+
+// The row warps read the fp32 points themselves when the operator's norm is that of
+// the fp16 / bf16 rounded values, the rows are whole 16-byte vectors, and A stays
+// resident in shared memory.
+bool tc_fast_can_fuse_rows(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  const bool recipe = (s->gemm == G_TC_F16 && s->norm == NM_LOW_F16) || (s->gemm == G_TC_BF16 && s->norm == NM_LOW_BF16);
+  if (!recipe || s->in != IN_F32) return false;
+  if (j.dim % 4 != 0 || (reinterpret_cast<uintptr_t>(j.P) & 15u) != 0) return false;
+  int nst = 0, a_res = 0;
+  tf_pipeline(tf_kblocks(j), &nst, &a_res);
+  return a_res != 0 && nst >= 2;
+}
 
 cudaError_t launch_tc_fast(const DistJob& j) {
   const OpSpec* s = j.spec;
@@ -506,19 +658,22 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   TfArgs a{};
   a.n = j.n;
   a.m = j.m;
-  a.kblocks = static_cast<int>((static_cast<int64_t>(j.ldlow) * esize) / 128);
+  a.kblocks = tf_kblocks(j);
   a.n_ct = static_cast<int>((j.m + TF_BN - 1) / TF_BN);
   a.n_rt = (j.n + TF_BM - 1) / TF_BM;
   tf_pipeline(a.kblocks, &a.nst, &a.a_res);
   if (a.nst < 2) return cudaErrorInvalidValue;
-  a.pp = static_cast<const float*>(j.pp);
+  if (j.fused_rows && !tc_fast_can_fuse_rows(j)) return cudaErrorInvalidValue;
+  a.pp = static_cast<float*>(j.pp);
+  a.X = static_cast<const float*>(j.P);
+  a.dim = j.dim;
   a.ccs = j.cc_sorted;
   a.perm = j.perm;
   a.omk = 1.f - j.kf;
   // screen margin: the rounding of S to the GEMM's output format dominates
   a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-16f);
   a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
-  a.aux_b = j.aux_b;
+  a.aux_e = j.aux_e;
   a.row_key = j.row_key;
   a.list = j.chunk_list;
   a.sbuf = j.chunk_s;
@@ -527,17 +682,21 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.redo = j.redo;
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
-  CUtensorMap ta, tb;
-  if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
+  CUtensorMap ta{}, tb;
+  if (!j.fused_rows && !tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1))
+    return cudaErrorInvalidValue;
   if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
-  CUtensorMap taa, tba;
+  CUtensorMap tba;
   const int64_t mpad = (j.m + TF_BN - 1) / TF_BN * TF_BN;
-  if (!tc_make_tmap_sw32(&taa, j.a_aux, TF_BM, esize, TF_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;
   if (!tc_make_tmap_sw32(&tba, j.b_aux_sorted, mpad, esize, TF_BN, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-  if (kind == 0) return launch_tf_t<0>(ta, tb, taa, tba, a, grid, j.stream);
-  if (kind == 1) return launch_tf_t<1>(ta, tb, taa, tba, a, grid, j.stream);
-  return launch_tf_t<2>(ta, tb, taa, tba, a, grid, j.stream);
+  if (j.fused_rows) {
+    if (kind == 0) return launch_tf_t<0, true>(ta, tb, tba, a, grid, j.stream);
+    return launch_tf_t<1, true>(ta, tb, tba, a, grid, j.stream);
+  }
+  if (kind == 0) return launch_tf_t<0, false>(ta, tb, tba, a, grid, j.stream);
+  if (kind == 1) return launch_tf_t<1, false>(ta, tb, tba, a, grid, j.stream);
+  return launch_tf_t<2, false>(ta, tb, tba, a, grid, j.stream);
 }
 
 int tf_error_and_clear() {
@@ -547,27 +706,28 @@ int tf_error_and_clear() {
   return v;
 }
 
+// s of one pair over the rounded operands the MMA consumes, summed in dimension order
+// with fused multiply-adds: the fp32 point row rounded here (the rounding of its
+// low-precision copy), the center row from its low-precision copy.  The copies' zero
+// padding would add nothing, so the sum stops at dim.
 template <int KIND>
-__device__ __forceinline__ float low_dot(const uint4* __restrict__ p, const uint4* __restrict__ c, int nvec) {
+__device__ __forceinline__ float low_dot(const float* __restrict__ p, const uint4* __restrict__ c, int dim) {
+  constexpr int PER = (KIND == 2) ? 4 : 8;  // elements per 16-byte vector of the copy
   float acc = 0.f;
-  for (int v = 0; v < nvec; ++v) {
-    const uint4 xv = __ldg(p + v), yv = __ldg(c + v);
-    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ys[4] = {yv.x, yv.y, yv.z, yv.w};
+  for (int v = 0; v * PER < dim; ++v) {
+    const uint4 yv = __ldg(c + v);
+    const uint32_t ys[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      if constexpr (KIND == 2) {
-        acc = __fmaf_rn(__uint_as_float(xs[w]), __uint_as_float(ys[w]), acc);
-      } else {
-        float2 fx, fy;
-        if constexpr (KIND == 0) {
-          fx = __half22float2(*reinterpret_cast<const __half2*>(&xs[w]));
-          fy = __half22float2(*reinterpret_cast<const __half2*>(&ys[w]));
-        } else {
-          fx = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[w]));
-          fy = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ys[w]));
-        }
-        acc = __fmaf_rn(fx.x, fy.x, acc);
-        acc = __fmaf_rn(fx.y, fy.y, acc);
+    for (int e = 0; e < PER; ++e) {
+      const int k = v * PER + e;
+      if (k < dim) {
+        const float x = low_value<KIND>(low_bits<KIND>(__ldg(p + k)));
+        float y;
+        if constexpr (KIND == 2)
+          y = __uint_as_float(ys[e]);
+        else
+          y = low_value<KIND>((ys[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
+        acc = __fmaf_rn(x, y, acc);
       }
     }
   }
@@ -595,8 +755,7 @@ __device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long k)
 
 struct EvArgs {
   const unsigned long long* clist;
-  const float* sbuf;            // the chunk's accumulators y = y0 - s, y0 = (cc + B) / 2 (0 for a non-finite cc)
-  const float* aux_b;
+  const float* sbuf;            // the chunk's accumulators y = y0 - s, y0 = (cc + Br) / 2 (0 for a non-finite cc)
   unsigned long long region_cap;
   const uint32_t* region_cnt;
   const float* pp;
@@ -680,11 +839,11 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
       cc[u] = jv[u] ? __ldg(a.cc_s + j) : 0.f;
       jo[u] = jv[u] ? static_cast<uint32_t>(__ldg(a.perm + j)) : 0u;
     }
-    const float B = __ldg(a.aux_b);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (skip[u]) continue;  // warp-uniform
-      const float y0 = cc[u] < 3.0e38f ? 0.5f * __fadd_rn(cc[u], B) : 0.f;
+      const float br = __fmul_rn(pp[u], kAuxRowScale);
+      const float y0 = cc[u] < 3.0e38f ? __fadd_rn(0.5f * cc[u], 0.5f * br) : 0.f;
       const float d = exact_d<SROUND>(y0 - sv[u], pp[u], cc[u]);
       const bool fl = jv[u] && d <= __fmul_rn(a.K, __fadd_rn(pp[u], cc[u]));
       const unsigned bal = __ballot_sync(0xffffffffu, fl);
@@ -707,12 +866,12 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   if (wcnt > 0) flush_pairs<REC>(a, wbuf, wcnt, lane);
 }
 
-// Rows whose candidates overflowed their region: every pair evaluated exactly, with
-// s summed in fp32 (sequential fused multiply-adds) over the rounded operands the MMA
-// consumed; flagged pairs take the direct distance here.
+// Rows whose candidates overflowed their region, or whose norm did not fit the extra K
+// block: every pair evaluated exactly, with s summed in fp32 (sequential fused
+// multiply-adds) over the rounded operands the MMA consumes; flagged pairs take the
+// direct distance here.
 
 struct RdArgs {
-  const void* Plow;
   const void* Clow;   // original order
   int nvec;           // 16-byte vectors per low row
   const float* P;
@@ -745,8 +904,7 @@ __global__ void __launch_bounds__(256) redo_rows_kernel(const RdArgs a) {
         const int64_t j = j0 + lane;
         bool fl = false;
         if (j < a.m) {
-          const float sv = low_dot<KIND>(static_cast<const uint4*>(a.Plow) + i * a.nvec,
-                                         static_cast<const uint4*>(a.Clow) + j * a.nvec, a.nvec);
+          const float sv = low_dot<KIND>(a.P + i * a.dim, static_cast<const uint4*>(a.Clow) + j * a.nvec, a.dim);
           const float cc = __ldg(a.cc + j);
           float d = exact_d<SROUND>(sv, pp, cc);
           fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
@@ -782,7 +940,6 @@ cudaError_t launch_eval_chunks(const DistJob& j) {
   EvArgs a{};
   a.clist = j.chunk_list;
   a.sbuf = j.chunk_s;
-  a.aux_b = j.aux_b;
   a.region_cap = j.chunk_cap / static_cast<unsigned long long>(j.regions);
   a.region_cnt = j.region_cnt;
   a.pp = static_cast<const float*>(j.pp);
@@ -815,7 +972,6 @@ cudaError_t launch_redo_rows(const DistJob& j) {
   const int kind = low_kind(s);
   const int esize = (kind == 2) ? 4 : 2;
   RdArgs a{};
-  a.Plow = j.Plow;
   a.Clow = j.Clow;
   a.nvec = static_cast<int>(static_cast<int64_t>(j.ldlow) * esize / 16);
   a.P = static_cast<const float*>(j.P);

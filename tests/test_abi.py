@@ -72,9 +72,9 @@ def test_host_queries(lib):
     al = lambda b: (b + 255) // 256 * 256
     mpad = (m + 255) // 256 * 256
     ccap = min(n * ((m + 31) // 32), max(2 * n, 1 << 16))  # candidate chunks: entry + 32 fp32 accumulators
-    # plus the extra-K rows of the screening MMA (32 bytes per row: 128 A rows, mpad B rows)
+    # plus the centers' extra-K rows of the screening MMA (32 bytes per sorted center)
     assert lib.euc_argmin_workspace_bytes(10, n, m, d) == (ws + al(m * 128 * 2) + 2 * al(mpad * 4) + al(1024 * 4)
-                                                           + al(n) + al(128 * 32) + al(mpad * 32) + al(ccap * 8)
+                                                           + al(n) + al(mpad * 32) + al(ccap * 8)
                                                            + al(ccap * 128) + al(n * 8))
 
 
