@@ -56,6 +56,12 @@ constexpr int TF_EPI_WARPS = 16;  // 4 groups (b, column half) x 4 TMEM lane qua
 constexpr int TF_ROW_WARPS = 2;   // row preparation: one thread per two rows of the tile
 constexpr int TF_ROW_THREADS = TF_ROW_WARPS * 32;
 constexpr int TF_THREADS = (2 + TF_EPI_WARPS + TF_ROW_WARPS) * 32;
+// warp roles; an epilogue warp reads TMEM lane quadrant warp % 4, so 16 consecutive
+// epilogue warps give each (group, quadrant) pair one warp
+constexpr int TF_W_PRODUCER = 0;
+constexpr int TF_W_MMA = 1;
+constexpr int TF_W_EPI0 = 2;
+constexpr int TF_W_ROW0 = TF_W_EPI0 + TF_EPI_WARPS;
 constexpr int TF_A_KB = TF_BM * 128;  // one 128-row x 128-byte K block of A
 constexpr int TF_B_KB = TF_BN * 128;  // one 256-row x 128-byte K block of B
 constexpr int TF_SLOTS = 4;             // center-metadata ring
@@ -64,7 +70,7 @@ constexpr int TF_META_BYTES = TF_BAUX_BYTES + TF_BN * 4;  // + the tile's sorted
 constexpr int TF_AAUX_BYTES = TF_BM * 32;       // per A buffer: the rows' extra-K rows
 constexpr int TF_ROWBUF_BYTES = 2 * TF_BM * 4;  // per A buffer: pp and Br of each row
 constexpr int TF_BAR_BYTES = 512;
-constexpr int TF_EPI_BYTES = 2 * 4 * TF_BM * 4;  // row merge
+constexpr int TF_EPI_BYTES = 2 * 3 * TF_BM * 4;  // row merge
 
 struct TfArgs {
   int64_t n, m;
@@ -197,8 +203,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kCols);
-  if (warp == 0 && lane == 0) {
+  if (warp == TF_W_MMA) tmem_alloc(tmem_slot, kCols);
+  if (warp == TF_W_PRODUCER && lane == 0) {
     if (!FUSED) prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmBaux);
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == TF_W_PRODUCER) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, rt_i = 0, t = 0;
@@ -264,7 +270,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       for (int s = 0; s < TF_SLOTS; ++s)
         if (m_issued & (1u << s)) mbar_wait(&metaf[s], (m_last >> s) & 1u, &no_abort);
     }
-  } else if (warp == 1) {
+  } else if (warp == TF_W_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
@@ -324,20 +330,20 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort);
     }
-  } else if (warp < 2 + TF_EPI_WARPS) {
+  } else if (warp >= TF_W_EPI0 && warp < TF_W_EPI0 + TF_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     // The accumulators hold y = (cc + Br) / 2 - s >= 0 (the extra K block adds the first
     // term), so a row's smallest distance in a chunk is its smallest y: keys are y with
     // the column in the low 5 mantissa bits, reduced with 3-way mins.
-    const int ew = warp - 2;            // 0..15
+    const int ew = warp - TF_W_EPI0;    // 0..15
     const int q = warp & 3;             // TMEM lane quadrant
     const int g = ew >> 2;              // group: tile parity b = g >> 1, column half hc = g & 1
     const int hc = g & 1;
     const uint32_t b = static_cast<uint32_t>(g >> 1);
     const int row_local = q * 32 + lane;
     const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * TF_BN + hc * 128;
-    float* mv = epi;                                             // row merge: [4][128] minima
-    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 4 * TF_BM);  //            [4][128] their columns
+    float* mv = epi;                                             // row merge: [3][128] minima
+    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 3 * TF_BM);  //            [3][128] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
     // screen: a pair can only be flagged (d <= K (pp + cc)) where
@@ -505,7 +511,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     // and their extra-K rows [2^E, 2^E, 2^E, parts of Br / 2 * 2^-E] for the MMA; with
     // FUSED also the rows of A and pp itself.  A row whose norm is not finite or does
     // not fit the extra K block gets a zero row term and is marked for the exact redo.
-    const int c = threadIdx.x - (2 + TF_EPI_WARPS) * 32;
+    const int c = threadIdx.x - TF_W_ROW0 * 32;
     const int E = __ldg(a.aux_e);
     const bool screen = E < kAuxNoScreen;
     const float sc = screen ? ldexpf(1.f, -E) : 0.f;
@@ -580,7 +586,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const unsigned long long c = *lcount;
     a.region_cnt[blockIdx.x] = static_cast<uint32_t>(c < a.region_cap ? c : a.region_cap);
   }
-  if (warp == 1) tmem_dealloc(tmem_base, kCols);
+  if (warp == TF_W_MMA) tmem_dealloc(tmem_base, kCols);
 }
 
 // ------------------------------------------------------------------ host side
@@ -682,7 +688,7 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.redo = j.redo;
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
-  CUtensorMap ta{}, tb;
+  CUtensorMap ta{}, tb;  // A: the low-precision copy (unused with FUSED)
   if (!j.fused_rows && !tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
   if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
