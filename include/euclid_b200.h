@@ -216,13 +216,15 @@ EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int6
  *   exact != 0: every pair's distance is formed exactly as `op` forms D, and the label
  *               is torch.argmin(D, 1) of that D (first index of the minimum).
  *   exact == 0: tensor-core operators screen each 32-center chunk: the MMA itself
- *               yields y = (|c|^2 + B)/2 - p.c (B = 1.0625 max_i |p_i|^2), and per pair
- *               one key (y with the column in its low 5 bits) and half a 3-way min
+ *               yields y = (|c|^2 + Br)/2 - p.c (Br = 1.0625 |p|^2 of the row), and per
+ *               pair one key (y with the column in its low 5 bits) and half a 3-way min
  *               remain; the exact path runs only on chunks where a pair could be
  *               flagged.  Labels equal the exact ones whenever the row's top-two
- *               distance gap exceeds 2^-10 (|p|^2 + max|c|^2) + 2^-16 (max|c|^2 + B)
+ *               distance gap exceeds 2^-10 (|p|^2 + max|c|^2) + 2^-16 (max|c|^2 + Br)
  *               (2^-7 for bf16 S); min_dist then carries about 18 significant bits
- *               relative to max|c|^2 + B.
+ *               relative to max|c|^2 + Br.  For the fp16/bf16 mix operators with
+ *               dim % 4 == 0 and a 16-byte aligned P, the screen reads the fp32 points
+ *               itself (no low-precision copy of P is made).
  * P/C element type follows `op` (fp64 for EUC_OP_DOUBLE, fp32 otherwise).  Outputs
  * are nullable: labels (int64[n]), labels32 (int32[n]), min_dist (fp32[n]; fp64[n]
  * for EUC_OP_DOUBLE). */
