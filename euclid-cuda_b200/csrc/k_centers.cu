@@ -9,10 +9,12 @@
 // Two strategies, chosen by the size of the k x (dim+1) table:
 //   * table <= 48 KiB  -> per-CTA privatised table in shared memory (smem fp64
 //     atomics), one flush of the table per CTA;
-//   * larger tables    -> counting sort by label (histogram, scan, warp-aggregated
-//     scatter with __match_any_sync) followed by a segmented reduction where each
-//     warp walks 1024 label-sorted rows with coalesced row reads and flushes one
-//     fp64 atomic per (segment, dim).
+//   * larger tables    -> counting sort by label followed by a segmented reduction
+//     where each warp walks 1024 label-sorted rows with coalesced row reads and
+//     flushes one fp64 atomic per (segment, dim).  The sort counts per block of rows
+//     in shared memory (k <= 16384): block histograms, per-label totals, a scan over
+//     labels, per-(block, label) offsets, and a scatter with shared-memory cursors.
+//     Larger k counts with warp-aggregated global atomics (__match_any_sync).
 // stats is the unit of the data-parallel all-reduce; centers = stats / count
 // (euc_center_finalize), empty clusters -> 0 as in center_kernels.cu:52,116.
 #include "common.cuh"
@@ -126,6 +128,96 @@ __global__ void scatter_kernel(const TL* __restrict__ labels, int64_t n, int k,
   }
 }
 
+// ------------------------------------------ sort strategy, block-private counting
+// Rows [b * rpb, (b + 1) * rpb) belong to block b.  T[b * k + c] first holds the block's
+// count of label c, then (priv_offsets_kernel) the position of its first such row.
+template <typename TL>
+__global__ void __launch_bounds__(512) priv_hist_kernel(const TL* __restrict__ labels, int64_t n, int k,
+                                                        int64_t rpb, unsigned int* __restrict__ T) {
+  extern __shared__ unsigned int cnt[];
+  for (int c = threadIdx.x; c < k; c += blockDim.x) cnt[c] = 0u;
+  __syncthreads();
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpb;
+  const int64_t r1 = min(n, r0 + rpb);
+  for (int64_t i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+    const int64_t c = load_label(labels, i);
+    if (c >= 0 && c < k) atomicAdd(&cnt[c], 1u);
+  }
+  __syncthreads();
+  unsigned int* row = T + static_cast<int64_t>(blockIdx.x) * k;
+  for (int c = threadIdx.x; c < k; c += blockDim.x) row[c] = cnt[c];
+}
+
+// The block dimension of T is cut into kPrivSlices slices of consecutive blocks, one
+// thread per (label, slice).  PS[s * k + c]: rows with label c in slice s.
+constexpr int kPrivSlices = 32;
+
+__global__ void priv_slice_sums_kernel(const unsigned int* __restrict__ T, int nb, int k,
+                                       unsigned int* __restrict__ PS) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, sl = blockIdx.y;
+  if (c >= k) return;
+  const int per = (nb + kPrivSlices - 1) / kPrivSlices;
+  const int b0 = sl * per, b1 = min(nb, b0 + per);
+  unsigned int t = 0u;
+  for (int b = b0; b < b1; ++b) t += T[static_cast<int64_t>(b) * k + c];
+  PS[static_cast<int64_t>(sl) * k + c] = t;
+}
+
+// counts[c] = total over the slices; PS becomes the exclusive prefix over slices
+__global__ void priv_slice_scan_kernel(unsigned int* __restrict__ PS, int k, unsigned int* __restrict__ counts) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= k) return;
+  unsigned int run = 0u;
+  for (int sl = 0; sl < kPrivSlices; ++sl) {
+    const int64_t at = static_cast<int64_t>(sl) * k + c;
+    const unsigned int t = PS[at];
+    PS[at] = run;
+    run += t;
+  }
+  counts[c] = run;
+}
+
+// T[b * k + c] <- offs[c] + rows with label c in blocks before b
+__global__ void priv_offsets_kernel(unsigned int* __restrict__ T, int nb, int k,
+                                    const unsigned long long* __restrict__ offs,
+                                    const unsigned int* __restrict__ PS) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, sl = blockIdx.y;
+  if (c >= k) return;
+  const int per = (nb + kPrivSlices - 1) / kPrivSlices;
+  const int b0 = sl * per, b1 = min(nb, b0 + per);
+  unsigned int run = static_cast<unsigned int>(offs[c]) + PS[static_cast<int64_t>(sl) * k + c];
+  for (int b = b0; b < b1; ++b) {
+    const int64_t at = static_cast<int64_t>(b) * k + c;
+    const unsigned int t = T[at];
+    T[at] = run;
+    run += t;
+  }
+}
+
+template <typename TL>
+__global__ void __launch_bounds__(512) priv_scatter_kernel(const TL* __restrict__ labels, int64_t n, int k,
+                                                           int64_t rpb, const unsigned int* __restrict__ T,
+                                                           unsigned int* __restrict__ perm) {
+  extern __shared__ unsigned int cur[];
+  const unsigned int* row = T + static_cast<int64_t>(blockIdx.x) * k;
+  for (int c = threadIdx.x; c < k; c += blockDim.x) cur[c] = row[c];
+  __syncthreads();
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpb;
+  const int64_t r1 = min(n, r0 + rpb);
+  for (int64_t i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+    const int64_t c = load_label(labels, i);
+    if (c >= 0 && c < k) perm[atomicAdd(&cur[c], 1u)] = static_cast<unsigned int>(i);
+  }
+}
+
+constexpr int kPrivMaxK = 16384;  // block-private counters: 64 KiB of shared memory
+
+// blocks of the block-private counting sort: at least 8192 rows each, at most 2048
+static int64_t priv_blocks(int64_t n) {
+  int64_t nb = (n + 8191) / 8192;
+  return nb < 1 ? 1 : (nb > 2048 ? 2048 : nb);
+}
+
 // Each warp reduces SEG label-sorted rows; NPL = dims per lane (ceil(dim/32)).
 template <typename TX, int NPL>
 __global__ void __launch_bounds__(256) segsum_kernel(const TX* __restrict__ X, int dim, int k,
@@ -151,23 +243,38 @@ __global__ void __launch_bounds__(256) segsum_kernel(const TX* __restrict__ X, i
 #pragma unroll
   for (int q = 0; q < NPL; ++q) acc[q] = 0.0;
   const int w = dim + 1;
-  for (int64_t p = p0; p < p1; ++p) {
-    while (static_cast<unsigned long long>(p) >= cend) {
+  // rows in batches of RB: their indices, then their values, are loaded before any is
+  // folded, so a warp keeps RB row reads in flight
+  constexpr int RB = NPL <= 2 ? 4 : (NPL <= 4 ? 2 : 1);
+  for (int64_t pb = p0; pb < p1; pb += RB) {
+    int64_t row[RB];
+#pragma unroll
+    for (int u = 0; u < RB; ++u) row[u] = (pb + u < p1) ? static_cast<int64_t>(perm[pb + u]) : -1;
+    TX v[RB][NPL];
+#pragma unroll
+    for (int u = 0; u < RB; ++u) {
 #pragma unroll
       for (int q = 0; q < NPL; ++q) {
         const int j = lane + 32 * q;
-        if (j < dim && acc[q] != 0.0) atomicAdd(stats + static_cast<int64_t>(c) * w + j, acc[q]);
-        acc[q] = 0.0;
+        v[u][q] = (row[u] >= 0 && j < dim) ? X[row[u] * dim + j] : static_cast<TX>(0);
       }
-      ++c;
-      cend = offs[c + 1];
     }
-    const int64_t row = perm[p];
-    const TX* xr = X + row * dim;
 #pragma unroll
-    for (int q = 0; q < NPL; ++q) {
-      const int j = lane + 32 * q;
-      if (j < dim) acc[q] += static_cast<double>(xr[j]);
+    for (int u = 0; u < RB; ++u) {
+      const int64_t p = pb + u;
+      if (p >= p1) break;
+      while (static_cast<unsigned long long>(p) >= cend) {
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          const int j = lane + 32 * q;
+          if (j < dim && acc[q] != 0.0) atomicAdd(stats + static_cast<int64_t>(c) * w + j, acc[q]);
+          acc[q] = 0.0;
+        }
+        ++c;
+        cend = offs[c + 1];
+      }
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) acc[q] += static_cast<double>(v[u][q]);
     }
   }
 #pragma unroll
@@ -183,7 +290,8 @@ static bool use_smem(int64_t dim, int64_t k) { return k * (dim + 1) * 8 <= 48 * 
 
 size_t center_ws_bytes(int64_t n, int64_t dim, int64_t k) {
   if (use_smem(dim, k)) return 256;
-  return al(k * 4) + al((k + 1) * 8) + al(k * 8) + al(n * 4) + 256;
+  const size_t tab = k <= kPrivMaxK ? al(static_cast<size_t>(priv_blocks(n)) * k * 4) + al(kPrivSlices * k * 4) : 0;
+  return al(k * 4) + al((k + 1) * 8) + al(k * 8) + al(n * 4) + tab + 256;
 }
 
 template <typename TX, typename TL>
@@ -209,12 +317,36 @@ static cudaError_t stats_t(const TX* X, const TL* labels, int64_t n, int dim, in
   unsigned long long* cursor = reinterpret_cast<unsigned long long*>(p);
   p += al(static_cast<size_t>(k) * 8);
   unsigned int* perm = reinterpret_cast<unsigned int*>(p);
-  e = cudaMemsetAsync(counts, 0, static_cast<size_t>(k) * 4, st);
-  if (e != cudaSuccess) return e;
-  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, sms * 8));
-  hist_kernel<TL><<<blocks, 256, 0, st>>>(labels, n, k, counts);
-  scan_kernel<<<1, 1024, 0, st>>>(counts, k, dim, offs, cursor, stats);
-  scatter_kernel<TL><<<blocks, 256, 0, st>>>(labels, n, k, cursor, perm);
+  p += al(static_cast<size_t>(n) * 4);
+  if (k <= kPrivMaxK) {
+    unsigned int* T = reinterpret_cast<unsigned int*>(p);
+    const int64_t nb = priv_blocks(n);
+    unsigned int* PS = reinterpret_cast<unsigned int*>(p + al(static_cast<size_t>(nb) * k * 4));
+    const int64_t rpb = (n + nb - 1) / nb;
+    const size_t sm = static_cast<size_t>(k) * 4;
+    if (sm > 48 * 1024) {
+      e = cudaFuncSetAttribute(priv_hist_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(priv_scatter_kernel<TL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sm));
+      if (e != cudaSuccess) return e;
+    }
+    const unsigned kb = static_cast<unsigned>((k + 255) / 256);
+    priv_hist_kernel<TL><<<static_cast<unsigned>(nb), 512, sm, st>>>(labels, n, k, rpb, T);
+    const dim3 g2(kb, kPrivSlices);
+    priv_slice_sums_kernel<<<g2, 256, 0, st>>>(T, static_cast<int>(nb), k, PS);
+    priv_slice_scan_kernel<<<kb, 256, 0, st>>>(PS, k, counts);
+    scan_kernel<<<1, 1024, 0, st>>>(counts, k, dim, offs, cursor, stats);
+    priv_offsets_kernel<<<g2, 256, 0, st>>>(T, static_cast<int>(nb), k, offs, PS);
+    priv_scatter_kernel<TL><<<static_cast<unsigned>(nb), 512, sm, st>>>(labels, n, k, rpb, T, perm);
+  } else {
+    e = cudaMemsetAsync(counts, 0, static_cast<size_t>(k) * 4, st);
+    if (e != cudaSuccess) return e;
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, sms * 8));
+    hist_kernel<TL><<<blocks, 256, 0, st>>>(labels, n, k, counts);
+    scan_kernel<<<1, 1024, 0, st>>>(counts, k, dim, offs, cursor, stats);
+    scatter_kernel<TL><<<blocks, 256, 0, st>>>(labels, n, k, cursor, perm);
+  }
   // rows with a valid label = offs[k] <= n; the grid covers n positions and each warp
   // clamps to offs[k] on the device.
   const int64_t warps = (n + 1023) / 1024;

@@ -332,7 +332,10 @@ def test_advanced_exact(shape):
     device_check()
 
 
-@pytest.mark.parametrize("n,d,k", [(500, 8, 10), (20000, 64, 300), (4097, 130, 4096), (3, 2, 5)])
+# shapes reach: the shared-memory table (first), the block-private counting sort (k <= 16384,
+# one and several row blocks) and the global-atomic counting sort (k > 16384)
+@pytest.mark.parametrize("n,d,k", [(500, 8, 10), (20000, 64, 300), (4097, 130, 4096), (3, 2, 5),
+                                   (100000, 16, 4096), (30000, 4, 20000)])
 @pytest.mark.parametrize("dtype", [np.float32, np.float64])
 def test_centers_vs_oracle(n, d, k, dtype):
     rng = np.random.default_rng(n + k)
