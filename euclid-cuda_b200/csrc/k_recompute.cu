@@ -79,13 +79,13 @@ __global__ void __launch_bounds__(256) recompute_kernel(const RecArgs a) {
 
 // Argmin mode with fp32 inputs, warp-cooperative: a warp takes 32 listed pairs and
 // stages their P and C rows through shared memory 32 dimensions at a time with coalesced
-// (16-byte) loads; each lane then runs its pair's sum in the same arithmetic and the
-// same k order as direct_dist.
+// (16-byte) loads, all of a slab's loads in flight together; each lane then runs its
+// pair's sum in the same arithmetic and the same k order as direct_dist.
 constexpr int RW_WARPS = 4;
 constexpr int RW_K = 32;
 
 template <int REC>
-__global__ void __launch_bounds__(RW_WARPS * 32) recompute_argmin_rows_kernel(const RecArgs a) {
+__global__ void __launch_bounds__(RW_WARPS * 32, 4) recompute_argmin_rows_kernel(const RecArgs a) {
   __shared__ float sp[RW_WARPS][32][RW_K + 1];
   __shared__ float sc[RW_WARPS][32][RW_K + 1];
   const float* P = static_cast<const float*>(a.P);
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(RW_WARPS * 32) recompute_argmin_rows_kernel(co
       const int kn = min(RW_K, dim - k0);
       if (vec) {
         const int quarter = lane >> 3, c4 = (lane & 7) * 4;  // 8 lanes x 16 bytes per row slab
-#pragma unroll 4
+#pragma unroll
         for (int rr = 0; rr < 32; rr += 4) {
           const int r = rr + quarter;
           const long long ir = __shfl_sync(0xffffffffu, i, r);

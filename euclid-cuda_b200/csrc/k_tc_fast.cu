@@ -869,7 +869,27 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
       }
     }
   }
-  if (wcnt > 0) flush_pairs<REC>(a, wbuf, wcnt, lane);
+  // the warps' remaining pairs: one list reservation for the whole block (a reservation
+  // per warp would queue thousands of atomics on the one counter)
+  __shared__ unsigned int s_tot;
+  __shared__ unsigned long long s_base;
+  if (threadIdx.x == 0) s_tot = 0u;
+  __syncthreads();
+  unsigned int off = 0u;
+  if (lane == 0 && wcnt > 0) off = atomicAdd(&s_tot, static_cast<unsigned int>(wcnt));
+  off = __shfl_sync(0xffffffffu, off, 0);
+  __syncthreads();
+  if (threadIdx.x == 0) s_base = s_tot ? atomicAdd(a.count, static_cast<unsigned long long>(s_tot)) : 0ull;
+  __syncthreads();
+  const unsigned long long base = s_base + off;
+  for (int q = lane; q < wcnt; q += 32) {
+    const unsigned long long e = wbuf[q];
+    if (base + q < a.cap)
+      a.list[base + q] = e;
+    else
+      fold_direct<REC>(a.P, a.C, a.dim, a.row_key, static_cast<int64_t>(e >> 32),
+                       static_cast<uint32_t>(e & 0xffffffffull));
+  }
 }
 
 // Rows whose candidates overflowed their region, or whose norm did not fit the extra K
