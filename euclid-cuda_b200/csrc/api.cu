@@ -283,7 +283,6 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.fused_rows = j.fast_argmin && tc_fast_can_fuse_rows(j);
 
   cudaError_t e = cudaMemsetAsync(j.count, 0, 8, st);
-  if (e == cudaSuccess && j.fast_argmin) e = cudaMemsetAsync(j.redo, 0, static_cast<size_t>(n), st);
   if (e == cudaSuccess && o.tile_counts) {
     const int64_t nt = ((n + o.tile_T - 1) / o.tile_T) * j.tiles_j;
     e = cudaMemsetAsync(o.tile_counts, 0, static_cast<size_t>(nt) * 4, st);
@@ -297,9 +296,10 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   if (e != cudaSuccess) return cuda_fail(e, s->name);
   if (j.fast_argmin) e = launch_eval_chunks(j);
   if (e == cudaSuccess) e = launch_recompute(j);
-  if (e == cudaSuccess && j.fast_argmin) e = launch_redo_rows(j);
+  if (e == cudaSuccess && j.fast_argmin)
+    e = launch_redo_rows(j, o.labels, o.labels32, static_cast<float*>(o.min_dist));
   if (e != cudaSuccess) return cuda_fail(e, "recompute");
-  if (argmin) {
+  if (argmin && !j.fast_argmin) {  // the fast path's redo pass has written the outputs
     if (j.row_key) {
       e = launch_keys_to_labels(j.row_key, n, o.labels, o.labels32, static_cast<float*>(o.min_dist), st);
     } else {

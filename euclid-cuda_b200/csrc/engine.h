@@ -127,7 +127,8 @@ cudaError_t launch_tc(const DistJob& j);
 // go to the recompute list), and rows whose candidates did not fit
 cudaError_t launch_tc_fast(const DistJob& j);
 cudaError_t launch_eval_chunks(const DistJob& j);
-cudaError_t launch_redo_rows(const DistJob& j);
+// ... and writes every row's outputs from its key (labels, labels32, mind nullable)
+cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
 int tc_fast_regions(int64_t n);  // CTAs (= list regions) of the screening kernel
 bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows, bool is_f32,
                   bool is_bf16);

@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const float br = __fmul_rn(pp, kAuxRowScale);
         const float w = 0.5f * br * sc;
         const bool fits = screen && br < 3.0e38f && (KIND != 0 || w < 32768.f);
-        if (valid && !fits) a.redo[i] = 1;
+        if (valid) a.redo[i] = fits ? 0 : 1;  // every row's byte: no clearing pass needed
         const bool use = valid && fits;
         rb[r] = pp;
         rb[TF_BM + r] = use ? br : kNaN;
@@ -895,7 +895,8 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
 // Rows whose candidates overflowed their region, or whose norm did not fit the extra K
 // block: every pair evaluated exactly, with s summed in fp32 (sequential fused
 // multiply-adds) over the rounded operands the MMA consumes; flagged pairs take the
-// direct distance here.
+// direct distance here.  The same pass then turns every row's key into its outputs
+// (label, int32 label, distance), as keys_to_labels_kernel does for the other paths.
 
 struct RdArgs {
   const void* Clow;   // original order
@@ -910,6 +911,9 @@ struct RdArgs {
   const uint8_t* redo;
   unsigned long long* row_key;
   unsigned long long* count;
+  int64_t* labels;    // nullable outputs
+  int32_t* labels32;
+  float* mind;
 };
 
 template <int KIND, int SROUND, int REC>
@@ -942,6 +946,14 @@ __global__ void __launch_bounds__(256) redo_rows_kernel(const RdArgs a) {
       }
       best = warp_min_u64(best);
       if (lane == 0) a.row_key[i] = best;
+    }
+    __syncwarp();
+    if (ii < a.n) {
+      const unsigned long long k = a.row_key[ii];
+      const uint32_t j = static_cast<uint32_t>(k & 0xffffffffull);
+      if (a.labels) a.labels[ii] = j;
+      if (a.labels32) a.labels32[ii] = static_cast<int32_t>(j);
+      if (a.mind) a.mind[ii] = __uint_as_float(static_cast<uint32_t>(k >> 32));
     }
   }
   if (lane == 0 && nfl) atomicAdd(a.count, nfl);
@@ -993,7 +1005,7 @@ cudaError_t launch_eval_chunks(const DistJob& j) {
   return cudaErrorNotSupported;
 }
 
-cudaError_t launch_redo_rows(const DistJob& j) {
+cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
   const OpSpec* s = j.spec;
   const int kind = low_kind(s);
   const int esize = (kind == 2) ? 4 : 2;
@@ -1011,6 +1023,9 @@ cudaError_t launch_redo_rows(const DistJob& j) {
   a.redo = j.redo;
   a.row_key = j.row_key;
   a.count = j.count;
+  a.labels = labels;
+  a.labels32 = labels32;
+  a.mind = mind;
   const int64_t warps = (j.n + 31) / 32;
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((warps + 7) / 8, static_cast<int64_t>(num_sms()) * 8));
 #define RD_CASE(KIND_, SR_, REC_)                                             \
