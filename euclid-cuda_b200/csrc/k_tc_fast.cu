@@ -815,32 +815,36 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   const int r = blockIdx.x / EV_BLOCKS_PER_REGION;
   const unsigned wr = (blockIdx.x % EV_BLOCKS_PER_REGION) * 8 + wib;
   constexpr unsigned kStride = EV_BLOCKS_PER_REGION * 8;
-  unsigned long long cnt = a.region_cnt[r];
-  if (cnt > a.region_cap) cnt = a.region_cap;
+  unsigned long long cnt64 = a.region_cnt[r];
+  if (cnt64 > a.region_cap) cnt64 = a.region_cap;
+  // a region holds at most max(2n, 2^16) / regions entries: 32 times that fits 32 bits
+  const uint32_t cnt = static_cast<uint32_t>(cnt64);
   const unsigned long long rbase = static_cast<unsigned long long>(r) * a.region_cap;
+  const unsigned long long* cl = a.clist + rbase;
+  const float* sb = a.sbuf + rbase * 32 + lane;
+  const uint32_t n32 = static_cast<uint32_t>(a.n), m32 = static_cast<uint32_t>(a.m);
   // four entries per iteration: their loads are independent and issue together
   constexpr int U = 4;
-  for (unsigned long long t0 = wr; t0 < cnt; t0 += kStride * U) {
+  for (uint32_t t0 = wr; t0 < cnt; t0 += kStride * U) {
     unsigned long long e[U];
     float sv[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const unsigned long long t = t0 + u * kStride;
+      const uint32_t t = t0 + u * kStride;
       const bool in = t < cnt;
-      e[u] = in ? a.clist[rbase + t] : ~0ull;
-      sv[u] = in ? a.sbuf[(rbase + t) * 32 + lane] : 0.f;
+      e[u] = in ? cl[t] : ~0ull;
+      sv[u] = in ? sb[t * 32u] : 0.f;
     }
-    int64_t i[U];
+    uint32_t i[U], jo[U];
     bool jv[U], skip[U];
     float pp[U], cc[U];
-    uint32_t jo[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      i[u] = static_cast<int64_t>(e[u] >> 32);
-      const int64_t j = static_cast<int64_t>(e[u] & 0xffffffffull) + lane;
-      const bool iv = i[u] < a.n;
-      skip[u] = !iv || a.redo[iv ? i[u] : 0] != 0;  // redo rows are evaluated whole
-      jv[u] = iv && j < a.m;
+      i[u] = static_cast<uint32_t>(e[u] >> 32);
+      const uint32_t j = static_cast<uint32_t>(e[u]) + lane;
+      const bool iv = i[u] < n32;
+      skip[u] = !iv || a.redo[iv ? i[u] : 0u] != 0;  // redo rows are evaluated whole
+      jv[u] = iv && j < m32;
       pp[u] = iv ? __ldg(a.pp + i[u]) : 0.f;
       cc[u] = jv[u] ? __ldg(a.cc_s + j) : 0.f;
       jo[u] = jv[u] ? static_cast<uint32_t>(__ldg(a.perm + j)) : 0u;
