@@ -807,7 +807,7 @@ __device__ __forceinline__ void flush_pairs(const EvArgs& a, unsigned long long*
 }
 
 template <int SROUND, int REC>
-__global__ void __launch_bounds__(256, 2) eval_chunks_kernel(const EvArgs a) {
+__global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   __shared__ unsigned long long s_buf[8][EV_WBUF];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   unsigned long long* wbuf = s_buf[wib];
@@ -823,8 +823,9 @@ __global__ void __launch_bounds__(256, 2) eval_chunks_kernel(const EvArgs a) {
   const unsigned long long* cl = a.clist + rbase;
   const float* sb = a.sbuf + rbase * 32 + lane;
   const uint32_t n32 = static_cast<uint32_t>(a.n), m32 = static_cast<uint32_t>(a.m);
-  // eight entries per iteration: their loads are independent and issue together
-  constexpr int U = 8;
+  // four entries per iteration: their loads are independent and issue together (eight
+  // measured slower at the Lloyd size: the registers they take halve the resident warps)
+  constexpr int U = 4;
   for (uint32_t t0 = wr; t0 < cnt; t0 += kStride * U) {
     unsigned long long e[U];
     float sv[U];
