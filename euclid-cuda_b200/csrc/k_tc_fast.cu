@@ -927,38 +927,58 @@ __global__ void __launch_bounds__(256) redo_rows_kernel(const RdArgs a) {
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   unsigned long long nfl = 0;
-  for (int64_t base = gw * 32; base < a.n; base += nw * 32) {
-    const int64_t ii = base + lane;
-    unsigned bal = __ballot_sync(0xffffffffu, ii < a.n && a.redo[ii] != 0);
-    while (bal) {
-      const int64_t i = base + (__ffs(bal) - 1);
-      bal &= bal - 1;
-      unsigned long long best = ~0ull;
-      const float pp = __ldg(a.pp + i);
-      for (int64_t j0 = 0; j0 < a.m; j0 += 32) {
-        const int64_t j = j0 + lane;
-        bool fl = false;
-        if (j < a.m) {
-          const float sv = low_dot<KIND>(a.P + i * a.dim, static_cast<const uint4*>(a.Clow) + j * a.nvec, a.dim);
-          const float cc = __ldg(a.cc + j);
-          float d = exact_d<SROUND>(sv, pp, cc);
-          fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
-          if (fl) d = static_cast<float>(direct_dist_scalar<float, REC>(a.P + i * a.dim, a.C + j * a.dim, a.dim));
-          const unsigned long long k = make_key(d, static_cast<uint32_t>(j));
-          best = k < best ? k : best;
+  // G groups of 32 rows per step: their redo bytes, then their keys, load together
+  constexpr int G = 4;
+  for (int64_t base0 = gw * 32 * G; base0 < a.n; base0 += nw * 32 * G) {
+    unsigned balg[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int64_t ii = base0 + g * 32 + lane;
+      balg[g] = __ballot_sync(0xffffffffu, ii < a.n && a.redo[ii] != 0);
+    }
+#pragma unroll 1
+    for (int g = 0; g < G; ++g) {
+      const int64_t base = base0 + g * 32;
+      unsigned bal = balg[g];
+      while (bal) {
+        const int64_t i = base + (__ffs(bal) - 1);
+        bal &= bal - 1;
+        unsigned long long best = ~0ull;
+        const float pp = __ldg(a.pp + i);
+        for (int64_t j0 = 0; j0 < a.m; j0 += 32) {
+          const int64_t j = j0 + lane;
+          bool fl = false;
+          if (j < a.m) {
+            const float sv = low_dot<KIND>(a.P + i * a.dim, static_cast<const uint4*>(a.Clow) + j * a.nvec, a.dim);
+            const float cc = __ldg(a.cc + j);
+            float d = exact_d<SROUND>(sv, pp, cc);
+            fl = d <= __fmul_rn(a.K, __fadd_rn(pp, cc));
+            if (fl) d = static_cast<float>(direct_dist_scalar<float, REC>(a.P + i * a.dim, a.C + j * a.dim, a.dim));
+            const unsigned long long k = make_key(d, static_cast<uint32_t>(j));
+            best = k < best ? k : best;
+          }
+          nfl += __popc(__ballot_sync(0xffffffffu, fl));
         }
-        nfl += __popc(__ballot_sync(0xffffffffu, fl));
+        best = warp_min_u64(best);
+        if (lane == 0) a.row_key[i] = best;
       }
-      best = warp_min_u64(best);
-      if (lane == 0) a.row_key[i] = best;
     }
     __syncwarp();
-    if (ii < a.n) {
-      const unsigned long long k = a.row_key[ii];
-      const uint32_t j = static_cast<uint32_t>(k & 0xffffffffull);
-      if (a.labels) a.labels[ii] = j;
-      if (a.labels32) a.labels32[ii] = static_cast<int32_t>(j);
-      if (a.mind) a.mind[ii] = __uint_as_float(static_cast<uint32_t>(k >> 32));
+    unsigned long long kg[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int64_t ii = base0 + g * 32 + lane;
+      kg[g] = ii < a.n ? a.row_key[ii] : 0ull;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int64_t ii = base0 + g * 32 + lane;
+      if (ii < a.n) {
+        const uint32_t j = static_cast<uint32_t>(kg[g] & 0xffffffffull);
+        if (a.labels) a.labels[ii] = j;
+        if (a.labels32) a.labels32[ii] = static_cast<int32_t>(j);
+        if (a.mind) a.mind[ii] = __uint_as_float(static_cast<uint32_t>(kg[g] >> 32));
+      }
     }
   }
   if (lane == 0 && nfl) atomicAdd(a.count, nfl);
@@ -1031,7 +1051,7 @@ cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels3
   a.labels = labels;
   a.labels32 = labels32;
   a.mind = mind;
-  const int64_t warps = (j.n + 31) / 32;
+  const int64_t warps = (j.n + 127) / 128;  // four groups of 32 rows per warp step
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((warps + 7) / 8, static_cast<int64_t>(num_sms()) * 8));
 #define RD_CASE(KIND_, SR_, REC_)                                             \
   if (kind == KIND_ && s->sround == SR_ && s->rec == REC_) {                  \
