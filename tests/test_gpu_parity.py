@@ -396,3 +396,24 @@ def test_error_paths_on_gpu():
     e = euclidean_cuda_mix.pairwise_euclidean_fp16_fp32(cuda(np.zeros((0, 3), np.float32)), P)
     assert e.shape == (0, 4)
     device_check()
+
+
+@pytest.mark.parametrize("op", ["fp16_fp32", "bf16_fp32"])
+def test_fast_argmin_fused_rows_equal_prepared_rows(op):
+    """The screen reads 16-byte aligned fp32 points itself; a point matrix one float off
+    that alignment takes the prepared low-precision copy instead.  Both round, and sum
+    the norms, the same way: identical outputs."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    n, m, d = 5000, 700, 96
+    base = torch.randn(n * d + 1, generator=g, device=DEV)
+    P_off = base[1:].view(n, d)  # 4 bytes past a 16-byte boundary
+    P = P_off.clone()            # aligned copy of the same values
+    C = torch.randn(m, d, generator=g, device=DEV)
+    kappa = 5.0 if op.startswith("fp16") else 0.1
+    fn = getattr(euclidean_cuda_mix, f"pairwise_euclidean_{op}_argmin")
+    la, ma, ca = fn(P, C, kappa)
+    lb, mb, cb = fn(P_off, C, kappa)
+    torch.testing.assert_close(la, lb, rtol=0, atol=0)
+    torch.testing.assert_close(ma, mb, rtol=0, atol=0)
+    assert int(ca.item()) == int(cb.item())
+    device_check()
