@@ -20,6 +20,8 @@
 #include "common.cuh"
 #include "engine.h"
 
+#include <type_traits>
+
 namespace euc {
 
 template <typename TL> __device__ __forceinline__ int64_t load_label(const TL* p, int64_t i) {
@@ -284,6 +286,82 @@ __global__ void __launch_bounds__(256) segsum_kernel(const TX* __restrict__ X, i
   }
 }
 
+// fp32 rows with dim = 64 NV, 16-byte aligned: each half-warp walks every other
+// label-sorted position (lane l of a half holds float4s l, l + 16, ... of the row), so a
+// load instruction brings two rows and a warp keeps 2 RB rows in flight; each half
+// flushes its own sums per segment.
+template <int NV>
+__global__ void __launch_bounds__(256) segsum_h_kernel(const float* __restrict__ X, int dim, int k,
+                                                       const unsigned long long* __restrict__ offs,
+                                                       const unsigned int* __restrict__ perm,
+                                                       double* __restrict__ stats) {
+  constexpr int SEG = 1024;
+  constexpr int RB = 4;
+  const int64_t total = static_cast<int64_t>(offs[k]);
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t p0 = gw * SEG;
+  if (p0 >= total) return;
+  const int64_t p1 = min(total, p0 + SEG);
+  const int64_t q0 = p0 + half;  // this half's first position
+  int c = 0;
+  unsigned long long cend = 0;
+  if (q0 < p1) {
+    int lo = 0, hi = k;  // invariant offs[lo] <= q0 < offs[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (offs[mid] <= static_cast<unsigned long long>(q0)) lo = mid; else hi = mid;
+    }
+    c = lo;
+    cend = offs[c + 1];
+  }
+  double acc[NV][4];
+#pragma unroll
+  for (int q = 0; q < NV; ++q)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[q][e] = 0.0;
+  const int w = dim + 1;
+  auto flush = [&]() {
+#pragma unroll
+    for (int q = 0; q < NV; ++q)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (acc[q][e] != 0.0) atomicAdd(stats + static_cast<int64_t>(c) * w + 64 * q + 4 * hl + e, acc[q][e]);
+        acc[q][e] = 0.0;
+      }
+  };
+  for (int64_t pb = q0; pb < p1; pb += 2 * RB) {
+    int64_t row[RB];
+#pragma unroll
+    for (int u = 0; u < RB; ++u) row[u] = (pb + 2 * u < p1) ? static_cast<int64_t>(perm[pb + 2 * u]) : -1;
+    float4 v[RB][NV];
+#pragma unroll
+    for (int u = 0; u < RB; ++u)
+#pragma unroll
+      for (int q = 0; q < NV; ++q)
+        v[u][q] = row[u] >= 0 ? __ldg(reinterpret_cast<const float4*>(X + row[u] * dim + 64 * q) + hl)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < RB; ++u) {
+      const int64_t p = pb + 2 * u;
+      if (p >= p1) break;
+      while (static_cast<unsigned long long>(p) >= cend) {
+        flush();
+        ++c;
+        cend = offs[c + 1];
+      }
+#pragma unroll
+      for (int q = 0; q < NV; ++q) {
+        acc[q][0] += static_cast<double>(v[u][q].x);
+        acc[q][1] += static_cast<double>(v[u][q].y);
+        acc[q][2] += static_cast<double>(v[u][q].z);
+        acc[q][3] += static_cast<double>(v[u][q].w);
+      }
+    }
+  }
+  if (q0 < p1) flush();
+}
+
 static inline size_t al(size_t b) { return (b + 255) & ~size_t(255); }
 
 static bool use_smem(int64_t dim, int64_t k) { return k * (dim + 1) * 8 <= 48 * 1024; }
@@ -351,6 +429,16 @@ static cudaError_t stats_t(const TX* X, const TL* labels, int64_t n, int dim, in
   // clamps to offs[k] on the device.
   const int64_t warps = (n + 1023) / 1024;
   const int64_t sblocks = (warps + 7) / 8;
+  if constexpr (std::is_same<TX, float>::value) {
+    if (dim % 64 == 0 && dim <= 256 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0) {
+      const unsigned b = static_cast<unsigned>(sblocks);
+      if (dim == 64) segsum_h_kernel<1><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
+      else if (dim == 128) segsum_h_kernel<2><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
+      else if (dim == 192) segsum_h_kernel<3><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
+      else segsum_h_kernel<4><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
+      return cudaGetLastError();
+    }
+  }
   const int npl = (dim + 31) / 32;
 #define SEG(NPL_)                                                                                        \
   if (npl <= NPL_) {                                                                                     \
