@@ -57,6 +57,8 @@ _SIGS = {
     "euc_center_stats_workspace_bytes": ([_I64, _I64, _I64], _SZ),
     "euc_center_stats": ([_V, _I, _V, _I, _I64, _I64, _I64, _V, _V, _SZ, _V], _I),
     "euc_center_finalize": ([_V, _I64, _I64, _V, _I, _V, _I, _V], _I),
+    "euc_kmeanspp_workspace_bytes": ([_I64, _I64, _I64], _SZ),
+    "euc_kmeanspp": ([_V, _I, _I64, _I64, _I64, ctypes.c_uint64, _V, _V, _V, _SZ, _V], _I),
 }
 for _n in ("fp16_fp64", "bf16_fp64", "tf32_fp64", "fp32_fp64", "fp16_fp16", "fp16_fp32", "bf16_bf16",
            "bf16_fp32", "fp32_fp32"):

@@ -595,6 +595,25 @@ int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* cente
   return e == cudaSuccess ? EUC_OK : cuda_fail(e, "center_finalize");
 }
 
+// ------------------------------------------------------------------ seeding
+size_t euc_kmeanspp_workspace_bytes(int64_t n, int64_t dim, int64_t k) {
+  (void)dim;
+  (void)k;
+  return n > 0 ? seed_ws_bytes(n) : 0;
+}
+
+int euc_kmeanspp(const void* X, int x_is_f64, int64_t n, int64_t dim, int64_t k, uint64_t seed, int64_t* indices,
+                 void* centers, void* ws, size_t ws_bytes, void* stream) {
+  if (n <= 0 || dim <= 0 || k <= 0 || k > n) return fail(EUC_ERR_SHAPE, "kmeanspp: need 1 <= k <= n and dim >= 1");
+  if (dim > (1 << 20) || n > (1ll << 40)) return fail(EUC_ERR_SHAPE, "kmeanspp: shape too large");
+  if (!X || !indices) return fail(EUC_ERR_ARG, "null pointer");
+  if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
+  if (!ws || ws_bytes < seed_ws_bytes(n)) return fail(EUC_ERR_WORKSPACE, "kmeanspp: workspace too small");
+  cudaError_t e = launch_kmeanspp(X, x_is_f64 != 0, n, dim, k, seed, indices, centers, ws,
+                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? EUC_OK : cuda_fail(e, "kmeanspp");
+}
+
 // ------------------------------------------------------------------ fused argmin
 int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa, int exact,
                int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count, void* ws, size_t ws_bytes,

@@ -154,6 +154,11 @@ cudaError_t launch_center_stats(const void* X, bool x_f64, const void* labels, b
 cudaError_t launch_center_finalize(const double* stats, int64_t dim, int64_t k, void* centers, bool f64,
                                    const void* prev, int empty_policy, cudaStream_t st);
 
+// k-means++ seeding (k_seed.cu): indices (int64[k]) and, if non-null, the chosen rows.
+size_t seed_ws_bytes(int64_t n);
+cudaError_t launch_kmeanspp(const void* X, bool x_f64, int64_t n, int64_t dim, int64_t k, uint64_t seed,
+                            int64_t* idx, void* centers, void* ws, cudaStream_t st);
+
 // Kernel timing hook (api.cu).
 void timing_begin(cudaStream_t st, const char* name);
 void timing_end(cudaStream_t st);

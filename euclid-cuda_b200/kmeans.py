@@ -80,6 +80,22 @@ class LloydKMeans:
         return C, labels
 
 
+def kmeanspp(X, k, seed=0):
+    """k-means++ seeding on X's device (euc_kmeanspp): returns (centers k x dim in X's
+    type, row indices int64[k]); deterministic for a given seed.  Single device: with
+    sharded rows, seed on one rank and broadcast the centers."""
+    X = X.contiguous()
+    n, d = X.shape
+    if X.dtype not in (torch.float32, torch.float64):
+        raise RuntimeError("kmeanspp: X must be float32 or float64")
+    idx = torch.empty(int(k), dtype=torch.int64, device=X.device)
+    centers = torch.empty((int(k), d), dtype=X.dtype, device=X.device)
+    ws = workspace(lib().euc_kmeanspp_workspace_bytes(n, d, int(k)), X.device)
+    check(lib().euc_kmeanspp(ptr(X), int(X.dtype == torch.float64), n, d, int(k), int(seed) & (2 ** 64 - 1),
+                             ptr(idx), ptr(centers), ptr(ws), ws.numel(), stream_of(X)))
+    return centers, idx
+
+
 def shard_rows(n, rank, world):
     """Contiguous row range [lo, hi) of rank `rank` out of `world`."""
     base, rem = divmod(n, world)

@@ -259,6 +259,19 @@ EUC_API int euc_center_stats(const void* X, int x_is_f64, const void* labels, in
 EUC_API int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* centers,
                         int centers_are_f64, const void* prev, int empty_policy, void* stream);
 
+/* No counterpart in the reference: k-means++ seeding, the caller-side step before the
+ * Lloyd loop, on the device and deterministic for a given `seed`.  Row 0 of the
+ * chosen set is uniform over the n rows; each next row is drawn with probability
+ * proportional to its squared distance to the nearest chosen row (the fp64 direct sum
+ * in dimension order), the weights scaled to exact 62-bit integers so that the draw
+ * does not depend on summation order; draw s uses the top 53 bits of
+ * SplitMix64(seed + (s + 1) * 0x9E3779B97F4A7C15).  Writes indices (int64[k], device)
+ * and, if non-null, centers (k x dim rows of X, X's type).  One host-side launch
+ * sequence of 3 kernels per center; `ws` of euc_kmeanspp_workspace_bytes(). */
+EUC_API size_t euc_kmeanspp_workspace_bytes(int64_t n, int64_t dim, int64_t k);
+EUC_API int euc_kmeanspp(const void* X, int x_is_f64, int64_t n, int64_t dim, int64_t k, uint64_t seed,
+                 int64_t* indices, void* centers, void* ws, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

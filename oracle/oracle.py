@@ -370,6 +370,53 @@ def center_stats(X, labels, k):
     return st
 
 
+# ------------------------------------------------------------- k-means++
+_GOLDEN_GAMMA = 0x9E3779B97F4A7C15
+_M64 = (1 << 64) - 1
+
+
+def seed_draw53(seed, s):
+    """Top 53 bits of SplitMix64(seed + (s + 1) * golden gamma) (the published SplitMix64
+    finaliser), as the engine's k-means++ draws them."""
+    z = (seed + (s + 1) * _GOLDEN_GAMMA) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    z ^= z >> 31
+    return z >> 11
+
+
+def kmeanspp(X, k, seed=0):
+    """Deterministic k-means++ seeding as euc_kmeanspp defines it: row 0 uniform, then
+    D^2 sampling with the fp64 direct distance (dimension order), weights scaled to
+    exact integers q = floor(D 2^S), S = 62 - ceil(log2 n) - (floor(log2 max D) + 1),
+    target floor(r * sum q / 2^53), the first row whose running sum exceeds it; all
+    weights 0 -> uniform.  Returns the int64 row indices."""
+    n = X.shape[0]
+    idx = [(seed_draw53(seed, 0) * n) >> 53]
+    D = None
+    lg = (n - 1).bit_length()  # ceil(log2 n)
+    rows = np.arange(n)
+    for s in range(1, k):
+        d2 = direct_pairs("fp64", X, X, rows, np.full(n, idx[-1]))
+        d2 = np.where(np.isnan(d2), 0.0, d2)
+        D = d2 if D is None else np.fmin(D, d2)
+        r = seed_draw53(seed, s)
+        maxd = float(D.max())
+        if maxd > 0.0:
+            S = 62 - lg - int(np.frexp(maxd)[1])  # frexp exponent = floor(log2) + 1
+            q = np.ldexp(D, S).astype(np.uint64)
+            total = int(q.sum(dtype=np.uint64))
+        else:
+            total = 0
+        if total == 0:
+            idx.append((r * n) >> 53)
+            continue
+        t = (r * total) >> 53
+        run = np.cumsum(q, dtype=np.uint64)
+        idx.append(int(np.searchsorted(run, np.uint64(t), side="right")))
+    return np.asarray(idx, np.int64)
+
+
 # ------------------------------------------------------------ CPU baseline
 def dist_argmin_f64(P, C, threads=0):
     """fp64 distance + argmin on the host cores; returns (labels, min dist, threads used)."""

@@ -125,3 +125,27 @@ def test_c5b_wide_fp16_inputs():
     assert sure.mean() > 0.25
     np.testing.assert_array_equal(lab.cpu().numpy()[sure], lo[sure])
     device_check()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("n,d,k,seed", [(5000, 16, 20, 1), (3000, 64, 64, 7), (1025, 3, 10, 123), (7, 2, 7, 5)])
+def test_kmeanspp_matches_oracle(n, d, k, seed, dtype):
+    """k-means++ seeding on the device picks the same rows as the oracle's restatement
+    (integer weights: the draw does not depend on summation order)."""
+    from kmeans import kmeanspp
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(n, d)).astype(dtype)
+    X[: n // 10] = X[0]  # duplicated rows: weight 0 once one of them is chosen
+    C, idx = kmeanspp(cuda(X), k, seed=seed)
+    io = O.kmeanspp(X, k, seed=seed)
+    np.testing.assert_array_equal(idx.cpu().numpy(), io)
+    np.testing.assert_array_equal(C.cpu().numpy(), X[io])
+    device_check()
+
+
+def test_kmeanspp_all_rows_equal_draws_uniformly():
+    from kmeans import kmeanspp
+    X = np.ones((300, 4), np.float32)
+    _, idx = kmeanspp(cuda(X), 5, seed=3)
+    np.testing.assert_array_equal(idx.cpu().numpy(), O.kmeanspp(X, 5, seed=3))
+    device_check()

@@ -131,3 +131,14 @@ def test_cpu_baseline_argmin():
     np.testing.assert_array_equal(lab, D.argmin(1))
     np.testing.assert_allclose(md, D.min(1), rtol=1e-12, atol=1e-12)
     assert used >= 1
+
+
+def test_kmeanspp_oracle_draws_distinct_rows():
+    """D^2 sampling never re-draws a chosen row while another row has weight > 0; the
+    first row is the uniform draw floor(r_0 n / 2^53)."""
+    rng = np.random.default_rng(0)
+    X = rng.normal(size=(400, 5))
+    idx = O.kmeanspp(X, 30, seed=11)
+    assert len(set(idx.tolist())) == 30
+    assert idx[0] == (O.seed_draw53(11, 0) * 400) >> 53
+    assert 0 <= O.seed_draw53(2 ** 64 - 1, 5) < 2 ** 53
