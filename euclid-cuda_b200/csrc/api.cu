@@ -605,7 +605,7 @@ size_t euc_kmeanspp_workspace_bytes(int64_t n, int64_t dim, int64_t k) {
 int euc_kmeanspp(const void* X, int x_is_f64, int64_t n, int64_t dim, int64_t k, uint64_t seed, int64_t* indices,
                  void* centers, void* ws, size_t ws_bytes, void* stream) {
   if (n <= 0 || dim <= 0 || k <= 0 || k > n) return fail(EUC_ERR_SHAPE, "kmeanspp: need 1 <= k <= n and dim >= 1");
-  if (dim > (1 << 20) || n > (1ll << 40)) return fail(EUC_ERR_SHAPE, "kmeanspp: shape too large");
+  if (dim > (1 << 20) || n > (1ll << 40) || k > 0x7fffffffll) return fail(EUC_ERR_SHAPE, "kmeanspp: shape too large");
   if (!X || !indices) return fail(EUC_ERR_ARG, "null pointer");
   if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
   if (!ws || ws_bytes < seed_ws_bytes(n)) return fail(EUC_ERR_WORKSPACE, "kmeanspp: workspace too small");
