@@ -9,16 +9,19 @@
 //    4 groups (b, column half), one warp per TMEM lane quadrant, so a group has two
 //    tile times to drain its half of an accumulator while the next tile's MMAs proceed;
 //  * centers arrive sorted by norm (stable); a 4-slot ring of 1-D bulk copies brings
-//    each center tile's norms into shared memory ahead of use;
+//    each center tile's norms into shared memory ahead of use, and the tile's extra-K
+//    rows ride in the stage of its last K block;
 //  * one extra 32-byte K block (aux.cuh) adds y0 = (cc_j + Br_i)/2 to the accumulator of
 //    pair (i, j) (Br_i = 1.0625 pp_i, centers stored negated), so the MMA yields
 //    y = y0 - s >= 0 directly; per 32-column chunk an epilogue warp replaces the low 5
 //    mantissa bits of y with the column (one LOP3) and takes the minimum with a
 //    depth-4 tree of 3-way mins;
 //  * two row warps build each row tile's extra-K rows and its norms; for the fp16/bf16
-//    operators whose norms are those of the rounded values they also read the fp32
-//    points themselves (FUSED): round, accumulate the norm in dimension order and write
-//    the 128B-swizzled A tile, so the points are never staged in HBM;
+//    operators whose norms are those of the rounded values they also take the fp32
+//    points themselves (FUSED): the next row tile's points arrive by TMA in a staging
+//    buffer while the current one is used, and the row warps round them into the
+//    128B-swizzled A tile, accumulating the norms in dimension order, so no
+//    low-precision copy of the points is written to HBM;
 //  * a chunk in which some pair could meet the cancellation test
 //        d <= K (pp + cc)  <=>  2 s >= (1 - K)(pp + cc)  (up to rounding margins)
 //    -- bounded with the chunk's smallest and largest norm, tight because norms are
@@ -66,7 +69,8 @@ constexpr int TF_A_KB = TF_BM * 128;  // one 128-row x 128-byte K block of A
 constexpr int TF_B_KB = TF_BN * 128;  // one 256-row x 128-byte K block of B
 constexpr int TF_SLOTS = 4;             // center-metadata ring
 constexpr int TF_BAUX_BYTES = TF_BN * 32;  // the tile's extra-K rows (32 bytes each)
-constexpr int TF_META_BYTES = TF_BAUX_BYTES + TF_BN * 4;  // + the tile's sorted center norms
+constexpr int TF_META_BYTES = TF_BN * 4;  // the tile's sorted center norms
+constexpr int TF_XBOX_BYTES = 32 * 4 * TF_BM;  // FUSED staging: 32 fp32 values of the 128 rows
 constexpr int TF_AAUX_BYTES = TF_BM * 32;       // per A buffer: the rows' extra-K rows
 constexpr int TF_ROWBUF_BYTES = 2 * TF_BM * 4;  // per A buffer: pp and Br of each row
 constexpr int TF_BAR_BYTES = 512;
@@ -91,55 +95,46 @@ struct TfArgs {
   uint8_t* redo;
 };
 
-// FUSED row preparation of one point row: its fp32 values rounded to the operand type
-// (fp16 / bf16, round to nearest even) into the A buffer, K-major with the 128-byte
-// swizzle the MMA descriptor names (16-byte chunk q of row r in K block kb at
-// kb * 16K + (r / 8) * 1024 + (r % 8) * 128 + ((q ^ r % 8) * 16)), and its norm: fused
-// multiply-adds of the rounded values in dimension order, rounded to the operand type
-// (the NM_LOW_F16 / NM_LOW_BF16 recipes of the standalone preparation).  Rows past n and
-// dimensions past dim are zeros.
+// FUSED row preparation, one staged box: 32 fp32 values of row r of the row tile (TMA
+// with the 128-byte swizzle: 16-byte chunk j of row r at r * 128 + ((j ^ r % 8) * 16))
+// rounded to the operand type (fp16 / bf16, round to nearest even) into K block kq / 2,
+// chunks 4 (kq % 2) .. + 3 of row r of A, K-major with the 128-byte swizzle the MMA
+// descriptor names (chunk q of row r in K block kb at kb * 16K + (r / 8) * 1024 +
+// (r % 8) * 128 + ((q ^ r % 8) * 16)); the row's norm continues over them: fused
+// multiply-adds of the rounded values in dimension order (the NM_LOW_F16 /
+// NM_LOW_BF16 recipes of the standalone preparation).
 template <int KIND>
-__device__ __forceinline__ float fused_row(const float* __restrict__ xr, int dim, int kblocks, uint8_t* sA, int r,
-                                           bool valid) {
+__device__ __forceinline__ float convert_box(const uint8_t* box, int r, uint8_t* sA, int kq, float acc) {
   static_assert(KIND == 0 || KIND == 1, "fp16 / bf16 operands");
-  float acc = 0.f;
-  uint8_t* rowp = sA + (r >> 3) * 1024 + (r & 7) * 128;
-  const int sw = r & 7;
-  const int d4 = valid ? (dim >> 2) : 0;
-  const float4* x4 = reinterpret_cast<const float4*>(xr);
-  for (int kb = 0; kb < kblocks; ++kb) {
-    float4 v[16];
+  const uint8_t* src = box + r * 128;
+  uint8_t* rowp = sA + (kq >> 1) * TF_A_KB + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int q = kb * 16 + u;
-      v[u] = q < d4 ? __ldg(x4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    uint8_t* kp = rowp + kb * TF_A_KB;
+  for (int jj = 0; jj < 4; ++jj) {
+    const float4 p0 = *reinterpret_cast<const float4*>(src + (((2 * jj) ^ (r & 7)) << 4));
+    const float4 p1 = *reinterpret_cast<const float4*>(src + (((2 * jj + 1) ^ (r & 7)) << 4));
+    const float x[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    uint32_t w[4];
 #pragma unroll
-    for (int u = 0; u < 16; u += 2) {
-      const float x[8] = {v[u].x, v[u].y, v[u].z, v[u].w, v[u + 1].x, v[u + 1].y, v[u + 1].z, v[u + 1].w};
-      uint32_t w[4];
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float lo, hi;
-        if constexpr (KIND == 0) {
-          const __half2 t = __floats2half2_rn(x[2 * h], x[2 * h + 1]);
-          w[h] = *reinterpret_cast<const uint32_t*>(&t);
-          lo = __low2float(t);
-          hi = __high2float(t);
-        } else {
-          const __nv_bfloat162 t = __floats2bfloat162_rn(x[2 * h], x[2 * h + 1]);
-          w[h] = *reinterpret_cast<const uint32_t*>(&t);
-          lo = __low2float(t);
-          hi = __high2float(t);
-        }
-        acc = __fmaf_rn(lo, lo, acc);
-        acc = __fmaf_rn(hi, hi, acc);
+    for (int h = 0; h < 4; ++h) {
+      float lo, hi;
+      if constexpr (KIND == 0) {
+        const __half2 t = __floats2half2_rn(x[2 * h], x[2 * h + 1]);
+        w[h] = *reinterpret_cast<const uint32_t*>(&t);
+        lo = __low2float(t);
+        hi = __high2float(t);
+      } else {
+        const __nv_bfloat162 t = __floats2bfloat162_rn(x[2 * h], x[2 * h + 1]);
+        w[h] = *reinterpret_cast<const uint32_t*>(&t);
+        lo = __low2float(t);
+        hi = __high2float(t);
       }
-      *reinterpret_cast<uint4*>(kp + (((u >> 1) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      acc = __fmaf_rn(lo, lo, acc);
+      acc = __fmaf_rn(hi, hi, acc);
     }
+    const int q = 4 * (kq & 1) + jj;
+    *reinterpret_cast<uint4*>(rowp + ((q ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  return KIND == 0 ? round_f16(acc) : round_bf16(acc);
+  return acc;
 }
 
 template <int KIND, bool FUSED>
@@ -152,10 +147,14 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   const bool a_res = a.a_res != 0;
   const int KB = a.kblocks;
   const uint32_t a_bytes = static_cast<uint32_t>(KB) * TF_A_KB;                   // all K blocks of A
-  const uint32_t stage_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);  // B  |  A B
+  // a stage: B  |  A B, then room for the tile's extra-K rows (used by its last K block)
+  const uint32_t ab_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);
+  const uint32_t stage_bytes = ab_bytes + TF_BAUX_BYTES;
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
-  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x (256 extra-K rows, 256 sorted norms)
-  uint8_t* aaux = meta + TF_SLOTS * TF_META_BYTES; // per A buffer: the A side of the extra K block
+  uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 256 sorted norms
+  const int nbox = (a.dim + 31) >> 5;              // FUSED: staged 32-value boxes per row
+  uint8_t* xst = meta + TF_SLOTS * TF_META_BYTES;  // FUSED: the next row tile's fp32 points
+  uint8_t* aaux = xst + (FUSED ? nbox * TF_XBOX_BYTES : 0);  // per A buffer: the A side of the extra K block
   float* rowbuf = reinterpret_cast<float*>(aaux + 2 * TF_AAUX_BYTES);  // per A buffer: pp[128], Br[128]
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(rowbuf) + 2 * TF_ROWBUF_BYTES);
   uint64_t* empty = full + NST;
@@ -166,7 +165,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   uint64_t* metaf = acce + 2;
   uint64_t* metae = metaf + TF_SLOTS;
   uint64_t* pempty = metae + TF_SLOTS;  // per A buffer: every epilogue warp has read its rows' pp, Br
-  uint64_t* drain = pempty + 2;
+  uint64_t* xfull = pempty + 2;         // FUSED staging: the row tile's points have landed
+  uint64_t* xempty = xfull + 1;         // FUSED staging: every row thread has read them
+  uint64_t* drain = xempty + 1;
   uint64_t* mfull = drain + 1;   // row merge: groups 1..3 have published their row minima
   uint64_t* mdone = mfull + 1;   // row merge: group 0 has consumed them
   unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
@@ -189,6 +190,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&afull[s], afull_count);
       mbar_init(&aempty[s], 1);
       mbar_init(&pempty[s], TF_EPI_WARPS);
+      if (s == 0) {
+        mbar_init(xfull, 1);
+        mbar_init(xempty, TF_ROW_THREADS);
+      }
       mbar_init(&accf[s], 1);
       mbar_init(&acce[s], TF_EPI_WARPS / 2);
     }
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   }
   if (warp == TF_W_MMA) tmem_alloc(tmem_slot, kCols);
   if (warp == TF_W_PRODUCER && lane == 0) {
-    if (!FUSED) prefetch_tmap(&tmA);
+    prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmBaux);
   }
@@ -238,20 +243,21 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* ms = meta + slot * TF_META_BYTES;
           mbar_arrive_expect_tx(&metaf[slot], TF_META_BYTES);
-          tma_load_2d(ms, &tmBaux, &metaf[slot], 0, ct * TF_BN);
-          bulk_load_1d(ms + TF_BAUX_BYTES, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
+          bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
           m_issued |= 1u << slot;
           m_last = (m_last & ~(1u << slot)) | (su << slot);
           for (int kb = 0; kb < KB; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
             uint8_t* st = stage_base + stage * stage_bytes;
-            mbar_arrive_expect_tx(&full[stage], stage_bytes);
+            const bool last_kb = kb == KB - 1;
+            mbar_arrive_expect_tx(&full[stage], last_kb ? stage_bytes : ab_bytes);
             if (a_res) {
               tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * TF_BN);
             } else {
               tma_load_2d(st, &tmA, &full[stage], kb * kelems, row0);
               tma_load_2d(st + TF_A_KB, &tmB, &full[stage], kb * kelems, ct * TF_BN);
             }
+            if (last_kb) tma_load_2d(st + ab_bytes, &tmBaux, &full[stage], 0, ct * TF_BN);
             issued_mask |= 1u << stage;
             last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
@@ -303,21 +309,18 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
               else
                 umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
             }
+            if (kb == KB - 1) {
+              // the extra K block: adds (cc_j + Br_i) / 2 to the accumulator of pair (i, j)
+              const uint64_t bd = sw32_kmajor_desc(st + ab_bytes);
+              if constexpr (KIND == 2)
+                umma_tf32(d_tmem, aux_ad, bd, idesc, 1u);
+              else
+                umma_f16(d_tmem, aux_ad, bd, idesc, 1u);
+            }
             umma_commit(&empty[stage]);
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          // the extra K block: adds y0_j = (cc_j + B) / 2 to every row of column j
-          {
-            const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
-            if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t bd = sw32_kmajor_desc(smem_u32(meta + slot * TF_META_BYTES));
-            if constexpr (KIND == 2)
-              umma_tf32(tmem_base + b * TF_BN, aux_ad, bd, idesc, 1u);
-            else
-              umma_f16(tmem_base + b * TF_BN, aux_ad, bd, idesc, 1u);
-          }
           umma_commit(&accf[b]);
         }
         if (ok) umma_commit(&aempty[abuf]);
@@ -380,7 +383,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
         const int64_t jt = static_cast<int64_t>(ct) * TF_BN + hc * 128;  // first (sorted) column of this warp
         if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
-        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES + TF_BAUX_BYTES) + hc * 128;
+        const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES) + hc * 128;
         const int64_t remt = a.m - jt;
         const int nvt = remt <= 0 ? 0 : (remt >= 128 ? 128 : static_cast<int>(remt));
         float u_own = 0.f;  // lane L < 4: U of chunk L
@@ -509,14 +512,26 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     // ------------------------------------------------------------ row preparation
     // Thread c owns rows c and c + 64 of each row tile: their pp and Br for the epilogue
     // and their extra-K rows [2^E, 2^E, 2^E, parts of Br / 2 * 2^-E] for the MMA; with
-    // FUSED also the rows of A and pp itself.  A row whose norm is not finite or does
-    // not fit the extra K block gets a zero row term and is marked for the exact redo.
+    // FUSED also the rows of A and pp itself, from the staged fp32 points (tmA maps
+    // them in 32-value x 128-row boxes; thread 0 loads the CTA's next row tile into the
+    // staging buffer once every row thread has read the current one, a row tile ahead
+    // of its use).  A row whose norm is not finite or does not fit the extra K block
+    // gets a zero row term and is marked for the exact redo.
     const int c = threadIdx.x - TF_W_ROW0 * 32;
     const int E = __ldg(a.aux_e);
     const bool screen = E < kAuxNoScreen;
     const float sc = screen ? ldexpf(1.f, -E) : 0.f;
     const uint32_t te = screen ? low_bits<KIND>(ldexpf(1.f, E)) : 0u;
     const float kNaN = __int_as_float(0x7fc00000);
+    bool x_pending = false;  // FUSED: a staged load this thread issued is in flight
+    if constexpr (FUSED) {
+      if (c == 0 && static_cast<int64_t>(blockIdx.x) < a.n_rt) {
+        mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(nbox * TF_XBOX_BYTES));
+        for (int bx = 0; bx < nbox; ++bx)
+          tma_load_2d(xst + bx * TF_XBOX_BYTES, &tmA, xfull, bx * 32, static_cast<int>(blockIdx.x) * TF_BM);
+        x_pending = true;
+      }
+    }
     uint32_t rt_i = 0;
     bool ok = true;
     for (int64_t rt = blockIdx.x; rt < a.n_rt; rt += gridDim.x, ++rt_i) {
@@ -527,16 +542,41 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         ok = false;
         break;
       }
+      float acc0 = 0.f, acc1 = 0.f;
       if constexpr (FUSED) {
-        // this CTA's next row tile into L2 while this one is read
+        if (!mbar_wait(xfull, rt_i & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (c == 0) x_pending = false;
+        uint8_t* sA = smem + abuf * a_bytes;
+        for (int bx = 0; bx < nbox; ++bx) {
+          acc0 = convert_box<KIND>(xst + bx * TF_XBOX_BYTES, c, sA, bx, acc0);
+          acc1 = convert_box<KIND>(xst + bx * TF_XBOX_BYTES, c + 64, sA, bx, acc1);
+        }
+        if (nbox & 1) {  // an odd number of boxes leaves the upper half of the last K block
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int r = c + 64 * h;
+            uint8_t* rowp = sA + (KB - 1) * TF_A_KB + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int q = 4; q < 8; ++q)
+              *reinterpret_cast<uint4*>(rowp + ((q ^ (r & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        mbar_arrive(xempty);
+        // the CTA's next row tile into the staging buffer, once every row thread is done
         const int64_t nrt = rt + gridDim.x;
         if (c == 0 && nrt < a.n_rt) {
-          const int64_t r0 = nrt * TF_BM;
-          const int64_t rows = (a.n - r0) < TF_BM ? (a.n - r0) : TF_BM;
-          const uint64_t bytes = static_cast<uint64_t>(rows) * static_cast<uint64_t>(a.dim) * 4u;
-          const char* src = reinterpret_cast<const char*>(a.X + r0 * a.dim);
-          for (uint64_t off = 0; off < bytes; off += 32768u)
-            bulk_prefetch_l2(src + off, static_cast<uint32_t>(bytes - off < 32768u ? bytes - off : 32768u));
+          if (!mbar_wait(xempty, rt_i & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_async_shared();
+          mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(nbox * TF_XBOX_BYTES));
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(xst + bx * TF_XBOX_BYTES, &tmA, xfull, bx * 32, static_cast<int>(nrt * TF_BM));
+          x_pending = true;
         }
       }
       float* rb = rowbuf + abuf * 2 * TF_BM;
@@ -548,7 +588,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const bool valid = i < a.n;
         float pp;
         if constexpr (FUSED) {
-          pp = fused_row<KIND>(a.X + (valid ? i : 0) * a.dim, a.dim, KB, smem + abuf * a_bytes, r, valid);
+          const float ah = h ? acc1 : acc0;
+          pp = KIND == 0 ? round_f16(ah) : round_bf16(ah);
           if (valid) a.pp[i] = pp;
         } else {
           pp = valid ? __ldg(a.pp + i) : 0.f;
@@ -577,6 +618,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       *abort_flag = 1;
       if (c == 0) atomicExch(&s_tf_err, DEV_TIMEOUT_ROWS);
     }
+    // a staged load still in flight lands before the CTA exits
+    if (x_pending) {
+      volatile int no_abort = 0;
+      mbar_wait(xfull, rt_i & 1u, &no_abort);
+    }
   }
 
   tc_fence_before();
@@ -594,25 +640,31 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 constexpr size_t TF_SMEM_LIMIT = 232448;
 constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + 2 * TF_AAUX_BYTES +
                             2 * TF_ROWBUF_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
+constexpr size_t TF_STAGE_EXTRA = TF_BAUX_BYTES;  // a stage's room for the tile's extra-K rows
+
+// FUSED staging: the row tile's fp32 points, 32 values of each row per box
+static size_t tf_xstage_bytes(int dim) { return static_cast<size_t>((dim + 31) / 32) * TF_XBOX_BYTES; }
 
 // Resident A (the row tile, double-buffered) with B-only stages when that leaves room
-// for 3 stages, else streaming (A B) stages.
-static void tf_pipeline(int kblocks, int* nst, int* a_res) {
+// for 3 stages (2 when the staging buffer of FUSED takes its share), else streaming
+// (A B) stages; FUSED needs resident A.
+static void tf_pipeline(int kblocks, size_t xbytes, int* nst, int* a_res) {
   const size_t abytes = static_cast<size_t>(kblocks) * TF_A_KB;
-  const size_t avail = TF_SMEM_LIMIT - TF_FIXED;
-  if (2 * abytes + 3 * TF_B_KB <= avail) {
+  const size_t avail = TF_SMEM_LIMIT - TF_FIXED - xbytes;
+  const size_t bst = TF_B_KB + TF_STAGE_EXTRA;
+  const size_t min_st = xbytes ? 2 : 3;
+  if (2 * abytes + min_st * bst <= avail) {
     *a_res = 1;
-    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / TF_B_KB));
+    *nst = static_cast<int>(std::min<size_t>(8, (avail - 2 * abytes) / bst));
   } else {
     *a_res = 0;
-    *nst = static_cast<int>(std::min<size_t>(8, avail / (TF_A_KB + TF_B_KB)));
+    *nst = xbytes ? 0 : static_cast<int>(std::min<size_t>(8, avail / (TF_A_KB + bst)));
   }
 }
-
-static size_t tf_smem_bytes(int kblocks, int nst, int a_res) {
-  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TF_A_KB + nst * static_cast<size_t>(TF_B_KB)
-                            : nst * static_cast<size_t>(TF_A_KB + TF_B_KB);
-  return TF_FIXED + body;
+static size_t tf_smem_bytes(int kblocks, int nst, int a_res, size_t xbytes) {
+  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TF_A_KB + nst * (TF_B_KB + TF_STAGE_EXTRA)
+                            : nst * (TF_A_KB + TF_B_KB + TF_STAGE_EXTRA);
+  return TF_FIXED + xbytes + body;
 }
 
 int tc_fast_regions(int64_t n) {
@@ -626,7 +678,7 @@ template <int KIND, bool FUSED>
 static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tba,
                                const TfArgs& args, int grid, cudaStream_t st) {
   auto kern = dist_tc_fast_kernel<KIND, FUSED>;
-  const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res);
+  const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res, FUSED ? tf_xstage_bytes(args.dim) : 0);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   timing_begin(st, "dist_tc_fast_kernel");
@@ -652,7 +704,7 @@ bool tc_fast_can_fuse_rows(const DistJob& j) {
   if (!recipe || s->in != IN_F32) return false;
   if (j.dim % 4 != 0 || (reinterpret_cast<uintptr_t>(j.P) & 15u) != 0) return false;
   int nst = 0, a_res = 0;
-  tf_pipeline(tf_kblocks(j), &nst, &a_res);
+  tf_pipeline(tf_kblocks(j), tf_xstage_bytes(j.dim), &nst, &a_res);
   return a_res != 0 && nst >= 2;
 }
 
@@ -667,7 +719,7 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.kblocks = tf_kblocks(j);
   a.n_ct = static_cast<int>((j.m + TF_BN - 1) / TF_BN);
   a.n_rt = (j.n + TF_BM - 1) / TF_BM;
-  tf_pipeline(a.kblocks, &a.nst, &a.a_res);
+  tf_pipeline(a.kblocks, j.fused_rows ? tf_xstage_bytes(j.dim) : 0, &a.nst, &a.a_res);
   if (a.nst < 2) return cudaErrorInvalidValue;
   if (j.fused_rows && !tc_fast_can_fuse_rows(j)) return cudaErrorInvalidValue;
   a.pp = static_cast<float*>(j.pp);
@@ -688,9 +740,13 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.redo = j.redo;
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
-  CUtensorMap ta{}, tb;  // A: the low-precision copy (unused with FUSED)
-  if (!j.fused_rows && !tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1))
+  // A: the low-precision copy, or with FUSED the fp32 points in 32-value x 128-row boxes
+  CUtensorMap ta, tb;
+  if (j.fused_rows) {
+    if (!tc_make_tmap(&ta, j.P, j.n, j.dim, 4, TF_BM, true, false)) return cudaErrorInvalidValue;
+  } else if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1)) {
     return cudaErrorInvalidValue;
+  }
   if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
   CUtensorMap tba;
