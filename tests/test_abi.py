@@ -89,3 +89,24 @@ def test_compute_entry_rejects_missing_device(lib):
                         ctypes.c_float(5.0), 0, None, None, None, None, None, ctypes.c_size_t(0), None)
     assert rc == 8
     assert b"sm_100" in lib.euc_last_error()
+
+
+def test_kmeanspp_entry_checks_shapes_before_the_device(lib):
+    """euc_kmeanspp rejects k outside [1, n] with EUC_ERR_SHAPE, and otherwise needs an
+    sm_100 device; the workspace is one fp64 weight per row plus block sums."""
+    import torch
+    lib.euc_kmeanspp.restype = ctypes.c_int
+    lib.euc_kmeanspp.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                 ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                 ctypes.c_void_p]
+    lib.euc_kmeanspp_workspace_bytes.restype = ctypes.c_size_t
+    lib.euc_kmeanspp_workspace_bytes.argtypes = [ctypes.c_int64] * 3
+    al = lambda b: (b + 255) // 256 * 256
+    n = 5000
+    assert lib.euc_kmeanspp_workspace_bytes(n, 8, 10) == al(n * 8) + al(((n + 1023) // 1024) * 8) + 256
+    for k in (0, n + 1):
+        assert lib.euc_kmeanspp(None, 0, n, 8, k, 1, None, None, None, 0, None) == 1  # EUC_ERR_SHAPE
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    assert lib.euc_kmeanspp(ctypes.c_void_p(16), 0, n, 8, 10, 1, ctypes.c_void_p(16), None, ctypes.c_void_p(16),
+                            1 << 20, None) == 8  # EUC_ERR_DEVICE
