@@ -138,11 +138,17 @@ def run_advanced(name, P, C, kappa, in_dtype, out_dtype):
 _LAST_COUNT = [None]
 
 
+ARGMIN_CERTIFIED = 2  # EUC_ARGMIN_CERTIFIED
+
+
 def run_argmin(op_name, P, C, kappa=5.0, exact=False, labels_dtype=torch.int64, min_dist=True):
     """Fused distance + argmin for distance operator `op_name` (a key of _lib.OPS):
     returns (labels, min_dist, flagged-pair count as a 0-d device tensor).  `exact`
-    selects the epilogue that forms every distance exactly as the D-producing
-    operator does (see euc_argmin in include/euclid_b200.h)."""
+    True selects the epilogue that forms every distance exactly as the D-producing
+    operator does; "certified" labels every row with the first index of its smallest
+    direct distance in the operator's recompute arithmetic, recomputing only the
+    centers that can win, and the count is then the number of direct distances taken
+    (see euc_argmin in include/euclid_b200.h)."""
     want = torch.float64 if op_name == "double" else torch.float32
     check_pair(P, C, want)
     n, d = P.shape
@@ -155,7 +161,8 @@ def run_argmin(op_name, P, C, kappa=5.0, exact=False, labels_dtype=torch.int64, 
     st = stream_of(P)
     l64 = labels if labels_dtype == torch.int64 else None
     l32 = labels if labels_dtype == torch.int32 else None
-    check(lib().euc_argmin(OPS[op_name], ptr(P), ptr(C), n, m, d, ctypes.c_float(kappa), int(bool(exact)),
+    mode = ARGMIN_CERTIFIED if isinstance(exact, str) and exact == "certified" else int(bool(exact))
+    check(lib().euc_argmin(OPS[op_name], ptr(P), ptr(C), n, m, d, ctypes.c_float(kappa), mode,
                            ptr(l64), ptr(l32),
                            ptr(md), ptr(cnt), ptr(ws), ws.numel(), st))
     return labels, md, cnt[0]

@@ -22,7 +22,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fvisibility=hidden"]
 SOURCES = ["api.cu", "k_prep.cu", "k_tc.cu", "k_tc_fast.cu", "k_simt.cu", "k_recompute.cu", "k_centers.cu", "k_seed.cu",
-           "noalloc.cu"]
+           "k_cert.cu", "noalloc.cu"]
 
 
 def _deps():

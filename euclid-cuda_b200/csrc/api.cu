@@ -206,7 +206,7 @@ static float k_float(const OpSpec* s, float kappa, int64_t dim) {
 }
 
 struct RunOut {
-  bool exact = false;                // argmin mode: exact epilogue instead of the fast screen
+  int mode = 0;                      // argmin mode: 0 screen, 1 exact epilogue, 2 certified
   void* D = nullptr;                 // D mode
   int64_t* labels = nullptr;         // argmin mode
   int32_t* labels32 = nullptr;
@@ -234,6 +234,10 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     cudaError_t e = launch_direct(s, P, C, n, m, static_cast<int>(dim), o.D, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, s->name);
   }
+  const bool cert = argmin && o.mode == 2;
+  if (cert && !(is_tc(s) && s->flag != FL_NONE && s->in == IN_F32 && (s->rec == RC_F32 || s->rec == RC_F64)))
+    return fail(EUC_ERR_UNSUPPORTED,
+                std::string(s->name) + ": no certified argmin (tensor-core operators with an fp32 or fp64 recompute)");
   const Layout L = layout_for(s, n, m, dim, argmin);
   if (!ws || ws_bytes < L.total)
     return fail(EUC_ERR_WORKSPACE, std::string(s->name) + ": workspace of " + std::to_string(L.total) +
@@ -262,7 +266,8 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.Clow = is_tc(s) ? w + L.clow : nullptr;
   j.ldlow = L.ldlow;
   // the screen bounds flagged pairs through 1 - K > 0
-  j.fast_argmin = argmin && is_tc(s) && s->flag != FL_NONE && !o.exact && j.kf < 1.f;
+  j.fast_argmin = argmin && is_tc(s) && s->flag != FL_NONE && ((o.mode == 0 && j.kf < 1.f) || cert);
+  j.cert = cert;
   j.Clow_sorted = L.clow_s ? w + L.clow_s : nullptr;
   j.cc_sorted = L.cc_s ? reinterpret_cast<float*>(w + L.cc_s) : nullptr;
   j.perm = L.perm ? reinterpret_cast<int*>(w + L.perm) : nullptr;
@@ -275,6 +280,27 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.regions = j.fast_argmin ? tc_fast_regions(n) : 0;
   j.b_aux_sorted = L.baux ? w + L.baux : nullptr;
   j.aux_e = reinterpret_cast<int*>(w + L.hdr + 16);
+  j.ccmax = reinterpret_cast<float*>(w + L.hdr + 20);
+  const int64_t n_rt = (n + 127) / 128;
+  if (cert) {
+    // the accumulator region of the candidate chunks (ccap >= n entries of 128 bytes) is
+    // unused: [4][n] keys, [4][n] second distances, per row the second screen's threshold
+    // and the list of rows evaluated whole, per 128-row tile its switch (56 n + n / 128
+    // bytes); the second screen lists its groups in the entry region
+    uint8_t* c = w + L.cs;
+    j.cert_key = reinterpret_cast<unsigned long long*>(c);
+    j.cert_d2 = reinterpret_cast<float*>(c + static_cast<size_t>(n) * 32);
+    j.cert_thr = reinterpret_cast<float*>(c + static_cast<size_t>(n) * 48);
+    j.cert_rows = reinterpret_cast<uint32_t*>(c + static_cast<size_t>(n) * 52);
+    j.cert_tiles = c + static_cast<size_t>(n) * 56;
+    j.cert_nrows = reinterpret_cast<unsigned int*>(w + L.hdr + 24);
+    // the flagged-pair list is unused too: the second screen lists its groups in the
+    // larger of the two entry regions
+    if (L.cap > L.ccap) {
+      j.chunk_list = reinterpret_cast<unsigned long long*>(w + L.list);
+      j.chunk_cap = L.cap;
+    }
+  }
   j.region_cnt = L.rcnt ? reinterpret_cast<uint32_t*>(w + L.rcnt) : nullptr;
   j.redo = L.redo ? w + L.redo : nullptr;
   j.stream = st;
@@ -287,13 +313,24 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     const int64_t nt = ((n + o.tile_T - 1) / o.tile_T) * j.tiles_j;
     e = cudaMemsetAsync(o.tile_counts, 0, static_cast<size_t>(nt) * 4, st);
   }
+  if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_nrows, 0, 4, st);
+  if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_tiles, 0, static_cast<size_t>(n_rt), st);
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
   if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
   if (e != cudaSuccess) return cuda_fail(e, "prep");
-  e = j.fast_argmin ? launch_tc_fast(j) : (is_tc(s) ? launch_tc(j) : launch_simt(j));
+  e = j.fast_argmin ? launch_tc_fast(j, cert ? 1 : 0) : (is_tc(s) ? launch_tc(j) : launch_simt(j));
   if (e != cudaSuccess) return cuda_fail(e, s->name);
+  if (cert) {
+    // rows the first screen decides; a second screen lists the candidate groups of the
+    // others; their direct distances, and the rows evaluated whole
+    float* md = static_cast<float*>(o.min_dist);
+    e = launch_cert_rows(j, o.labels, o.labels32, md);
+    if (e == cudaSuccess) e = launch_tc_fast(j, 2);
+    if (e == cudaSuccess) e = launch_cert_finish(j, o.labels, o.labels32, md);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "certified rows");
+  }
   if (j.fast_argmin) e = launch_eval_chunks(j);
   if (e == cudaSuccess) e = launch_recompute(j);
   if (e == cudaSuccess && j.fast_argmin)
@@ -626,7 +663,7 @@ int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64
   if (!allowed) return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) + ": no fused argmin form");
   if (m > 0xffffffffll) return fail(EUC_ERR_SHAPE, "too many centers");
   RunOut o;
-  o.exact = exact != 0;
+  o.mode = exact == EUC_ARGMIN_CERTIFIED ? 2 : (exact != 0 ? 1 : 0);
   o.labels = labels;
   o.labels32 = labels32;
   o.min_dist = min_dist;

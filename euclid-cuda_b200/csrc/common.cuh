@@ -225,6 +225,13 @@ __device__ __forceinline__ float fmin3(float a, float b, float c) {
   return r;
 }
 
+// max that returns NaN when either operand is NaN (PTX max.NaN)
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 // ------------------------------------------------------ reference rounding
 // Value of x after a round-to-nearest-even store to fp16 / bf16, as fp32.
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }

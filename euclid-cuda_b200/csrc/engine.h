@@ -28,7 +28,9 @@ enum Norm {
   NM_LOW_BF16 = 1,  // same for bf16 (mix.cu:122-135)
   NM_F32_FMA = 2,   // fp32 fmaf over fp32 values (euclidean_kernels.cu:16-26)
   NM_F32_SUMSQ = 3, // sum of fp32-rounded squares: (P*P).sum(1) (tiled.cu:338)
-  NM_F64_FMA = 4    // fp64 fma over fp64 values (euclidean_kernels.cu:28-38)
+  NM_F64_FMA = 4,   // fp64 fma over fp64 values (euclidean_kernels.cu:28-38)
+  NM_OPERAND = 5    // fp32 fmaf over the values rounded to the MMA operand type, kept in fp32
+                    // (the certified screen's norms: |p~|^2 to fp32 accuracy)
 };
 enum Form {
   FM_F32 = 0,        // d = max((pp - 2s) + cc, 0) in fp32
@@ -116,6 +118,18 @@ struct DistJob {
   // fast argmin: the screening kernel reads the fp32 points itself (rounding, norms and
   // the extra-K rows in shared memory) instead of a prepared low-precision copy
   bool fused_rows;
+  // certified argmin: the screen keeps, per row and column group of 8 sorted centers, the
+  // best and second-best screened distance; every (parity, column half) group of the
+  // epilogue writes its partial result ([4][n] keys and second distances); ccmax is the
+  // largest finite center norm (device scalar, written by the center sort)
+  bool cert;
+  unsigned long long* cert_key;
+  float* cert_d2;
+  float* ccmax;
+  float* cert_thr;               // per row: threshold of the second screen (-inf: decided)
+  uint8_t* cert_tiles;           // per row tile: whether the second screen visits it
+  uint32_t* cert_rows;           // rows evaluated whole
+  unsigned int* cert_nrows;
   cudaStream_t stream;
 };
 
@@ -125,7 +139,9 @@ cudaError_t launch_sort_centers(const DistJob& j);
 cudaError_t launch_tc(const DistJob& j);
 // fast argmin: screening kernel, exact evaluation of the candidate chunks (flagged pairs
 // go to the recompute list), and rows whose candidates did not fit
-cudaError_t launch_tc_fast(const DistJob& j);
+// cert_pass: 0 the screen of the fast argmin, 1 the certified screen, 2 its second
+// screen over the rows the first did not decide
+cudaError_t launch_tc_fast(const DistJob& j, int cert_pass = 0);
 cudaError_t launch_eval_chunks(const DistJob& j);
 // ... and writes every row's outputs from its key (labels, labels32, mind nullable)
 cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
@@ -136,6 +152,11 @@ bool tc_make_tmap_sw32(CUtensorMap* map, const void* base, int64_t rows, int esi
                        bool is_bf16);
 // whether the screening kernel can prepare the points itself for this job
 bool tc_fast_can_fuse_rows(const DistJob& j);
+// certified argmin (k_cert.cu): every row's outputs from the screen's partial results,
+// with the direct distances of its candidates (labels, labels32, mind nullable)
+cudaError_t launch_cert_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
+// ... and, after the second screen, its listed groups and the rows evaluated whole
+cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
 cudaError_t launch_simt(const DistJob& j);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);

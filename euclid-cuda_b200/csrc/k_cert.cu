@@ -1,0 +1,371 @@
+// Certified argmin: second pass after the screening kernel's CERT form (sm_100a).
+//
+// The label of row i is the first index of the smallest direct distance
+// D_ij = direct(p_i, c_j) over all centers, in the operator's recompute arithmetic
+// (fp32 or fp64 sequential sum of squared differences, direct.cuh) -- what the
+// operator stores for a pair it flags, so the labels equal the reference's whenever
+// every pair of the row is flagged.  Only the candidates that can win are recomputed.
+//
+// The screening kernel leaves, for each of its four epilogue groups (tile parity,
+// column half), the group's best screened distance d with the sorted start of its
+// center's group of 8 sorted centers, and the second-best screened distance outside
+// that group.  Merged: d1 (the row's best), its group G, and m2 (smallest screened
+// distance of any center outside G).  The screened distance of pair j is
+// d^_j = 2 y_j - Br + pp with y_j the MMA accumulator (aux.cuh).  It differs from
+// |p~ - c~_j|^2 (p~, c~ the operands rounded to the MMA type) by a row-common part rho
+// (pp against |p~|^2, the split of Br) and a pair part e_j (cc_j against |c~_j|^2, the
+// fp32 accumulation of the MMA, the key truncation, the fp32 adds of the formula); and
+// |p~ - c~_j| differs from a_j = |p - c_j| by at most Delta = u (|p| + |c_j|) + 2 eta
+// sqrt(dim) (unit roundoff u of the MMA type, eta its absolute rounding floor).  The
+// direct sum is within gd = (dim + 4) 2^-24 of a_j^2.  Hence
+//   D_j <= UB = (sqrt(d1 + rho + e) + Delta)^2 (1 + gd)          for the winner,
+//   D_j >= LB = max(sqrt(max(m2 - rho - e, 0)) - Delta, 0)^2 (1 - gd)  outside G,
+// with rho, e and Delta bounded from pp and the largest center norm.  If LB > UB no
+// center outside G reaches the winner's distance: the 8 direct distances of G decide
+// the row.  Otherwise a center j can only win if its screened distance is at most
+//   T = (sqrt(UB / (1 - gd)) + Delta)^2 + rho + e,
+// and a second screen over the row tiles holding such rows lists every group of 8 with
+// a screened distance <= T; the direct distances of the listed groups decide the row.
+// Rows the screen does not bound (norms not finite or out of the extra K block's range)
+// and rows whose listed groups overflow the list take every center's direct distance.
+//
+// d_count receives the number of direct distances evaluated.
+#include "common.cuh"
+#include "engine.h"
+#include "direct.cuh"
+#include "aux.cuh"
+
+#include <cmath>
+
+namespace euc {
+
+struct CertArgs {
+  const float* P;
+  const float* C;
+  int64_t n, m;
+  int dim;
+  const int* perm;               // sorted position -> center index
+  const float* pp;               // the screen's point norms
+  const float* ccmax;            // largest finite center norm (device scalar)
+  const uint8_t* redo;           // rows the screen does not bound
+  const unsigned long long* key; // [4][n] (best screened distance, sorted start of its group)
+  const float* d2;               // [4][n] second-best screened distance outside that group
+  float* thr;                    // per row: T of the second screen, -inf for a decided row
+  uint8_t* tiles;                // per row tile: holds a row for the second screen
+  unsigned long long* row_key;   // rows of the second screen: smallest (distance, index)
+  const unsigned long long* glist;  // second screen: (row << 32 | sorted group start) entries
+  unsigned long long region_cap;    //   in regions of region_cap entries,
+  const uint32_t* region_cnt;       //   region_cnt[r] of them used
+  int regions;
+  uint32_t* rows;                // rows evaluated whole
+  unsigned int* nrows;
+  unsigned long long* count;
+  int64_t* labels;
+  int32_t* labels32;
+  float* mind;
+  // bound constants
+  double u;      // unit roundoff of the MMA operand type
+  double un;     // relative error of a norm against |p~|^2
+  double eta_n;  // absolute error of a norm (subnormal range of its type)
+  double gmma;   // relative error of the MMA's fp32 accumulation, against the sum of |terms|
+  double gd;     // relative error of the direct sum
+  double eta;    // absolute rounding floor of one operand element
+  double sqd;    // sqrt(dim)
+};
+
+__device__ __forceinline__ float key_dist(unsigned long long k) {
+  return __uint_as_float(static_cast<uint32_t>(k >> 32));
+}
+
+__device__ __forceinline__ void cert_write(const CertArgs& a, int64_t i, unsigned long long k) {
+  const uint32_t j = static_cast<uint32_t>(k & 0xffffffffull);
+  if (a.labels) a.labels[i] = j;
+  if (a.labels32) a.labels32[i] = static_cast<int32_t>(j);
+  if (a.mind) a.mind[i] = key_dist(k);
+}
+
+// 1 when every center outside the winning group has a direct distance above the
+// winner's (LB > UB above); else 2 with the second screen's threshold T in *thr, or 0
+// when the screen gives no bound.  fp64 throughout; the bounds are monotone in the
+// norms, so the largest center norm stands in for each center's.
+__device__ int cert_bounds(const CertArgs& a, float ppf, float d1f, float m2f, float* thr) {
+  const float kInf = __int_as_float(0x7f800000);
+  if (!(d1f < kInf)) return 0;
+  if (!(m2f < kInf)) return 1;  // no other center
+  const double pp = ppf, ccm = *a.ccmax, d1 = d1f, m2 = m2f;
+  const double br = static_cast<double>(__fmul_rn(ppf, kAuxRowScale));
+  // |p|, |c| (fp32 vectors) and |p~|, |c~| (rounded), upper bounds
+  const double np = (sqrt((pp + a.eta_n) / (1.0 - a.un)) + a.eta * a.sqd) / (1.0 - a.u);
+  const double nc = (sqrt((ccm + a.eta_n) / (1.0 - a.un)) + a.eta * a.sqd) / (1.0 - a.u);
+  const double npt = (1.0 + a.u) * np + a.eta * a.sqd;
+  const double nct = (1.0 + a.u) * nc + a.eta * a.sqd;
+  const double delta = a.u * (np + nc) + 2.0 * a.eta * a.sqd;
+  const double sterm = npt * nct + 0.505 * (ccm + br);  // sum of |terms| of one MMA accumulator
+  const double rho = a.un * npt * npt + a.eta_n + 0x1p-24 * br;
+  const double e = a.un * nct * nct + a.eta_n + 0x1p-24 * ccm + (2.0 * a.gmma + 0x1.1p-17) * sterm +
+                   0x1p-23 * (2.0 * sterm + br + pp);
+  const double slack = rho + e;
+  const double ua = sqrt(d1 + slack) + delta;
+  const double ub = ua * ua * (1.0 + a.gd);
+  const double la = fmax(sqrt(fmax(m2 - slack, 0.0)) - delta, 0.0);
+  const double lb = la * la * (1.0 - a.gd);
+  if (lb > ub * (1.0 + 0x1p-30)) return 1;
+  const double ta = sqrt(ub / (1.0 - a.gd)) + delta;
+  const float t = __double2float_ru((ta * ta + slack) * (1.0 + 0x1p-30));
+  if (!(t < kInf)) return 0;
+  *thr = t;
+  return 2;
+}
+
+// Four rows per warp, 8 lanes per row.  Rows the winning group decides take its 8 direct
+// distances here; rows it does not decide get their threshold T and their row tile is
+// switched on for the second screen; rows without bounds are listed for
+// cert_whole_rows_kernel.
+template <int REC>
+__global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int t = lane & 7;
+  const float kInf = __int_as_float(0x7f800000);
+  const int64_t nq = (a.n + 3) / 4;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  unsigned long long evals = 0;
+  for (int64_t qd = gw; qd < nq; qd += nw) {
+    const int64_t i = qd * 4 + (lane >> 3);
+    const bool valid = i < a.n;
+    bool whole = valid;
+    float thr = -kInf;
+    unsigned long long k1 = ~0ull;
+    if (valid && a.redo[i] == 0) {
+      // merge the four partial results: the best key, and m2 = the other groups' best
+      // distances and the winner's second-best
+      float m2 = kInf, d2w = kInf;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const unsigned long long k = __ldg(a.key + g * a.n + i);
+        const float d2 = __ldg(a.d2 + g * a.n + i);
+        if (k < k1) {
+          if (k1 != ~0ull) m2 = fminf(m2, key_dist(k1));
+          k1 = k;
+          d2w = d2;
+        } else {
+          m2 = fminf(m2, key_dist(k));
+        }
+      }
+      m2 = fminf(m2, d2w);
+      const int r = cert_bounds(a, __ldg(a.pp + i), key_dist(k1), m2, &thr);
+      whole = r == 0;
+      if (r == 2 && t == 0) {  // to the second screen
+        a.row_key[i] = ~0ull;
+        a.tiles[i / 128] = 1;
+      }
+      if (r != 2) thr = -kInf;
+    }
+    if (valid && t == 0) a.thr[i] = thr;
+    const bool grp = valid && !whole && !(thr > -kInf);
+    unsigned long long best = ~0ull;
+    if (grp) {
+      const int64_t s = static_cast<int64_t>(k1 & 0xffffffffull) + t;  // sorted position
+      if (s < a.m) {
+        const int j = __ldg(a.perm + s);
+        const double v = direct_dist<float, REC>(a.P + i * a.dim, a.C + static_cast<int64_t>(j) * a.dim, a.dim);
+        best = make_key(static_cast<float>(v), static_cast<uint32_t>(j));
+        ++evals;
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other < best ? other : best;
+    }
+    if (grp && t == 0) cert_write(a, i, best);
+    // rows evaluated whole: one list entry each, one reservation per warp
+    const bool push = whole && t == 0;
+    const unsigned int bal = __ballot_sync(0xffffffffu, push);
+    if (bal) {
+      unsigned int base = 0;
+      if (lane == 0) base = atomicAdd(a.nrows, static_cast<unsigned int>(__popc(bal)));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (push) a.rows[base + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint32_t>(i);
+    }
+  }
+  evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned int>(evals));
+  if (lane == 0 && evals) atomicAdd(a.count, evals);
+}
+
+// Listed rows: one warp per row, lanes over the centers, first index of the minimum.
+template <int REC>
+__global__ void __launch_bounds__(256) cert_whole_rows_kernel(const CertArgs a) {
+  const int lane = threadIdx.x & 31;
+  const unsigned int nr = *a.nrows;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  unsigned long long evals = 0;
+  for (int64_t r = gw; r < nr; r += nw) {
+    const int64_t i = a.rows[r];
+    const float* p = a.P + i * a.dim;
+    unsigned long long best = ~0ull;
+    for (int64_t j = lane; j < a.m; j += 32) {
+      const double v = direct_dist<float, REC>(p, a.C + j * a.dim, a.dim);
+      const unsigned long long k = make_key(static_cast<float>(v), static_cast<uint32_t>(j));
+      best = k < best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other < best ? other : best;
+    }
+    if (lane == 0) {
+      cert_write(a, i, best);
+      evals += static_cast<unsigned long long>(a.m);
+    }
+  }
+  if (lane == 0 && evals) atomicAdd(a.count, evals);
+}
+
+// The second screen's listed groups: 8 direct distances each (four entries per warp),
+// folded into the row's key with one 64-bit atomicMin.
+template <int REC>
+__global__ void __launch_bounds__(256) cert_groups_kernel(const CertArgs a) {
+  constexpr int kBlocksPerRegion = 8;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int t = lane & 7;
+  const int r = blockIdx.x / kBlocksPerRegion;
+  const uint32_t wr = (blockIdx.x % kBlocksPerRegion) * 8 + wib;
+  constexpr uint32_t kStride = kBlocksPerRegion * 8 * 4;
+  unsigned long long cnt64 = a.region_cnt[r];
+  if (cnt64 > a.region_cap) cnt64 = a.region_cap;
+  const uint32_t cnt = static_cast<uint32_t>(cnt64);
+  const unsigned long long* gl = a.glist + static_cast<unsigned long long>(r) * a.region_cap;
+  unsigned long long evals = 0;
+  for (uint32_t t0 = wr * 4; t0 < cnt; t0 += kStride) {
+    const uint32_t q = t0 + (lane >> 3);
+    unsigned long long best = ~0ull;
+    int64_t i = -1;
+    if (q < cnt) {
+      const unsigned long long e = gl[q];
+      i = static_cast<int64_t>(e >> 32);
+      const int64_t s = static_cast<int64_t>(e & 0xffffffffull) + t;
+      // a row whose entries overflowed (redo 2) is evaluated whole instead
+      if (i < a.n && s < a.m && a.redo[i] == 0) {
+        const int j = __ldg(a.perm + s);
+        const double v = direct_dist<float, REC>(a.P + i * a.dim, a.C + static_cast<int64_t>(j) * a.dim, a.dim);
+        best = make_key(static_cast<float>(v), static_cast<uint32_t>(j));
+        ++evals;
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other < best ? other : best;
+    }
+    if (t == 0 && i >= 0 && i < a.n && best != ~0ull) atomicMin(a.row_key + i, best);
+  }
+  evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned int>(evals));
+  if (lane == 0 && evals) atomicAdd(a.count, evals);
+}
+
+// Rows of the second screen: outputs from the key, or (list overflow, redo 2) to the
+// rows evaluated whole.
+__global__ void __launch_bounds__(256) cert_second_rows_kernel(const CertArgs a) {
+  const float kInf = __int_as_float(0x7f800000);
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < a.n;
+       base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    bool push = false;
+    if (i < a.n && a.thr[i] > -kInf) {
+      const unsigned long long k = a.row_key[i];
+      push = a.redo[i] != 0 || k == ~0ull;
+      if (!push) cert_write(a, i, k);
+    }
+    const unsigned int bal = __ballot_sync(0xffffffffu, push);
+    if (bal) {
+      unsigned int b = 0;
+      if (lane == 0) b = atomicAdd(a.nrows, static_cast<unsigned int>(__popc(bal)));
+      b = __shfl_sync(0xffffffffu, b, 0);
+      if (push) a.rows[b + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint32_t>(i);
+    }
+  }
+}
+
+static CertArgs cert_args(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
+  const OpSpec* s = j.spec;
+  CertArgs a{};
+  a.P = static_cast<const float*>(j.P);
+  a.C = static_cast<const float*>(j.C);
+  a.n = j.n;
+  a.m = j.m;
+  a.dim = j.dim;
+  a.perm = j.perm;
+  a.pp = static_cast<const float*>(j.pp);
+  a.ccmax = j.ccmax;
+  a.redo = j.redo;
+  a.key = j.cert_key;
+  a.d2 = j.cert_d2;
+  a.thr = j.cert_thr;
+  a.tiles = j.cert_tiles;
+  a.row_key = j.row_key;
+  a.glist = j.chunk_list;
+  a.region_cap = j.regions > 0 ? j.chunk_cap / static_cast<unsigned long long>(j.regions) : 0;
+  a.region_cnt = j.region_cnt;
+  a.regions = j.regions;
+  a.rows = j.cert_rows;
+  a.nrows = j.cert_nrows;
+  a.count = j.count;
+  a.labels = labels;
+  a.labels32 = labels32;
+  a.mind = mind;
+  const bool bf16 = s->gemm == G_TC_BF16;
+  const bool f16 = s->gemm == G_TC_F16;
+  a.u = bf16 ? 0x1p-8 : 0x1p-11;  // fp16, tf32 (cvt.rna): 11 significant bits; bf16: 8
+  // the screen's norms are fp32 sums of squares of the rounded operands (NM_OPERAND): the
+  // products are exact, the sum's relative error is at most (dim + 2) 2^-24, and squares
+  // below fp32's normal range lose at most 2^-149 each
+  a.un = (static_cast<double>(j.dim) + 2.0) * 0x1p-24 * 1.01;
+  a.eta_n = (static_cast<double>(j.dim) + 1.0) * 0x1p-149;
+  a.gmma = (static_cast<double>(j.ldlow) + 32.0) * 0x1p-22;
+  a.gd = (static_cast<double>(j.dim) + 4.0) * 0x1p-24 * 1.01 + 0x1p-24;
+  a.eta = f16 ? 0x1p-25 : 0x1p-133;
+  a.sqd = std::sqrt(static_cast<double>(j.dim));
+  return a;
+}
+
+static bool cert_job_ok(const DistJob& j) {
+  const OpSpec* s = j.spec;
+  return s->in == IN_F32 && (s->rec == RC_F32 || s->rec == RC_F64) && j.cert_key && j.cert_d2 && j.cert_thr &&
+         j.cert_tiles && j.ccmax && j.cert_rows && j.cert_nrows && j.redo && j.perm && j.row_key && j.chunk_list &&
+         j.region_cnt && j.regions > 0;
+}
+
+cudaError_t launch_cert_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
+  if (!cert_job_ok(j)) return cudaErrorInvalidValue;
+  const CertArgs a = cert_args(j, labels, labels32, mind);
+  const int64_t nq = (j.n + 3) / 4;
+  const int blocks = static_cast<int>(std::min<int64_t>((nq + 7) / 8, static_cast<int64_t>(num_sms()) * 8));
+  if (j.spec->rec == RC_F32)
+    cert_rows_kernel<RC_F32><<<blocks, 256, 0, j.stream>>>(a);
+  else
+    cert_rows_kernel<RC_F64><<<blocks, 256, 0, j.stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
+  if (!cert_job_ok(j)) return cudaErrorInvalidValue;
+  const CertArgs a = cert_args(j, labels, labels32, mind);
+  const int gblocks = j.regions * 8;
+  const int sblocks = static_cast<int>(std::min<int64_t>((j.n + 255) / 256, static_cast<int64_t>(num_sms()) * 8));
+  const int wblocks = num_sms() * 8;
+  if (j.spec->rec == RC_F32) {
+    cert_groups_kernel<RC_F32><<<gblocks, 256, 0, j.stream>>>(a);
+    cert_second_rows_kernel<<<sblocks, 256, 0, j.stream>>>(a);
+    cert_whole_rows_kernel<RC_F32><<<wblocks, 256, 0, j.stream>>>(a);
+  } else {
+    cert_groups_kernel<RC_F64><<<gblocks, 256, 0, j.stream>>>(a);
+    cert_second_rows_kernel<<<sblocks, 256, 0, j.stream>>>(a);
+    cert_whole_rows_kernel<RC_F64><<<wblocks, 256, 0, j.stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace euc

@@ -35,6 +35,17 @@ template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __h
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
 
 // LOWT: 0 none, 1 fp16, 2 bf16, 3 tf32 (fp32 storage, rounded to 10 mantissa bits)
+// value of x rounded to the MMA operand type LOWT (1 fp16, 2 bf16, 3 tf32), as fp32
+template <int LOWT> __device__ __forceinline__ float operand_value(float x) {
+  if constexpr (LOWT == 1) return round_f16(x);
+  else if constexpr (LOWT == 2) return round_bf16(x);
+  else {
+    uint32_t b;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b) : "f"(x));
+    return __uint_as_float(b);
+  }
+}
+
 template <typename TIN, int NORM, int LOWT>
 __global__ void __launch_bounds__(128) prep_rows_kernel(const TIN* __restrict__ X, int64_t rows, int dim,
                                                         void* __restrict__ low, int ldl,
@@ -76,6 +87,9 @@ __global__ void __launch_bounds__(128) prep_rows_kernel(const TIN* __restrict__ 
         acc = __fmaf_rn(x, x, acc);
       } else if constexpr (NORM == NM_F32_SUMSQ) {
         acc = __fadd_rn(acc, __fmul_rn(x, x));
+      } else if constexpr (NORM == NM_OPERAND) {
+        const float h = operand_value<LOWT>(x);
+        acc = __fmaf_rn(h, h, acc);
       } else {
         acc = fma(x, x, acc);
       }
@@ -200,6 +214,9 @@ __global__ void __launch_bounds__(128) prep_rows_v4_kernel(const float* __restri
         acc = __fmaf_rn(h, h, acc);
       } else if constexpr (NORM == NM_F32_FMA) {
         acc = __fmaf_rn(x, x, acc);
+      } else if constexpr (NORM == NM_OPERAND) {
+        const float h = operand_value<LOWT>(x);
+        acc = __fmaf_rn(h, h, acc);
       } else {
         acc = __fadd_rn(acc, __fmul_rn(x, x));
       }
@@ -248,8 +265,10 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
   if (make_low) lowt = (s->gemm == G_TC_F16) ? 1 : (s->gemm == G_TC_BF16 ? 2 : 3);
   cudaStream_t st = j.stream;
 
+  // the certified screen takes the fp32 norms of the rounded operands instead
+  const int norm = (j.cert && make_low) ? static_cast<int>(NM_OPERAND) : static_cast<int>(s->norm);
 #define PREP(TIN_, NORM_, LOWT_)                                   \
-  if (s->norm == NORM_ && lowt == LOWT_)                           \
+  if (norm == NORM_ && lowt == LOWT_)                              \
     return go<TIN_, NORM_, LOWT_>(X, rows, j.dim, low, ldl, nrm, st);
 
   switch (s->in) {
@@ -262,6 +281,9 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
       PREP(float, NM_F32_SUMSQ, 2)
       PREP(float, NM_F32_SUMSQ, 0)
       PREP(float, NM_F64_FMA, 0)
+      PREP(float, NM_OPERAND, 1)
+      PREP(float, NM_OPERAND, 2)
+      PREP(float, NM_OPERAND, 3)
       break;
     case IN_F16:
       PREP(__half, NM_LOW_F16, 1)
@@ -283,17 +305,18 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
 // Stable rank sort of the centers by norm (ties kept in index order, NaN as +inf):
 // rank_j = #{i : key_i < key_j or (key_i == key_j and i < j)}.  One warp per center,
 // its lanes counting over the norms staged in shared memory.  Every block also reduces
-// the largest finite norm (all blocks see all norms, so they agree) and derives E of the
-// extra K block (aux.cuh).  Sorted position r receives the norm, the original index, the
-// low-precision row NEGATED (the screening MMA forms y0 - s) and the center's extra-K
-// row [c0, c1, c2, 2^E, 2^E, 2^E] (all zero for a norm that is not finite); the padded
-// positions m .. mpad-1 get +inf in c0, so their keys never win.
+// the largest finite norm (all blocks see all norms, so they agree), derives E of the
+// extra K block (aux.cuh) and block 0 stores both.  Sorted position r receives the
+// norm, the original index, the low-precision row NEGATED (the screening MMA forms
+// y0 - s) and the center's extra-K row [c0, c1, c2, 2^E, 2^E, 2^E] (all zero for a norm
+// that is not finite); the padded positions m .. mpad-1 get +inf in c0, so their keys
+// never win.
 template <int KIND>
 __global__ void __launch_bounds__(256) sort_centers_kernel(const float* __restrict__ cc, int m, int mpad,
                                                            const uint4* __restrict__ low, int row_u4,
                                                            float* __restrict__ cc_s, int* __restrict__ perm,
                                                            uint4* __restrict__ low_s, int* __restrict__ aux_e,
-                                                           uint4* __restrict__ b_aux) {
+                                                           float* __restrict__ ccmax, uint4* __restrict__ b_aux) {
   constexpr int SLAB = 2048;
   __shared__ float tile[SLAB];
   __shared__ unsigned int s_max;
@@ -330,7 +353,10 @@ __global__ void __launch_bounds__(256) sort_centers_kernel(const float* __restri
   if (lane == 0) atomicMax(&s_max, wm);
   __syncthreads();
   const int E = aux_exponent<KIND>(__uint_as_float(s_max));
-  if (blockIdx.x == 0 && threadIdx.x == 0) *aux_e = E;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *aux_e = E;
+    *ccmax = __uint_as_float(s_max);
+  }
   if (j >= m && j < mpad && lane == 0) {
     const uint32_t inf_bits = (KIND == 2) ? 0x7f800000u : (KIND == 1 ? 0x7f80u : 0x7c00u);
     b_aux[2 * static_cast<int64_t>(j)] = make_uint4(inf_bits, 0u, 0u, 0u);
@@ -373,11 +399,14 @@ cudaError_t launch_sort_centers(const DistJob& j) {
   uint4* low_s = static_cast<uint4*>(j.Clow_sorted);
   uint4* ba = static_cast<uint4*>(j.b_aux_sorted);
   if (kind == 0)
-    sort_centers_kernel<0><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
+    sort_centers_kernel<0><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e,
+                                                       j.ccmax, ba);
   else if (kind == 1)
-    sort_centers_kernel<1><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
+    sort_centers_kernel<1><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e,
+                                                       j.ccmax, ba);
   else
-    sort_centers_kernel<2><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e, ba);
+    sort_centers_kernel<2><<<grid, 256, 0, j.stream>>>(cc, m, mpad, low, row_u4, j.cc_sorted, j.perm, low_s, j.aux_e,
+                                                       j.ccmax, ba);
   return cudaGetLastError();
 }
 

@@ -86,6 +86,7 @@ struct TfArgs {
   const float* ccs;   // norms, sorted, padded to whole 256-center tiles
   const int* perm;    // sorted position -> original index, padded
   float omk, margin, ovf;
+  float nlim;         // norms at or above this are not screened (their rows are redone)
   const int* aux_e;             // E of the extra K block (device scalar)
   unsigned long long* row_key;
   unsigned long long* list;     // candidate chunks: region r = list + r * region_cap
@@ -93,7 +94,20 @@ struct TfArgs {
   unsigned long long region_cap;
   uint32_t* region_cnt;
   uint8_t* redo;
+  unsigned long long* cert_key;  // certified: [4][n] (best screened distance, sorted start of its group)
+  float* cert_d2;                // certified: [4][n] second-best screened distance outside that group
+  const float* cert_thr;         // certified, second screen: per row, the largest screened distance of a
+                                 // center that can win (-inf: the row is decided)
+  const uint8_t* tile_on;        // null, or per row tile: whether it is screened
 };
+
+// The CTA's next row tile at or after rt (same stride as the persistent loop), skipping
+// the tiles switched off.  Every role walks the same sequence.
+__device__ __forceinline__ int64_t tf_next_tile(const TfArgs& a, int64_t rt) {
+  if (a.tile_on != nullptr)
+    while (rt < a.n_rt && a.tile_on[rt] == 0) rt += gridDim.x;
+  return rt;
+}
 
 // FUSED row preparation, one staged box: 32 fp32 values of row r of the row tile (TMA
 // with the 128-byte swizzle: 16-byte chunk j of row r at r * 128 + ((j ^ r % 8) * 16))
@@ -137,7 +151,7 @@ __device__ __forceinline__ float convert_box(const uint8_t* box, int r, uint8_t*
   return acc;
 }
 
-template <int KIND, bool FUSED>
+template <int KIND, bool FUSED, int CERT>
 __global__ void __launch_bounds__(TF_THREADS, 1)
     dist_tc_fast_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmBaux, const TfArgs a) {
@@ -226,7 +240,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       uint32_t issued_mask = 0, last_phase = 0, a_issued = 0, a_last = 0, m_issued = 0, m_last = 0;
       bool ok = true;
       const int kelems = (KIND == 2) ? 32 : 64;
-      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+      for (int64_t rt = tf_next_tile(a, blockIdx.x); rt < a.n_rt && ok; rt = tf_next_tile(a, rt + gridDim.x), ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const int row0 = static_cast<int>(rt * TF_BM);
         if (!FUSED && a_res) {
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       constexpr uint32_t idesc = umma_idesc(fmt, 128, TF_BN);
       uint32_t stage = 0, phase = 0, t = 0, rt_i = 0;
       bool ok = true;
-      for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+      for (int64_t rt = tf_next_tile(a, blockIdx.x); rt < a.n_rt && ok; rt = tf_next_tile(a, rt + gridDim.x), ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
         const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux + abuf * TF_AAUX_BYTES));
@@ -361,7 +375,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const float kInf = __int_as_float(0x7f800000);
     uint32_t rt_i = 0, t = 0, uses = 0;
     bool ok = true;
-    for (int64_t rt = blockIdx.x; rt < a.n_rt && ok; rt += gridDim.x, ++rt_i) {
+    for (int64_t rt = tf_next_tile(a, blockIdx.x); rt < a.n_rt && ok; rt = tf_next_tile(a, rt + gridDim.x), ++rt_i) {
       const int64_t i = rt * TF_BM + row_local;
       // the row's norm and Br from the row warps (Br NaN: past n, or redone whole)
       const uint32_t abuf = rt_i & 1u;
@@ -372,9 +386,21 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       if (lane == 0) mbar_arrive(&pempty[abuf]);
       const bool row_ok = i < a.n && br == br;
       const float vlane = 0.5f * __fmaf_rn(br, 1.f + a.margin, pp * (a.margin - a.omk));
+      // certified, second screen: the row's threshold on y (a group is listed when its
+      // smallest key is at or below), from its distance threshold T: y = (T + Br - pp) / 2,
+      // raised by 2^-16 of the magnitudes for the key truncation and the fp32 roundings
+      float yt = -kInf;
+      if constexpr (CERT == 2) {
+        const float T = row_ok ? __ldg(a.cert_thr + i) : -kInf;
+        if (T > -kInf) {
+          const float h = 0.5f * __fadd_rn(__fadd_rn(T, br), -pp);
+          yt = h + (fabsf(h) + fabsf(T) + br + pp) * 0x1p-16f;
+        }
+      }
       // best screened key of the row: y with its column in the low 5 bits, and the first
       // sorted column of its chunk
       float best_y = kInf;
+      float sec_y = kInf;  // certified: second-best group minimum of the row
       uint32_t best_c = 0;
       for (int ct = 0; ct < a.n_ct; ++ct, ++t) {
         if ((t & 1u) != b) continue;  // the other parity's groups take this tile
@@ -394,32 +420,59 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const float ccmax_t = nvt > 0 ? mcc[nvt - 1] : 0.f;
         // rows whose S may overflow its rounded format, or whose norms (or this tile's)
         // are not finite, list every chunk
-        const bool lane_exact = !(pp < 3.0e38f && ccmax_t < 3.0e38f && pp * ccmax_t <= a.ovf);
+        const bool lane_exact = !(pp < a.nlim && ccmax_t < a.nlim && pp * ccmax_t <= a.ovf);
         const float vl = row_ok ? vlane : -kInf;  // rows past n never list a chunk
         const bool force = row_ok && lane_exact;
+        if constexpr (CERT != 0) {
+          if (force) a.redo[i] = 1;  // the certified pass evaluates this row whole
+        }
         const int nch = (nvt + 31) >> 5;
         if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
         tc_fence_after();
 
         uint32_t cmask = 0;  // this lane's candidate chunks of the tile
+        uint32_t gmask = 0;  // certified, second screen: bit 4 ch + u for group u of chunk ch
 #pragma unroll 1
         for (int ch = 0; ch < nch; ++ch) {
           float v[32];
           tmem_ld32(tmem_acc + ch * 32, v);
-          const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vl;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             uint32_t kb;
             asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(kb) : "r"(__float_as_uint(v[e])), "r"(kmask), "r"(static_cast<uint32_t>(e)));
             v[e] = __uint_as_float(kb);
           }
-          float tt[11];
+          float km;
+          bool cand = false;
+          if constexpr (CERT != 0) {
+            // four groups of 8 columns: the chunk's minimum, its second-smallest group
+            // minimum, and the row's best and second-best group minima.  Padded
+            // centers give NaN keys: fminf skips them and max.NaN keeps them out of
+            // the second-best (NaN acts as +inf).
+            float gm[4];
 #pragma unroll
-          for (int u = 0; u < 10; ++u) tt[u] = fmin3(v[3 * u], v[3 * u + 1], v[3 * u + 2]);
-          tt[10] = fminf(v[30], v[31]);
-          const float km = fmin3(fmin3(tt[0], tt[1], tt[2]), fmin3(tt[3], tt[4], tt[5]),
-                                 fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
-          const bool cand = force || km <= thr;
+            for (int u = 0; u < 4; ++u)
+              gm[u] = fmin3(fmin3(v[8 * u], v[8 * u + 1], v[8 * u + 2]), fmin3(v[8 * u + 3], v[8 * u + 4], v[8 * u + 5]),
+                            fminf(v[8 * u + 6], v[8 * u + 7]));
+            const float lo01 = fminf(gm[0], gm[1]), lo23 = fminf(gm[2], gm[3]);
+            km = fminf(lo01, lo23);
+            if constexpr (CERT == 1) {
+              const float s2 = fminf(fmax_nan(lo01, lo23), fminf(fmax_nan(gm[0], gm[1]), fmax_nan(gm[2], gm[3])));
+              sec_y = fmin3(sec_y, s2, fmax_nan(best_y, km));
+            } else {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) gmask |= static_cast<uint32_t>(gm[u] <= yt) << (4 * ch + u);
+            }
+          } else {
+            const float thr = __shfl_sync(0xffffffffu, u_own, ch) + vl;
+            float tt[11];
+#pragma unroll
+            for (int u = 0; u < 10; ++u) tt[u] = fmin3(v[3 * u], v[3 * u + 1], v[3 * u + 2]);
+            tt[10] = fminf(v[30], v[31]);
+            km = fmin3(fmin3(tt[0], tt[1], tt[2]), fmin3(tt[3], tt[4], tt[5]),
+                       fmin3(fmin3(tt[6], tt[7], tt[8]), tt[9], tt[10]));
+            cand = force || km <= thr;
+          }
           const float kf = cand ? kInf : km;
           if (kf < best_y) {
             best_y = kf;
@@ -428,6 +481,34 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           cmask |= static_cast<uint32_t>(cand) << ch;
         }
 
+        if constexpr (CERT == 2) {
+          // the tile's listed groups: (row << 32 | sorted start of the group) entries in
+          // this CTA's list region, one shared-memory reservation per warp and tile; a row
+          // whose entries do not fit is evaluated whole (redo 2)
+          if (__any_sync(0xffffffffu, gmask != 0)) {
+            const uint32_t cnt = static_cast<uint32_t>(__popc(gmask));
+            uint32_t incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += v;
+            }
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+            unsigned long long base = 0;
+            if (lane == 31) base = atomicAdd(lcount, static_cast<unsigned long long>(total));
+            base = __shfl_sync(0xffffffffu, base, 31) + (incl - cnt);
+            bool lost = false;
+            for (uint32_t gmk = gmask; gmk; gmk &= gmk - 1u, ++base) {
+              const uint32_t bit = static_cast<uint32_t>(__ffs(gmk) - 1);
+              if (base < a.region_cap)
+                region[base] = (static_cast<unsigned long long>(i) << 32) |
+                               static_cast<unsigned long long>(jt + (bit >> 2) * 32 + (bit & 3u) * 8);
+              else
+                lost = true;
+            }
+            if (lost) a.redo[i] = 2;
+          }
+        }
         // candidate chunks of this tile (some pair may be flagged): each goes, with its
         // accumulators y (read again from TMEM), to this CTA's list region for the exact
         // second pass; one shared-memory reservation per warp and tile
@@ -474,6 +555,25 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
       }
       if (!ok) break;
+      if constexpr (CERT == 2) continue;
+      if constexpr (CERT == 1) {
+        // this group's partial result: its best screened distance with the sorted start
+        // of that center's group of 8, and its second-best screened distance
+        if (row_ok) {
+          float bestv = kInf, d2 = kInf;
+          uint32_t gs = 0xffffffffu;
+          if (best_y < kInf) {
+            const uint32_t kb = __float_as_uint(best_y);
+            bestv = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(kb & ~31u), -br), pp), 0.f);
+            gs = best_c + (kb & 24u);
+          }
+          if (sec_y < kInf)
+            d2 = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(__float_as_uint(sec_y) & ~31u), -br), pp), 0.f);
+          a.cert_key[static_cast<int64_t>(g) * a.n + i] = make_key(bestv, gs);
+          a.cert_d2[static_cast<int64_t>(g) * a.n + i] = d2;
+        }
+        continue;
+      }
       // this group's screened minimum of the row: distance d = 2 y - Br + pp and original
       // center index
       float bestv = kInf;
@@ -525,16 +625,17 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const float kNaN = __int_as_float(0x7fc00000);
     bool x_pending = false;  // FUSED: a staged load this thread issued is in flight
     if constexpr (FUSED) {
-      if (c == 0 && static_cast<int64_t>(blockIdx.x) < a.n_rt) {
+      const int64_t rt0 = tf_next_tile(a, blockIdx.x);
+      if (c == 0 && rt0 < a.n_rt) {
         mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(nbox * TF_XBOX_BYTES));
         for (int bx = 0; bx < nbox; ++bx)
-          tma_load_2d(xst + bx * TF_XBOX_BYTES, &tmA, xfull, bx * 32, static_cast<int>(blockIdx.x) * TF_BM);
+          tma_load_2d(xst + bx * TF_XBOX_BYTES, &tmA, xfull, bx * 32, static_cast<int>(rt0 * TF_BM));
         x_pending = true;
       }
     }
     uint32_t rt_i = 0;
     bool ok = true;
-    for (int64_t rt = blockIdx.x; rt < a.n_rt; rt += gridDim.x, ++rt_i) {
+    for (int64_t rt = tf_next_tile(a, blockIdx.x); rt < a.n_rt; rt = tf_next_tile(a, rt + gridDim.x), ++rt_i) {
       const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
       // the MMAs of the buffer's previous row tile are done, and the epilogue has read
       // its pp and Br
@@ -566,7 +667,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
         mbar_arrive(xempty);
         // the CTA's next row tile into the staging buffer, once every row thread is done
-        const int64_t nrt = rt + gridDim.x;
+        const int64_t nrt = tf_next_tile(a, rt + gridDim.x);
         if (c == 0 && nrt < a.n_rt) {
           if (!mbar_wait(xempty, rt_i & 1u, abort_flag)) {
             ok = false;
@@ -589,7 +690,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         float pp;
         if constexpr (FUSED) {
           const float ah = h ? acc1 : acc0;
-          pp = KIND == 0 ? round_f16(ah) : round_bf16(ah);
+          // the operator's norm, rounded to the operand type; the certified screen keeps
+          // the fp32 norm of the rounded values
+          pp = CERT != 0 ? ah : (KIND == 0 ? round_f16(ah) : round_bf16(ah));
           if (valid) a.pp[i] = pp;
         } else {
           pp = valid ? __ldg(a.pp + i) : 0.f;
@@ -674,10 +777,10 @@ int tc_fast_regions(int64_t n) {
   return grid < 1 ? 1 : grid;
 }
 
-template <int KIND, bool FUSED>
+template <int KIND, bool FUSED, int CERT>
 static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tba,
                                const TfArgs& args, int grid, cudaStream_t st) {
-  auto kern = dist_tc_fast_kernel<KIND, FUSED>;
+  auto kern = dist_tc_fast_kernel<KIND, FUSED, CERT>;
   const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res, FUSED ? tf_xstage_bytes(args.dim) : 0);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -708,7 +811,7 @@ bool tc_fast_can_fuse_rows(const DistJob& j) {
   return a_res != 0 && nst >= 2;
 }
 
-cudaError_t launch_tc_fast(const DistJob& j) {
+cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   const OpSpec* s = j.spec;
   const int kind = low_kind(s);
   const int esize = (kind == 2) ? 4 : 2;
@@ -730,7 +833,10 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.omk = 1.f - j.kf;
   // screen margin: the rounding of S to the GEMM's output format dominates
   a.margin = s->sround == SR_F16 ? 0x1p-10f : (s->sround == SR_BF16 ? 0x1p-7f : 0x1p-16f);
-  a.ovf = s->sround == SR_F16 ? 3.9e9f : 1.0e36f;  // (65504 / 1.05)^2: no fp16 overflow of s
+  // (65504 / 1.05)^2: no fp16 overflow of s (the certified pass never rounds s)
+  a.ovf = (s->sround == SR_F16 && !j.cert) ? 3.9e9f : 1.0e36f;
+  // certified: below 4e9 no element of an fp32 row exceeds fp16's range
+  a.nlim = (j.cert && kind == 0) ? 4.0e9f : 3.0e38f;
   a.aux_e = j.aux_e;
   a.row_key = j.row_key;
   a.list = j.chunk_list;
@@ -738,6 +844,8 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   a.region_cap = j.chunk_cap / static_cast<unsigned long long>(j.regions);
   a.region_cnt = j.region_cnt;
   a.redo = j.redo;
+  a.cert_key = j.cert_key;
+  a.cert_d2 = j.cert_d2;
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
   // A: the low-precision copy, or with FUSED the fp32 points in 32-value x 128-row boxes
@@ -752,13 +860,26 @@ cudaError_t launch_tc_fast(const DistJob& j) {
   CUtensorMap tba;
   const int64_t mpad = (j.m + TF_BN - 1) / TF_BN * TF_BN;
   if (!tc_make_tmap_sw32(&tba, j.b_aux_sorted, mpad, esize, TF_BN, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-  if (j.fused_rows) {
-    if (kind == 0) return launch_tf_t<0, true>(ta, tb, tba, a, grid, j.stream);
-    return launch_tf_t<1, true>(ta, tb, tba, a, grid, j.stream);
+#define TF_LAUNCH(CM_)                                                          \
+  if (j.fused_rows) {                                                           \
+    if (kind == 0) return launch_tf_t<0, true, CM_>(ta, tb, tba, a, grid, j.stream); \
+    return launch_tf_t<1, true, CM_>(ta, tb, tba, a, grid, j.stream);           \
+  }                                                                             \
+  if (kind == 0) return launch_tf_t<0, false, CM_>(ta, tb, tba, a, grid, j.stream);  \
+  if (kind == 1) return launch_tf_t<1, false, CM_>(ta, tb, tba, a, grid, j.stream);  \
+  return launch_tf_t<2, false, CM_>(ta, tb, tba, a, grid, j.stream);
+  if (cert_pass == 1) {
+    if (!j.cert_key || !j.cert_d2) return cudaErrorInvalidValue;
+    TF_LAUNCH(1)
   }
-  if (kind == 0) return launch_tf_t<0, false>(ta, tb, tba, a, grid, j.stream);
-  if (kind == 1) return launch_tf_t<1, false>(ta, tb, tba, a, grid, j.stream);
-  return launch_tf_t<2, false>(ta, tb, tba, a, grid, j.stream);
+  if (cert_pass == 2) {
+    if (!j.cert_thr || !j.cert_tiles) return cudaErrorInvalidValue;
+    a.cert_thr = j.cert_thr;
+    a.tile_on = j.cert_tiles;
+    TF_LAUNCH(2)
+  }
+  TF_LAUNCH(0)
+#undef TF_LAUNCH
 }
 
 int tf_error_and_clear() {

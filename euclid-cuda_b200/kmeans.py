@@ -23,18 +23,23 @@ import _ops
 from _lib import check, lib, ptr, stream_of, workspace
 
 EMPTY_POLICY = {"zero": 0, "keep": 1}
+# labels: the screen (exact wherever the top-two gap exceeds its resolution), the exact
+# epilogue, or the certified first index of the smallest direct distance
+ASSIGN_MODE = {"fast": False, "exact": True, "certified": "certified"}
 
 
 class LloydKMeans:
     """One Lloyd iteration per `step`; `op` is the distance operator (e.g. 'bf16_fp32',
-    'fp16_fp32', 'double') whose cancellation test and recompute define the labels."""
+    'fp16_fp32', 'double') whose cancellation test and recompute define the labels;
+    `mode` ('fast', 'exact', 'certified') is the argmin mode of euc_argmin."""
 
-    def __init__(self, n_clusters, op="bf16_fp32", kappa=5.0, empty="zero", group=None):
+    def __init__(self, n_clusters, op="bf16_fp32", kappa=5.0, empty="zero", group=None, mode="fast"):
         self.k = int(n_clusters)
         self.op = op
         self.kappa = float(kappa)
         self.empty = EMPTY_POLICY[empty]
         self.group = group
+        self.mode = ASSIGN_MODE[mode]
         self._ws = None
 
     def _world(self):
@@ -59,8 +64,10 @@ class LloydKMeans:
         return out
 
     def assign(self, X, C):
-        """Labels (int32) of the local rows and the flagged-pair count (0-d tensor)."""
-        labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, labels_dtype=torch.int32, min_dist=False)
+        """Labels (int32) of the local rows and the flagged-pair count (0-d tensor; the
+        number of direct distances taken in the certified mode)."""
+        labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, exact=self.mode, labels_dtype=torch.int32,
+                                         min_dist=False)
         return labels, cnt
 
     def step(self, X, C):

@@ -210,11 +210,26 @@ EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int6
  * No counterpart in the reference: the k-means caller composes these instead of
  * materialising D (the Lloyd hot path: distances -> argmin -> center update). */
 
+/* `exact` value of euc_argmin selecting the certified mode (no counterpart in the
+ * reference). */
+#define EUC_ARGMIN_CERTIFIED 2
+
 /* Fused distance + row argmin for distance operator `op` (an EUC_OP_MIX_*,
  * EUC_OP_TILED_*, EUC_OP_TC_*, EUC_OP_SINGLE or EUC_OP_DOUBLE id), without
  * materialising D.  Flagged pairs take their recomputed value, as in the reference.
- *   exact != 0: every pair's distance is formed exactly as `op` forms D, and the label
- *               is torch.argmin(D, 1) of that D (first index of the minimum).
+ *   exact == EUC_ARGMIN_CERTIFIED (tensor-core operators whose recompute is fp32 or
+ *               fp64): the label is the first index of the smallest direct distance
+ *               direct(p, c_j) over all centers, in the operator's recompute
+ *               arithmetic (the value `op` stores for a pair it flags), and min_dist is
+ *               that distance -- the reference's labels when every pair of the row is
+ *               flagged.  The tensor-core screen bounds every pair; only the
+ *               centers that can win are recomputed (the 8 of the best group of 8
+ *               norm-sorted centers when the bounds separate it from the rest, else all
+ *               of the row's).  d_count receives the number of direct distances
+ *               evaluated.  Other operators return EUC_ERR_UNSUPPORTED.
+ *   exact != 0 (other values): every pair's distance is formed exactly as `op` forms
+ *               D, and the label is torch.argmin(D, 1) of that D (first index of the
+ *               minimum).
  *   exact == 0: tensor-core operators screen each 32-center chunk: the MMA itself
  *               yields y = (|c|^2 + Br)/2 - p.c (Br = 1.0625 |p|^2 of the row), and per
  *               pair one key (y with the column in its low 5 bits) and half a 3-way min

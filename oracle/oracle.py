@@ -337,6 +337,26 @@ def argmin_first(D):
     return np.argmin(D, axis=1).astype(np.int64)
 
 
+def certified_argmin(name, P, C):
+    """The certified argmin of operator `name` (a MIX or TILED key whose recompute is
+    fp32 or fp64): label = first index of the smallest direct distance over all
+    centers in the operator's recompute arithmetic (direct_dist of the reference's
+    fallback kernels, euclidean_kernels_mix.cu:156-177, 481-504), stored as fp32 as
+    the operator stores a recomputed pair; returns (labels, min_dist).  Equal to
+    argmin_first of the operator's D when every pair is flagged."""
+    rec = MIX[name][5] if name in MIX else TILED[name.split("_", 1)[1]][2]
+    if rec not in ("fp32", "fp64"):
+        raise ValueError(f"{name}: the certified argmin needs an fp32 or fp64 recompute")
+    P = _c(P, np.float32)
+    C = _c(C, np.float32)
+    n, m = P.shape[0], C.shape[0]
+    ii = np.repeat(np.arange(n, dtype=np.int64), m)
+    jj = np.tile(np.arange(m, dtype=np.int64), n)
+    D = direct_pairs(rec, P, C, ii, jj).astype(np.float32).reshape(n, m)
+    lab = argmin_first(D)
+    return lab, D[np.arange(n), lab]
+
+
 def top2_gap(D):
     part = np.partition(D, 1, axis=1)[:, :2]
     return part[:, 1] - part[:, 0]

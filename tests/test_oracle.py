@@ -142,3 +142,25 @@ def test_kmeanspp_oracle_draws_distinct_rows():
     assert len(set(idx.tolist())) == 30
     assert idx[0] == (O.seed_draw53(11, 0) * 400) >> 53
     assert 0 <= O.seed_draw53(2 ** 64 - 1, 5) < 2 ** 53
+
+
+@pytest.mark.parametrize("name", ["fp16_fp32", "bf16_fp64", "tf32_fp64"])
+def test_certified_oracle_is_the_fully_flagged_operator(name):
+    # with every pair flagged (kappa large enough that K >= 2), the operator's D is the
+    # direct distance of every pair: its first-index argmin is the certified label
+    rng = np.random.default_rng(4)
+    P = rng.normal(size=(120, 9)).astype(np.float32)
+    C = np.concatenate([rng.normal(size=(30, 9)), P[:3]]).astype(np.float32)
+    D, flag, cnt = O.mix(name, P, C, kappa=1e6)
+    assert flag.all()
+    lab, md = O.certified_argmin(name, P, C)
+    np.testing.assert_array_equal(lab, O.argmin_first(D))
+    np.testing.assert_array_equal(md, D[np.arange(120), lab])
+    assert (lab[:3] == 30 + np.arange(3)).all()  # the points themselves, at distance 0
+    assert (md[:3] == 0).all()
+
+
+def test_certified_oracle_rejects_half_arithmetic_recompute():
+    P = np.ones((2, 3), np.float32)
+    with pytest.raises(ValueError):
+        O.certified_argmin("fp16_fp16", P, P)
