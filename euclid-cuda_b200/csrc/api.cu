@@ -293,6 +293,22 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     j.cert_thr = reinterpret_cast<float*>(c + static_cast<size_t>(n) * 48);
     j.cert_rows = reinterpret_cast<uint32_t*>(c + static_cast<size_t>(n) * 52);
     j.cert_tiles = c + static_cast<size_t>(n) * 56;
+    // by group, where the region has room: 5 n entries and their sorted rows, and three
+    // tables of ng + 1 counters (ng <= 16384: the block histograms fit shared memory)
+    const size_t nb = static_cast<size_t>(n);
+    const size_t cs_bytes = al(L.ccap * 128);
+    const int64_t ng = (m + 7) / 8;
+    const size_t b0 = (nb * 56 + static_cast<size_t>(n_rt) + 15) & ~size_t(15);
+    const size_t need = b0 + nb * 60 + 12 * static_cast<size_t>(ng + 1);
+    j.cert_ng = (ng <= 16384 && 5 * nb <= 0xffffffffull && need <= cs_bytes) ? static_cast<int>(ng) : 0;
+    if (j.cert_ng > 0) {
+      j.cert_ent = reinterpret_cast<unsigned long long*>(c + b0);
+      j.cert_ent_cap = static_cast<unsigned int>(5 * nb);
+      j.cert_srow = reinterpret_cast<uint32_t*>(c + b0 + nb * 40);
+      j.cert_gcnt = reinterpret_cast<unsigned int*>(c + b0 + nb * 60);
+      j.cert_goff = j.cert_gcnt + (ng + 1);
+      j.cert_ent_n = reinterpret_cast<unsigned int*>(w + L.hdr + 28);
+    }
     j.cert_nrows = reinterpret_cast<unsigned int*>(w + L.hdr + 24);
     // the flagged-pair list is unused too: the second screen lists its groups in the
     // larger of the two entry regions
@@ -315,6 +331,10 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   }
   if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_nrows, 0, 4, st);
   if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_tiles, 0, static_cast<size_t>(n_rt), st);
+  if (e == cudaSuccess && cert && j.cert_ng > 0) {
+    e = cudaMemsetAsync(j.cert_ent_n, 0, 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(j.cert_gcnt, 0, static_cast<size_t>(j.cert_ng) * 4, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "memset");
   if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));

@@ -130,6 +130,14 @@ struct DistJob {
   uint8_t* cert_tiles;           // per row tile: whether the second screen visits it
   uint32_t* cert_rows;           // rows evaluated whole
   unsigned int* cert_nrows;
+  // direct distances by group of 8 sorted centers (cert_ng groups; 0: row by row)
+  int cert_ng;
+  unsigned long long* cert_ent;  // (row << 32 | sorted group start) entries
+  unsigned int* cert_ent_n;
+  unsigned int cert_ent_cap;
+  unsigned int* cert_gcnt;
+  unsigned int* cert_goff;
+  uint32_t* cert_srow;
   cudaStream_t stream;
 };
 

@@ -29,6 +29,11 @@
 // Rows the screen does not bound (norms not finite or out of the extra K block's range)
 // and rows whose listed groups overflow the list take every center's direct distance.
 //
+// The direct distances of the groups (the decided rows' and the second screen's) are
+// taken by group: the (row, group) entries are counted and sorted by group, and a block
+// stages its group's 8 centers once for all its rows.  When the workspace has no room
+// for that, the decided rows take theirs row by row and the listed groups entry by entry.
+//
 // d_count receives the number of direct distances evaluated.
 #include "common.cuh"
 #include "engine.h"
@@ -47,7 +52,7 @@ struct CertArgs {
   const int* perm;               // sorted position -> center index
   const float* pp;               // the screen's point norms
   const float* ccmax;            // largest finite center norm (device scalar)
-  const uint8_t* redo;           // rows the screen does not bound
+  uint8_t* redo;                 // rows the screen does not bound (2: entries overflowed)
   const unsigned long long* key; // [4][n] (best screened distance, sorted start of its group)
   const float* d2;               // [4][n] second-best screened distance outside that group
   float* thr;                    // per row: T of the second screen, -inf for a decided row
@@ -59,6 +64,17 @@ struct CertArgs {
   int regions;
   uint32_t* rows;                // rows evaluated whole
   unsigned int* nrows;
+  // by group (ng > 0): (row << 32 | sorted group start) entries of the decided rows and
+  // of the second screen, counted per group of 8 sorted centers, then their rows sorted
+  // by group
+  int ng;
+  unsigned long long* ent;
+  unsigned int* ent_n;
+  unsigned int ent_cap;
+  unsigned int* gcnt;            // entries per group, then the scatter cursors
+  unsigned int* goff;            // exclusive prefix over the groups, ng + 1
+  unsigned int* boff;            // exclusive prefix of the groups' 32-row batches, ng + 1
+  uint32_t* srow;
   unsigned long long* count;
   int64_t* labels;
   int32_t* labels32;
@@ -117,10 +133,31 @@ __device__ int cert_bounds(const CertArgs& a, float ppf, float d1f, float m2f, f
   return 2;
 }
 
-// Four rows per warp, 8 lanes per row.  Rows the winning group decides take its 8 direct
-// distances here; rows it does not decide get their threshold T and their row tile is
-// switched on for the second screen; rows without bounds are listed for
-// cert_whole_rows_kernel.
+// The four partial results of row i merged: the best key, and m2 = the other groups'
+// best distances and the winner's second-best.
+__device__ __forceinline__ float cert_merge(const CertArgs& a, int64_t i, unsigned long long& k1) {
+  const float kInf = __int_as_float(0x7f800000);
+  float m2 = kInf, d2w = kInf;
+  k1 = ~0ull;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const unsigned long long k = __ldg(a.key + g * a.n + i);
+    const float d2 = __ldg(a.d2 + g * a.n + i);
+    if (k < k1) {
+      if (k1 != ~0ull) m2 = fminf(m2, key_dist(k1));
+      k1 = k;
+      d2w = d2;
+    } else {
+      m2 = fminf(m2, key_dist(k));
+    }
+  }
+  return fminf(m2, d2w);
+}
+
+// Row by row (no room to sort by group): four rows per warp, 8 lanes per row.  Rows the
+// winning group decides take its 8 direct distances here; rows it does not decide get
+// their threshold T and their row tile is switched on for the second screen; rows
+// without bounds are listed for cert_whole_rows_kernel.
 template <int REC>
 __global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
   const int lane = threadIdx.x & 31;
@@ -137,22 +174,7 @@ __global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
     float thr = -kInf;
     unsigned long long k1 = ~0ull;
     if (valid && a.redo[i] == 0) {
-      // merge the four partial results: the best key, and m2 = the other groups' best
-      // distances and the winner's second-best
-      float m2 = kInf, d2w = kInf;
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const unsigned long long k = __ldg(a.key + g * a.n + i);
-        const float d2 = __ldg(a.d2 + g * a.n + i);
-        if (k < k1) {
-          if (k1 != ~0ull) m2 = fminf(m2, key_dist(k1));
-          k1 = k;
-          d2w = d2;
-        } else {
-          m2 = fminf(m2, key_dist(k));
-        }
-      }
-      m2 = fminf(m2, d2w);
+      const float m2 = cert_merge(a, i, k1);
       const int r = cert_bounds(a, __ldg(a.pp + i), key_dist(k1), m2, &thr);
       whole = r == 0;
       if (r == 2 && t == 0) {  // to the second screen
@@ -161,7 +183,9 @@ __global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
       }
       if (r != 2) thr = -kInf;
     }
-    if (valid && t == 0) a.thr[i] = thr;
+    // thr: the second screen's T, -inf for a row its group decides, NaN for a row
+    // evaluated whole
+    if (valid && t == 0) a.thr[i] = whole ? __int_as_float(0x7fc00000) : thr;
     const bool grp = valid && !whole && !(thr > -kInf);
     unsigned long long best = ~0ull;
     if (grp) {
@@ -191,6 +215,290 @@ __global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
   }
   evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned int>(evals));
   if (lane == 0 && evals) atomicAdd(a.count, evals);
+}
+
+// By group, one thread per row: a row its group decides gets an entry (row, group); a
+// row it does not decide its threshold T, with its row tile switched on for the second
+// screen; a row without bounds goes to the rows evaluated whole.  thr: T, -inf for a
+// decided row, NaN for a row evaluated whole.
+__global__ void __launch_bounds__(256) cert_decide_kernel(const CertArgs a) {
+  const int lane = threadIdx.x & 31;
+  const float kInf = __int_as_float(0x7f800000);
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < a.n;
+       base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const bool valid = i < a.n;
+    int r = 0;
+    float thr = -kInf;
+    unsigned long long k1 = ~0ull;
+    if (valid && a.redo[i] == 0) {
+      const float m2 = cert_merge(a, i, k1);
+      r = cert_bounds(a, __ldg(a.pp + i), key_dist(k1), m2, &thr);
+    }
+    const bool whole = valid && r == 0, dec = valid && r == 1;
+    if (valid) {
+      if (r == 2) a.tiles[i / 128] = 1;
+      if (r != 0) a.row_key[i] = ~0ull;
+      a.thr[i] = whole ? __int_as_float(0x7fc00000) : (r == 2 ? thr : -kInf);
+    }
+    const unsigned int lt = (1u << lane) - 1u;
+    const unsigned int bd = __ballot_sync(0xffffffffu, dec);
+    if (bd) {
+      unsigned int b = 0;
+      if (lane == 0) b = atomicAdd(a.ent_n, static_cast<unsigned int>(__popc(bd)));
+      b = __shfl_sync(0xffffffffu, b, 0);
+      if (dec) a.ent[b + __popc(bd & lt)] = (static_cast<unsigned long long>(i) << 32) | (k1 & 0xffffffffull);
+    }
+    const unsigned int bw = __ballot_sync(0xffffffffu, whole);
+    if (bw) {
+      unsigned int b = 0;
+      if (lane == 0) b = atomicAdd(a.nrows, static_cast<unsigned int>(__popc(bw)));
+      b = __shfl_sync(0xffffffffu, b, 0);
+      if (whole) a.rows[b + __popc(bw & lt)] = static_cast<uint32_t>(i);
+    }
+  }
+}
+
+// By group: the second screen's entries appended to the decided rows' (one reservation
+// per block); a row whose entry finds no room is evaluated whole (redo 2).
+__global__ void __launch_bounds__(256) cert_gather_kernel(const CertArgs a) {
+  __shared__ unsigned int s_base;
+  constexpr int kBlocksPerRegion = 8;
+  const int r = blockIdx.x / kBlocksPerRegion, b = blockIdx.x % kBlocksPerRegion;
+  unsigned long long cnt64 = a.region_cnt[r];
+  if (cnt64 > a.region_cap) cnt64 = a.region_cap;
+  const uint32_t cnt = static_cast<uint32_t>(cnt64);
+  const uint32_t lo = static_cast<uint32_t>(static_cast<unsigned long long>(cnt) * b / kBlocksPerRegion);
+  const uint32_t hi = static_cast<uint32_t>(static_cast<unsigned long long>(cnt) * (b + 1) / kBlocksPerRegion);
+  if (lo >= hi) return;  // the whole block
+  if (threadIdx.x == 0) s_base = atomicAdd(a.ent_n, hi - lo);
+  __syncthreads();
+  const unsigned long long* gl = a.glist + static_cast<unsigned long long>(r) * a.region_cap;
+  for (uint32_t q = lo + threadIdx.x; q < hi; q += blockDim.x) {
+    const unsigned long long e = gl[q];
+    const unsigned long long pos = static_cast<unsigned long long>(s_base) + (q - lo);
+    const int64_t i = static_cast<int64_t>(e >> 32);
+    if (i >= a.n) continue;
+    if (pos < a.ent_cap)
+      a.ent[pos] = e;
+    else
+      a.redo[i] = 2;
+  }
+}
+
+// This block's contiguous share [lo, hi) of the entries.
+__device__ __forceinline__ void cert_share(const CertArgs& a, unsigned int& lo, unsigned int& hi) {
+  const unsigned int ne = min(*a.ent_n, a.ent_cap);
+  lo = static_cast<unsigned int>(static_cast<unsigned long long>(ne) * blockIdx.x / gridDim.x);
+  hi = static_cast<unsigned int>(static_cast<unsigned long long>(ne) * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Entries per group: a shared-memory histogram per block, flushed once per group.
+__global__ void __launch_bounds__(256) cert_count_kernel(const CertArgs a) {
+  extern __shared__ unsigned int hist[];
+  for (int g = threadIdx.x; g < a.ng; g += blockDim.x) hist[g] = 0;
+  __syncthreads();
+  unsigned int lo, hi;
+  cert_share(a, lo, hi);
+  for (unsigned int q = lo + threadIdx.x; q < hi; q += blockDim.x)
+    atomicAdd(hist + (static_cast<uint32_t>(a.ent[q]) >> 3), 1u);
+  __syncthreads();
+  for (int g = threadIdx.x; g < a.ng; g += blockDim.x)
+    if (hist[g]) atomicAdd(a.gcnt + g, hist[g]);
+}
+
+// Exclusive prefixes over the groups (one block): goff of the entry counts (the counts
+// become the scatter cursors) and boff of the 32-row batches.
+__global__ void __launch_bounds__(1024) cert_scan_kernel(unsigned int* __restrict__ gcnt,
+                                                         unsigned int* __restrict__ goff,
+                                                         unsigned int* __restrict__ boff, int ng) {
+  __shared__ unsigned int wsum[2][32];
+  const int per = (ng + 1023) / 1024;
+  const int g0 = threadIdx.x * per, g1 = min(g0 + per, ng);
+  unsigned int sum = 0, bsum = 0;
+  for (int g = g0; g < g1; ++g) {
+    sum += gcnt[g];
+    bsum += (gcnt[g] + 31u) / 32u;
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  unsigned int incl = sum, bincl = bsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned int v = __shfl_up_sync(0xffffffffu, incl, o);
+    const unsigned int bv = __shfl_up_sync(0xffffffffu, bincl, o);
+    if (lane >= o) {
+      incl += v;
+      bincl += bv;
+    }
+  }
+  if (lane == 31) {
+    wsum[0][w] = incl;
+    wsum[1][w] = bincl;
+  }
+  __syncthreads();
+  if (w < 2) {
+    unsigned int x = wsum[w][lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned int v = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += v;
+    }
+    wsum[w][lane] = x;  // inclusive over the warps
+  }
+  __syncthreads();
+  unsigned int run = incl - sum + (w > 0 ? wsum[0][w - 1] : 0u);
+  unsigned int brun = bincl - bsum + (w > 0 ? wsum[1][w - 1] : 0u);
+  for (int g = g0; g < g1; ++g) {
+    const unsigned int c = gcnt[g];
+    goff[g] = run;
+    boff[g] = brun;
+    gcnt[g] = run;
+    run += c;
+    brun += (c + 31u) / 32u;
+  }
+  if (threadIdx.x == 1023) {
+    goff[ng] = wsum[0][31];
+    boff[ng] = wsum[1][31];
+  }
+}
+
+// Rows of the entries sorted by group (any order within a group): per block, a
+// histogram of its share, one cursor reservation per group, then shared-memory cursors.
+__global__ void __launch_bounds__(256) cert_scatter_kernel(const CertArgs a) {
+  extern __shared__ unsigned int sm[];
+  unsigned int* cur = sm;          // per group: this block's count, then its cursor
+  unsigned int* gbase = sm + a.ng; // per group: this block's first position
+  for (int g = threadIdx.x; g < a.ng; g += blockDim.x) cur[g] = 0;
+  __syncthreads();
+  unsigned int lo, hi;
+  cert_share(a, lo, hi);
+  for (unsigned int q = lo + threadIdx.x; q < hi; q += blockDim.x)
+    atomicAdd(cur + (static_cast<uint32_t>(a.ent[q]) >> 3), 1u);
+  __syncthreads();
+  for (int g = threadIdx.x; g < a.ng; g += blockDim.x) {
+    const unsigned int c = cur[g];
+    gbase[g] = c ? atomicAdd(a.gcnt + g, c) : 0u;
+    cur[g] = 0;
+  }
+  __syncthreads();
+  for (unsigned int q = lo + threadIdx.x; q < hi; q += blockDim.x) {
+    const unsigned long long e = a.ent[q];
+    const uint32_t g = static_cast<uint32_t>(e) >> 3;
+    a.srow[gbase[g] + atomicAdd(cur + g, 1u)] = static_cast<uint32_t>(e >> 32);
+  }
+}
+
+// Batches of up to 32 rows of one group, the batches of all groups in order and each
+// block taking a contiguous share: the group's 8 sorted centers and the rows are staged in
+// shared memory CB_KD dimensions at a time with coalesced loads (the centers once per
+// group when dim <= CB_KD), and thread (row, center) runs the pair's direct sum in the
+// arithmetic and dimension order of direct_dist.  The 8 keys of a row fold into its key
+// with one 64-bit atomicMin.  Rows evaluated whole are skipped.
+constexpr int CB_KD = 64;
+
+template <int REC>
+__global__ void __launch_bounds__(256) cert_bucket_kernel(const CertArgs a) {
+  __shared__ float cs[8][CB_KD + 1];
+  __shared__ float ps[32][CB_KD + 1];
+  __shared__ int cj[8];
+  __shared__ long long ri[32];
+  const int tid = threadIdx.x, r = tid >> 3, c = tid & 7;
+  const int dim = a.dim;
+  const unsigned int nb = a.boff[a.ng];
+  const unsigned int qlo = static_cast<unsigned int>(static_cast<unsigned long long>(nb) * blockIdx.x / gridDim.x);
+  const unsigned int qhi = static_cast<unsigned int>(static_cast<unsigned long long>(nb) * (blockIdx.x + 1) / gridDim.x);
+  if (qlo >= qhi) return;  // the whole block
+  // the group of batch qlo: the largest g with boff[g] <= qlo
+  int g = 0;
+  {
+    int ghi = a.ng - 1;
+    while (g < ghi) {
+      const int mid = (g + ghi + 1) >> 1;
+      if (a.boff[mid] <= qlo) g = mid; else ghi = mid - 1;
+    }
+  }
+  int staged = -1;  // group whose centers are in cs (dim <= CB_KD)
+  unsigned long long evals = 0;
+  for (unsigned int q = qlo; q < qhi; ++q) {
+    while (a.boff[g + 1] <= q) ++g;
+    const unsigned int q0 = a.goff[g] + (q - a.boff[g]) * 32u;
+    const unsigned int q1 = min(q0 + 32u, a.goff[g + 1]);
+    if (tid < 8 && staged != g) {
+      const int64_t s = static_cast<int64_t>(g) * 8 + tid;
+      cj[tid] = s < a.m ? __ldg(a.perm + s) : -1;
+    }
+    if (tid < 32) {
+      long long ii = -1;
+      if (q0 + tid < q1) {
+        ii = static_cast<long long>(a.srow[q0 + tid]);
+        if (a.redo[ii] != 0) ii = -1;
+      }
+      ri[tid] = ii;
+    }
+    DirectAcc<REC> acc;
+    for (int k0 = 0; k0 < dim; k0 += CB_KD) {
+      const int kn = min(CB_KD, dim - k0);
+      __syncthreads();  // ri and cj written, the previous slab consumed
+      if (dim > CB_KD || staged != g) {
+        for (int e = tid; e < 8 * CB_KD; e += 256) {
+          const int cr = e / CB_KD, kk = e % CB_KD;
+          const int jj = cj[cr];
+          cs[cr][kk] = (jj >= 0 && kk < kn) ? __ldg(a.C + static_cast<int64_t>(jj) * dim + k0 + kk) : 0.f;
+        }
+      }
+      for (int e = tid; e < 32 * CB_KD; e += 256) {
+        const int pr = e / CB_KD, kk = e % CB_KD;
+        const long long ii = ri[pr];
+        ps[pr][kk] = (ii >= 0 && kk < kn) ? __ldg(a.P + ii * dim + k0 + kk) : 0.f;
+      }
+      __syncthreads();
+      for (int kk = 0; kk < kn; ++kk) acc.add(ps[r][kk], cs[c][kk]);
+    }
+    staged = g;
+    const long long i = ri[r];
+    const int jc = cj[c];
+    unsigned long long key = ~0ull;
+    if (i >= 0 && jc >= 0) {
+      key = make_key(static_cast<float>(acc.get()), static_cast<uint32_t>(jc));
+      ++evals;
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other < key ? other : key;
+    }
+    if (c == 0 && i >= 0) atomicMin(a.row_key + i, key);
+    __syncthreads();  // cj and ri are rewritten for the next batch
+  }
+  evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned int>(evals));
+  if ((tid & 31) == 0 && evals) atomicAdd(a.count, evals);
+}
+
+// By group: every row's outputs from its key -- rows its group decided and rows of the
+// second screen; rows whose entries overflowed (redo 2) or found no key go to the rows
+// evaluated whole (thr NaN: listed already).
+__global__ void __launch_bounds__(256) cert_out_kernel(const CertArgs a) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < a.n;
+       base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    bool push = false;
+    if (i < a.n) {
+      const float t = a.thr[i];
+      if (t == t) {
+        const unsigned long long k = a.row_key[i];
+        push = a.redo[i] != 0 || k == ~0ull;
+        if (!push) cert_write(a, i, k);
+      }
+    }
+    const unsigned int bal = __ballot_sync(0xffffffffu, push);
+    if (bal) {
+      unsigned int b = 0;
+      if (lane == 0) b = atomicAdd(a.nrows, static_cast<unsigned int>(__popc(bal)));
+      b = __shfl_sync(0xffffffffu, b, 0);
+      if (push) a.rows[b + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint32_t>(i);
+    }
+  }
 }
 
 // Listed rows: one warp per row, lanes over the centers, first index of the minimum.
@@ -312,6 +620,14 @@ static CertArgs cert_args(const DistJob& j, int64_t* labels, int32_t* labels32, 
   a.regions = j.regions;
   a.rows = j.cert_rows;
   a.nrows = j.cert_nrows;
+  a.ng = j.cert_ng;
+  a.ent = j.cert_ent;
+  a.ent_n = j.cert_ent_n;
+  a.ent_cap = j.cert_ent_cap;
+  a.gcnt = j.cert_gcnt;
+  a.goff = j.cert_goff;
+  a.boff = j.cert_goff + (j.cert_ng + 1);
+  a.srow = j.cert_srow;
   a.count = j.count;
   a.labels = labels;
   a.labels32 = labels32;
@@ -341,6 +657,11 @@ static bool cert_job_ok(const DistJob& j) {
 cudaError_t launch_cert_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
   if (!cert_job_ok(j)) return cudaErrorInvalidValue;
   const CertArgs a = cert_args(j, labels, labels32, mind);
+  if (a.ng > 0) {
+    const int blocks = static_cast<int>(std::min<int64_t>((j.n + 255) / 256, static_cast<int64_t>(num_sms()) * 8));
+    cert_decide_kernel<<<blocks, 256, 0, j.stream>>>(a);
+    return cudaGetLastError();
+  }
   const int64_t nq = (j.n + 3) / 4;
   const int blocks = static_cast<int>(std::min<int64_t>((nq + 7) / 8, static_cast<int64_t>(num_sms()) * 8));
   if (j.spec->rec == RC_F32)
@@ -356,15 +677,36 @@ cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* label
   const int gblocks = j.regions * 8;
   const int sblocks = static_cast<int>(std::min<int64_t>((j.n + 255) / 256, static_cast<int64_t>(num_sms()) * 8));
   const int wblocks = num_sms() * 8;
-  if (j.spec->rec == RC_F32) {
-    cert_groups_kernel<RC_F32><<<gblocks, 256, 0, j.stream>>>(a);
-    cert_second_rows_kernel<<<sblocks, 256, 0, j.stream>>>(a);
-    cert_whole_rows_kernel<RC_F32><<<wblocks, 256, 0, j.stream>>>(a);
+  const bool f32 = j.spec->rec == RC_F32;
+  if (a.ng > 0) {
+    // by group: the second screen's entries join the decided rows', sorted by group
+    const size_t hist = static_cast<size_t>(a.ng) * 4;
+    cudaError_t e = cudaFuncSetAttribute(cert_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(hist));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(cert_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(2 * hist));
+    if (e != cudaSuccess) return e;
+    cert_gather_kernel<<<gblocks, 256, 0, j.stream>>>(a);
+    cert_count_kernel<<<wblocks, 256, hist, j.stream>>>(a);
+    cert_scan_kernel<<<1, 1024, 0, j.stream>>>(a.gcnt, a.goff, a.boff, a.ng);
+    cert_scatter_kernel<<<wblocks, 256, 2 * hist, j.stream>>>(a);
+    if (f32)
+      cert_bucket_kernel<RC_F32><<<wblocks, 256, 0, j.stream>>>(a);
+    else
+      cert_bucket_kernel<RC_F64><<<wblocks, 256, 0, j.stream>>>(a);
+    cert_out_kernel<<<sblocks, 256, 0, j.stream>>>(a);
   } else {
-    cert_groups_kernel<RC_F64><<<gblocks, 256, 0, j.stream>>>(a);
+    if (f32)
+      cert_groups_kernel<RC_F32><<<gblocks, 256, 0, j.stream>>>(a);
+    else
+      cert_groups_kernel<RC_F64><<<gblocks, 256, 0, j.stream>>>(a);
     cert_second_rows_kernel<<<sblocks, 256, 0, j.stream>>>(a);
-    cert_whole_rows_kernel<RC_F64><<<wblocks, 256, 0, j.stream>>>(a);
   }
+  if (f32)
+    cert_whole_rows_kernel<RC_F32><<<wblocks, 256, 0, j.stream>>>(a);
+  else
+    cert_whole_rows_kernel<RC_F64><<<wblocks, 256, 0, j.stream>>>(a);
   return cudaGetLastError();
 }
 
