@@ -293,21 +293,31 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     j.cert_thr = reinterpret_cast<float*>(c + static_cast<size_t>(n) * 48);
     j.cert_rows = reinterpret_cast<uint32_t*>(c + static_cast<size_t>(n) * 52);
     j.cert_tiles = c + static_cast<size_t>(n) * 56;
-    // by group, where the region has room: 5 n entries and their sorted rows, and three
-    // tables of ng + 1 counters (ng <= 16384: the block histograms fit shared memory)
+    // by group, where the region has room: 4 n entries and their sorted rows, and three
+    // tables of ng + 1 counters (ng <= 16384: the block histograms fit shared memory);
+    // then, for the second screen over the undecided rows alone, their list, norms,
+    // thresholds and redo bytes (13 n)
     const size_t nb = static_cast<size_t>(n);
     const size_t cs_bytes = al(L.ccap * 128);
     const int64_t ng = (m + 7) / 8;
     const size_t b0 = (nb * 56 + static_cast<size_t>(n_rt) + 15) & ~size_t(15);
-    const size_t need = b0 + nb * 60 + 12 * static_cast<size_t>(ng + 1);
-    j.cert_ng = (ng <= 16384 && 5 * nb <= 0xffffffffull && need <= cs_bytes) ? static_cast<int>(ng) : 0;
+    const size_t need = b0 + nb * 48 + 12 * static_cast<size_t>(ng + 1);
+    j.cert_ng = (ng <= 16384 && 4 * nb <= 0xffffffffull && need <= cs_bytes) ? static_cast<int>(ng) : 0;
     if (j.cert_ng > 0) {
       j.cert_ent = reinterpret_cast<unsigned long long*>(c + b0);
-      j.cert_ent_cap = static_cast<unsigned int>(5 * nb);
-      j.cert_srow = reinterpret_cast<uint32_t*>(c + b0 + nb * 40);
-      j.cert_gcnt = reinterpret_cast<unsigned int*>(c + b0 + nb * 60);
+      j.cert_ent_cap = static_cast<unsigned int>(4 * nb);
+      j.cert_srow = reinterpret_cast<uint32_t*>(c + b0 + nb * 32);
+      j.cert_gcnt = reinterpret_cast<unsigned int*>(c + b0 + nb * 48);
       j.cert_goff = j.cert_gcnt + (ng + 1);
       j.cert_ent_n = reinterpret_cast<unsigned int*>(w + L.hdr + 28);
+      const size_t g0 = (need + 15) & ~size_t(15);
+      if (g0 + nb * 13 <= cs_bytes) {
+        j.cert_F = reinterpret_cast<uint32_t*>(c + g0);
+        j.cert_pg = reinterpret_cast<float*>(c + g0 + nb * 4);
+        j.cert_thr_g = reinterpret_cast<float*>(c + g0 + nb * 8);
+        j.cert_redo_g = c + g0 + nb * 12;
+        j.cert_nF = reinterpret_cast<unsigned int*>(w + L.hdr + 32);
+      }
     }
     j.cert_nrows = reinterpret_cast<unsigned int*>(w + L.hdr + 24);
     // the flagged-pair list is unused too: the second screen lists its groups in the
@@ -323,6 +333,9 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   if (j.fast_argmin && j.regions > kMaxRegions) return fail(EUC_ERR_UNSUPPORTED, "more SMs than list regions");
   // the screening kernel prepares the points itself where it can (no low-precision copy)
   j.fused_rows = j.fast_argmin && tc_fast_can_fuse_rows(j);
+  // certified, points read by the screen itself: the second screen runs on a gathered
+  // low-precision copy of the undecided rows (the copy region is free)
+  j.cert_gather = cert && j.cert_ng > 0 && j.fused_rows && j.cert_F != nullptr && j.Plow != nullptr;
 
   cudaError_t e = cudaMemsetAsync(j.count, 0, 8, st);
   if (e == cudaSuccess && o.tile_counts) {
@@ -331,6 +344,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   }
   if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_nrows, 0, 4, st);
   if (e == cudaSuccess && cert) e = cudaMemsetAsync(j.cert_tiles, 0, static_cast<size_t>(n_rt), st);
+  if (e == cudaSuccess && j.cert_gather) e = cudaMemsetAsync(j.cert_nF, 0, 4, st);
   if (e == cudaSuccess && cert && j.cert_ng > 0) {
     e = cudaMemsetAsync(j.cert_ent_n, 0, 4, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(j.cert_gcnt, 0, static_cast<size_t>(j.cert_ng) * 4, st);
@@ -347,7 +361,19 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     // others; their direct distances, and the rows evaluated whole
     float* md = static_cast<float*>(o.min_dist);
     e = launch_cert_rows(j, o.labels, o.labels32, md);
-    if (e == cudaSuccess) e = launch_tc_fast(j, 2);
+    if (e == cudaSuccess && j.cert_gather) {
+      // the undecided rows gathered into whole row tiles of a low-precision copy, with
+      // their norms, thresholds and redo bytes; the second screen reads that copy
+      e = launch_cert_compact(j);
+      DistJob j2 = j;
+      j2.fused_rows = false;
+      j2.pp = j.cert_pg;
+      j2.redo = j.cert_redo_g;
+      j2.cert_thr = j.cert_thr_g;
+      if (e == cudaSuccess) e = launch_tc_fast(j2, 2);
+    } else if (e == cudaSuccess) {
+      e = launch_tc_fast(j, 2);
+    }
     if (e == cudaSuccess) e = launch_cert_finish(j, o.labels, o.labels32, md);
     return e == cudaSuccess ? ok() : cuda_fail(e, "certified rows");
   }

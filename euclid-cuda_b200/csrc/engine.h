@@ -138,6 +138,14 @@ struct DistJob {
   unsigned int* cert_gcnt;
   unsigned int* cert_goff;
   uint32_t* cert_srow;
+  // second screen over the undecided rows alone (FUSED points): their list, and per
+  // listed row its norm, threshold and redo byte; the low-precision copy goes to Plow
+  bool cert_gather;
+  uint32_t* cert_F;
+  unsigned int* cert_nF;
+  float* cert_pg;
+  float* cert_thr_g;
+  uint8_t* cert_redo_g;
   cudaStream_t stream;
 };
 
@@ -163,6 +171,8 @@ bool tc_fast_can_fuse_rows(const DistJob& j);
 // certified argmin (k_cert.cu): every row's outputs from the screen's partial results,
 // with the direct distances of its candidates (labels, labels32, mind nullable)
 cudaError_t launch_cert_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
+// the undecided rows gathered for the second screen (cert_gather)
+cudaError_t launch_cert_compact(const DistJob& j);
 // ... and, after the second screen, its listed groups and the rows evaluated whole
 cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
 cudaError_t launch_simt(const DistJob& j);

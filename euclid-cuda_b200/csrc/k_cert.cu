@@ -75,6 +75,17 @@ struct CertArgs {
   unsigned int* goff;            // exclusive prefix over the groups, ng + 1
   unsigned int* boff;            // exclusive prefix of the groups' 32-row batches, ng + 1
   uint32_t* srow;
+  // second screen over the undecided rows alone: their list F (nF of them), and per
+  // listed row its norm, threshold and redo byte; its entries name list positions
+  bool gather;
+  uint32_t* F;
+  unsigned int* nF;
+  float* pg;
+  float* thr_g;
+  uint8_t* redo_g;
+  void* plow;                    // the gathered low-precision rows (ldlow elements each)
+  int ldlow;
+  int lowkind;                   // 0 fp16, 1 bf16
   unsigned long long* count;
   int64_t* labels;
   int32_t* labels32;
@@ -237,11 +248,22 @@ __global__ void __launch_bounds__(256) cert_decide_kernel(const CertArgs a) {
     }
     const bool whole = valid && r == 0, dec = valid && r == 1;
     if (valid) {
-      if (r == 2) a.tiles[i / 128] = 1;
+      if (r == 2 && !a.gather) a.tiles[i / 128] = 1;
       if (r != 0) a.row_key[i] = ~0ull;
       a.thr[i] = whole ? __int_as_float(0x7fc00000) : (r == 2 ? thr : -kInf);
     }
     const unsigned int lt = (1u << lane) - 1u;
+    if (a.gather) {
+      // undecided rows to the list of the second screen
+      const bool und = valid && r == 2;
+      const unsigned int bu = __ballot_sync(0xffffffffu, und);
+      if (bu) {
+        unsigned int b = 0;
+        if (lane == 0) b = atomicAdd(a.nF, static_cast<unsigned int>(__popc(bu)));
+        b = __shfl_sync(0xffffffffu, b, 0);
+        if (und) a.F[b + __popc(bu & lt)] = static_cast<uint32_t>(i);
+      }
+    }
     const unsigned int bd = __ballot_sync(0xffffffffu, dec);
     if (bd) {
       unsigned int b = 0;
@@ -274,15 +296,60 @@ __global__ void __launch_bounds__(256) cert_gather_kernel(const CertArgs a) {
   if (threadIdx.x == 0) s_base = atomicAdd(a.ent_n, hi - lo);
   __syncthreads();
   const unsigned long long* gl = a.glist + static_cast<unsigned long long>(r) * a.region_cap;
+  const unsigned int nf = a.gather ? *a.nF : 0u;
   for (uint32_t q = lo + threadIdx.x; q < hi; q += blockDim.x) {
-    const unsigned long long e = gl[q];
+    unsigned long long e = gl[q];
     const unsigned long long pos = static_cast<unsigned long long>(s_base) + (q - lo);
-    const int64_t i = static_cast<int64_t>(e >> 32);
+    int64_t i = static_cast<int64_t>(e >> 32);
+    if (a.gather) {  // the entry names a list position
+      if (i >= nf) continue;
+      i = a.F[i];
+      e = (static_cast<unsigned long long>(i) << 32) | (e & 0xffffffffull);
+    }
     if (i >= a.n) continue;
     if (pos < a.ent_cap)
       a.ent[pos] = e;
     else
       a.redo[i] = 2;
+  }
+}
+
+// Listed rows whose groups did not fit the second screen's list (redo 2 at their list
+// position) are evaluated whole.
+__global__ void __launch_bounds__(256) cert_relay_redo_kernel(const CertArgs a) {
+  const unsigned int nf = *a.nF;
+  for (unsigned int f = blockIdx.x * blockDim.x + threadIdx.x; f < nf; f += gridDim.x * blockDim.x)
+    if (a.redo_g[f] != 0) a.redo[a.F[f]] = 2;
+}
+
+// The undecided rows gathered for the second screen, one warp per list position f, over
+// whole 128-row tiles: row f of the low-precision copy (the operand rounding of the
+// screen, zero beyond dim), its norm and threshold, and its tile switched on; positions
+// past the list get threshold -inf (no group is listed for them).
+template <int LOWK>
+__global__ void __launch_bounds__(256) cert_compact_kernel(const CertArgs a) {
+  const int lane = threadIdx.x & 31;
+  const unsigned int nf = *a.nF;
+  const unsigned int nfp = (nf + 127u) & ~127u;
+  const float kInf = __int_as_float(0x7f800000);
+  for (unsigned int f = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; f < nfp; f += (gridDim.x * blockDim.x) >> 5) {
+    uint16_t* dst = static_cast<uint16_t*>(a.plow) + static_cast<size_t>(f) * a.ldlow;
+    if (f < nf) {
+      const int64_t i = a.F[f];
+      const float* src = a.P + i * a.dim;
+      for (int k = lane; k < a.ldlow; k += 32) {
+        const float x = k < a.dim ? __ldg(src + k) : 0.f;
+        dst[k] = LOWK == 0 ? __half_as_ushort(__float2half_rn(x)) : __bfloat16_as_ushort(__float2bfloat16_rn(x));
+      }
+      if (lane == 0) {
+        a.pg[f] = __ldg(a.pp + i);
+        a.thr_g[f] = a.thr[i];
+        a.tiles[f / 128] = 1;
+      }
+    } else if (lane == 0) {
+      a.pg[f] = 0.f;
+      a.thr_g[f] = -kInf;
+    }
   }
 }
 
@@ -628,6 +695,15 @@ static CertArgs cert_args(const DistJob& j, int64_t* labels, int32_t* labels32, 
   a.goff = j.cert_goff;
   a.boff = j.cert_goff + (j.cert_ng + 1);
   a.srow = j.cert_srow;
+  a.gather = j.cert_gather;
+  a.F = j.cert_F;
+  a.nF = j.cert_nF;
+  a.pg = j.cert_pg;
+  a.thr_g = j.cert_thr_g;
+  a.redo_g = j.cert_redo_g;
+  a.plow = j.Plow;
+  a.ldlow = j.ldlow;
+  a.lowkind = j.spec->gemm == G_TC_BF16 ? 1 : 0;
   a.count = j.count;
   a.labels = labels;
   a.labels32 = labels32;
@@ -671,6 +747,17 @@ cudaError_t launch_cert_rows(const DistJob& j, int64_t* labels, int32_t* labels3
   return cudaGetLastError();
 }
 
+cudaError_t launch_cert_compact(const DistJob& j) {
+  if (!cert_job_ok(j) || !j.cert_gather || j.spec->gemm == G_TC_TF32) return cudaErrorInvalidValue;
+  const CertArgs a = cert_args(j, nullptr, nullptr, nullptr);
+  const int blocks = num_sms() * 8;
+  if (a.lowkind == 0)
+    cert_compact_kernel<0><<<blocks, 256, 0, j.stream>>>(a);
+  else
+    cert_compact_kernel<1><<<blocks, 256, 0, j.stream>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind) {
   if (!cert_job_ok(j)) return cudaErrorInvalidValue;
   const CertArgs a = cert_args(j, labels, labels32, mind);
@@ -688,6 +775,7 @@ cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* label
                                static_cast<int>(2 * hist));
     if (e != cudaSuccess) return e;
     cert_gather_kernel<<<gblocks, 256, 0, j.stream>>>(a);
+    if (a.gather) cert_relay_redo_kernel<<<wblocks, 256, 0, j.stream>>>(a);
     cert_count_kernel<<<wblocks, 256, hist, j.stream>>>(a);
     cert_scan_kernel<<<1, 1024, 0, j.stream>>>(a.gcnt, a.goff, a.boff, a.ng);
     cert_scatter_kernel<<<wblocks, 256, 2 * hist, j.stream>>>(a);
