@@ -33,6 +33,9 @@ PKG = os.path.join(REPO, "euclid-cuda_b200")
 sys.path.insert(0, PKG)
 sys.path.insert(0, REPO)
 
+# euc_argmin's `exact` argument and the Python modules' `exact`, per argmin mode
+MODE_ARG = {"fast": 0, "exact": 1, "certified": 2}
+MODE_PY = {"fast": False, "exact": True, "certified": "certified"}
 METRIC = "distance GFLOP/s vs TC/HBM roofline; Lloyd iters/sec at 1/2/4/8 B200"
 C2 = dict(n=1 << 20, d=128, k=1024, op="fp16_fp32", kappa=5.0, seed=1)
 LLOYD = dict(n=1 << 24, d=64, k=4096, op="bf16_fp32", kappa=0.1, seed=3)
@@ -195,6 +198,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c2", "lloyd"])
+    ap.add_argument("--mode", default="fast", choices=["fast", "exact", "certified"],
+                    help="argmin mode of euc_argmin (the headline line uses the default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -277,12 +282,12 @@ def main():
 
     if a.workload == "c2":
         def step():
-            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, 0, None, ptr(labels), None, ptr(cnt),
-                               ptr(ws), ws.numel(), sp))
+            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, MODE_ARG[a.mode], None, ptr(labels),
+                               None, ptr(cnt), ptr(ws), ws.numel(), sp))
         work_units = 2.0 * n_local * k * d * world  # flop per step, all ranks
     else:
         from kmeans import LloydKMeans
-        km = LloydKMeans(k, op=cfg["op"], kappa=cfg["kappa"])
+        km = LloydKMeans(k, op=cfg["op"], kappa=cfg["kappa"], mode=a.mode)
         state = {"C": Cm}
 
         def step():
@@ -313,8 +318,8 @@ def main():
         if a.workload == "c2":
             step()
         else:
-            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, 0, None, ptr(labels), None, ptr(cnt),
-                               ptr(ws), ws.numel(), sp))
+            check(L.euc_argmin(op_id, ptr(X), ptr(Cm), n_local, k, d, kappa, MODE_ARG[a.mode], None, ptr(labels),
+                               None, ptr(cnt), ptr(ws), ws.numel(), sp))
         kms.append(L.euc_last_kernel_ms())
     L.euc_set_kernel_timing(0)
     kname = L.euc_last_kernel_name().decode()
@@ -353,7 +358,7 @@ def main():
                            f"c4: Lloyd n={n} x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
                            "n_per_rank": n_local, "k": k, "d": d, "op": cfg["op"], "kappa": cfg["kappa"],
                            "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
-                           "parallelism": f"dp{world}"},
+                           "parallelism": f"dp{world}", "argmin_mode": a.mode},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
                 "gpu_launches": None if launches_per_step is None else launches_per_step * a.steps,
                 "launches_per_step": launches_per_step, "flagged_last_step": int(cnt.item())}
@@ -380,8 +385,9 @@ def run_e2e(a, cfg, X, Cm, dev, st, barrier, max_over_ranks, world):
     def e2e_step():
         Xd = Xh.to(dev, non_blocking=True)
         Cd = Ch.to(dev, non_blocking=True)
-        lab, _, _ = euclidean_cuda_mix.pairwise_euclidean_fp16_fp32_argmin(Xd, Cd, C2["kappa"]) \
-            if a.workload == "c2" else _ops.run_argmin(cfg["op"], Xd, Cd, cfg["kappa"], min_dist=False)
+        lab, _, _ = euclidean_cuda_mix.pairwise_euclidean_fp16_fp32_argmin(Xd, Cd, C2["kappa"], exact=MODE_PY[a.mode]) \
+            if a.workload == "c2" else _ops.run_argmin(cfg["op"], Xd, Cd, cfg["kappa"], exact=MODE_PY[a.mode],
+                                                       min_dist=False)
         out_h.copy_(lab, non_blocking=True)
 
     for _ in range(2):

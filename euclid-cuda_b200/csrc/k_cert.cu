@@ -228,12 +228,37 @@ __global__ void __launch_bounds__(256) cert_rows_kernel(const CertArgs a) {
   if (lane == 0 && evals) atomicAdd(a.count, evals);
 }
 
+// Appends this thread's item (if `take`) to a list: one reservation per block and list
+// (a warp-shared global counter would serialise a few hundred thousand atomics).
+// Every thread of the block calls it.
+__device__ __forceinline__ void block_append(bool take, unsigned int* counter, unsigned int* wcnt,
+                                             unsigned int* sbase, unsigned int& pos) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const unsigned int bal = __ballot_sync(0xffffffffu, take);
+  if (lane == 0) wcnt[w] = __popc(bal);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int tot = 0;
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) {
+      const unsigned int c = wcnt[k];
+      wcnt[k] = tot;
+      tot += c;
+    }
+    *sbase = tot ? atomicAdd(counter, tot) : 0u;
+  }
+  __syncthreads();
+  pos = *sbase + wcnt[w] + __popc(bal & ((1u << lane) - 1u));
+  __syncthreads();  // wcnt and sbase are reused by the next call
+}
+
 // By group, one thread per row: a row its group decides gets an entry (row, group); a
-// row it does not decide its threshold T, with its row tile switched on for the second
-// screen; a row without bounds goes to the rows evaluated whole.  thr: T, -inf for a
-// decided row, NaN for a row evaluated whole.
+// row it does not decide its threshold T, and its row tile switched on for the second
+// screen (or, gathering, the row goes to that screen's list); a row without bounds goes
+// to the rows evaluated whole.  thr: T, -inf for a decided row, NaN for a row
+// evaluated whole.
 __global__ void __launch_bounds__(256) cert_decide_kernel(const CertArgs a) {
-  const int lane = threadIdx.x & 31;
+  __shared__ unsigned int wcnt[8];
+  __shared__ unsigned int sbase;
   const float kInf = __int_as_float(0x7f800000);
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < a.n;
        base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -246,38 +271,21 @@ __global__ void __launch_bounds__(256) cert_decide_kernel(const CertArgs a) {
       const float m2 = cert_merge(a, i, k1);
       r = cert_bounds(a, __ldg(a.pp + i), key_dist(k1), m2, &thr);
     }
-    const bool whole = valid && r == 0, dec = valid && r == 1;
+    const bool whole = valid && r == 0, dec = valid && r == 1, und = valid && r == 2;
     if (valid) {
-      if (r == 2 && !a.gather) a.tiles[i / 128] = 1;
+      if (und && !a.gather) a.tiles[i / 128] = 1;
       if (r != 0) a.row_key[i] = ~0ull;
-      a.thr[i] = whole ? __int_as_float(0x7fc00000) : (r == 2 ? thr : -kInf);
+      a.thr[i] = whole ? __int_as_float(0x7fc00000) : (und ? thr : -kInf);
     }
-    const unsigned int lt = (1u << lane) - 1u;
-    if (a.gather) {
-      // undecided rows to the list of the second screen
-      const bool und = valid && r == 2;
-      const unsigned int bu = __ballot_sync(0xffffffffu, und);
-      if (bu) {
-        unsigned int b = 0;
-        if (lane == 0) b = atomicAdd(a.nF, static_cast<unsigned int>(__popc(bu)));
-        b = __shfl_sync(0xffffffffu, b, 0);
-        if (und) a.F[b + __popc(bu & lt)] = static_cast<uint32_t>(i);
-      }
+    unsigned int pos;
+    if (a.gather) {  // block-uniform
+      block_append(und, a.nF, wcnt, &sbase, pos);
+      if (und) a.F[pos] = static_cast<uint32_t>(i);
     }
-    const unsigned int bd = __ballot_sync(0xffffffffu, dec);
-    if (bd) {
-      unsigned int b = 0;
-      if (lane == 0) b = atomicAdd(a.ent_n, static_cast<unsigned int>(__popc(bd)));
-      b = __shfl_sync(0xffffffffu, b, 0);
-      if (dec) a.ent[b + __popc(bd & lt)] = (static_cast<unsigned long long>(i) << 32) | (k1 & 0xffffffffull);
-    }
-    const unsigned int bw = __ballot_sync(0xffffffffu, whole);
-    if (bw) {
-      unsigned int b = 0;
-      if (lane == 0) b = atomicAdd(a.nrows, static_cast<unsigned int>(__popc(bw)));
-      b = __shfl_sync(0xffffffffu, b, 0);
-      if (whole) a.rows[b + __popc(bw & lt)] = static_cast<uint32_t>(i);
-    }
+    block_append(dec, a.ent_n, wcnt, &sbase, pos);
+    if (dec) a.ent[pos] = (static_cast<unsigned long long>(i) << 32) | (k1 & 0xffffffffull);
+    block_append(whole, a.nrows, wcnt, &sbase, pos);
+    if (whole) a.rows[pos] = static_cast<uint32_t>(i);
   }
 }
 
@@ -322,34 +330,50 @@ __global__ void __launch_bounds__(256) cert_relay_redo_kernel(const CertArgs a) 
     if (a.redo_g[f] != 0) a.redo[a.F[f]] = 2;
 }
 
-// The undecided rows gathered for the second screen, one warp per list position f, over
-// whole 128-row tiles: row f of the low-precision copy (the operand rounding of the
-// screen, zero beyond dim), its norm and threshold, and its tile switched on; positions
-// past the list get threshold -inf (no group is listed for them).
+// The undecided rows gathered for the second screen over whole 128-row tiles, one thread
+// per 8 values of a list position f: row f of the low-precision copy (the operand
+// rounding of the screen, zero beyond dim; the points are whole 16-byte vectors), and
+// per position its norm, threshold and row tile; positions past the list get threshold
+// -inf (no group is listed for them).
 template <int LOWK>
 __global__ void __launch_bounds__(256) cert_compact_kernel(const CertArgs a) {
-  const int lane = threadIdx.x & 31;
   const unsigned int nf = *a.nF;
   const unsigned int nfp = (nf + 127u) & ~127u;
   const float kInf = __int_as_float(0x7f800000);
-  for (unsigned int f = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; f < nfp; f += (gridDim.x * blockDim.x) >> 5) {
-    uint16_t* dst = static_cast<uint16_t*>(a.plow) + static_cast<size_t>(f) * a.ldlow;
+  const unsigned int per = static_cast<unsigned int>(a.ldlow) / 8u;  // 8-value pieces per row
+  const unsigned long long items = static_cast<unsigned long long>(nfp) * per;
+  for (unsigned long long t = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < items;
+       t += static_cast<unsigned long long>(gridDim.x) * blockDim.x) {
+    const unsigned int f = static_cast<unsigned int>(t / per), q = static_cast<unsigned int>(t % per);
+    uint4 out = make_uint4(0u, 0u, 0u, 0u);
     if (f < nf) {
       const int64_t i = a.F[f];
-      const float* src = a.P + i * a.dim;
-      for (int k = lane; k < a.ldlow; k += 32) {
-        const float x = k < a.dim ? __ldg(src + k) : 0.f;
-        dst[k] = LOWK == 0 ? __half_as_ushort(__float2half_rn(x)) : __bfloat16_as_ushort(__float2bfloat16_rn(x));
+      const int k = static_cast<int>(q) * 8;
+      float x[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k + 4 * h < a.dim) v = __ldg(reinterpret_cast<const float4*>(a.P + i * a.dim + k + 4 * h));
+        x[4 * h] = v.x;
+        x[4 * h + 1] = v.y;
+        x[4 * h + 2] = v.z;
+        x[4 * h + 3] = v.w;
       }
-      if (lane == 0) {
+      uint32_t b[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        b[e] = LOWK == 0 ? __half_as_ushort(__float2half_rn(x[e])) : __bfloat16_as_ushort(__float2bfloat16_rn(x[e]));
+      out = make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16), b[4] | (b[5] << 16), b[6] | (b[7] << 16));
+      if (q == 0) {
         a.pg[f] = __ldg(a.pp + i);
         a.thr_g[f] = a.thr[i];
         a.tiles[f / 128] = 1;
       }
-    } else if (lane == 0) {
+    } else if (q == 0) {
       a.pg[f] = 0.f;
       a.thr_g[f] = -kInf;
     }
+    reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.plow) + static_cast<size_t>(f) * a.ldlow)[q] = out;
   }
 }
 
@@ -429,8 +453,9 @@ __global__ void __launch_bounds__(1024) cert_scan_kernel(unsigned int* __restric
   }
 }
 
-// Rows of the entries sorted by group (any order within a group): per block, a
-// histogram of its share, one cursor reservation per group, then shared-memory cursors.
+// Rows of the entries sorted by group (any order within a group; ~0 for a row evaluated
+// whole): per block, a histogram of its share, one cursor reservation per group, then
+// shared-memory cursors.
 __global__ void __launch_bounds__(256) cert_scatter_kernel(const CertArgs a) {
   extern __shared__ unsigned int sm[];
   unsigned int* cur = sm;          // per group: this block's count, then its cursor
@@ -451,32 +476,36 @@ __global__ void __launch_bounds__(256) cert_scatter_kernel(const CertArgs a) {
   for (unsigned int q = lo + threadIdx.x; q < hi; q += blockDim.x) {
     const unsigned long long e = a.ent[q];
     const uint32_t g = static_cast<uint32_t>(e) >> 3;
-    a.srow[gbase[g] + atomicAdd(cur + g, 1u)] = static_cast<uint32_t>(e >> 32);
+    const uint32_t i = static_cast<uint32_t>(e >> 32);
+    // a row evaluated whole (redo, final here) is skipped by the group evaluation
+    a.srow[gbase[g] + atomicAdd(cur + g, 1u)] = a.redo[i] != 0 ? 0xffffffffu : i;
   }
 }
 
 // Batches of up to 32 rows of one group, the batches of all groups in order and each
-// block taking a contiguous share: the group's 8 sorted centers and the rows are staged in
-// shared memory CB_KD dimensions at a time with coalesced loads (the centers once per
-// group when dim <= CB_KD), and thread (row, center) runs the pair's direct sum in the
-// arithmetic and dimension order of direct_dist.  The 8 keys of a row fold into its key
-// with one 64-bit atomicMin.  Rows evaluated whole are skipped.
+// block taking a contiguous share.  A batch is evaluated CB_KD dimensions (a slab) at a
+// time: the group's 8 sorted centers and the rows are staged in shared memory (the
+// centers once per group when dim <= CB_KD), and thread (row, center) runs the pair's
+// direct sum in the arithmetic and dimension order of direct_dist.  The next slab's
+// values are loaded into registers while the current one is summed, and the row ids
+// come from a shared-memory window of the sorted rows, so no load waits on another.
+// The 8 keys of a row fold into its key with one 64-bit atomicMin.
 constexpr int CB_KD = 64;
+constexpr int CB_WIN = 256;  // sorted row ids staged per window
 
 template <int REC>
 __global__ void __launch_bounds__(256) cert_bucket_kernel(const CertArgs a) {
   __shared__ float cs[8][CB_KD + 1];
   __shared__ float ps[32][CB_KD + 1];
-  __shared__ int cj[8];
-  __shared__ long long ri[32];
+  __shared__ uint32_t rs[CB_WIN];
   const int tid = threadIdx.x, r = tid >> 3, c = tid & 7;
   const int dim = a.dim;
-  const unsigned int nb = a.boff[a.ng];
+  const int nk = (dim + CB_KD - 1) / CB_KD;
+  const unsigned int nb = a.boff[a.ng], ntot = a.goff[a.ng];
   const unsigned int qlo = static_cast<unsigned int>(static_cast<unsigned long long>(nb) * blockIdx.x / gridDim.x);
   const unsigned int qhi = static_cast<unsigned int>(static_cast<unsigned long long>(nb) * (blockIdx.x + 1) / gridDim.x);
   if (qlo >= qhi) return;  // the whole block
-  // the group of batch qlo: the largest g with boff[g] <= qlo
-  int g = 0;
+  int g = 0;  // the group of batch qlo: the largest g with boff[g] <= qlo
   {
     int ghi = a.ng - 1;
     while (g < ghi) {
@@ -484,58 +513,101 @@ __global__ void __launch_bounds__(256) cert_bucket_kernel(const CertArgs a) {
       if (a.boff[mid] <= qlo) g = mid; else ghi = mid - 1;
     }
   }
-  int staged = -1;  // group whose centers are in cs (dim <= CB_KD)
-  unsigned long long evals = 0;
-  for (unsigned int q = qlo; q < qhi; ++q) {
-    while (a.boff[g + 1] <= q) ++g;
-    const unsigned int q0 = a.goff[g] + (q - a.boff[g]) * 32u;
-    const unsigned int q1 = min(q0 + 32u, a.goff[g + 1]);
-    if (tid < 8 && staged != g) {
-      const int64_t s = static_cast<int64_t>(g) * 8 + tid;
-      cj[tid] = s < a.m ? __ldg(a.perm + s) : -1;
-    }
-    if (tid < 32) {
-      long long ii = -1;
-      if (q0 + tid < q1) {
-        ii = static_cast<long long>(a.srow[q0 + tid]);
-        if (a.redo[ii] != 0) ii = -1;
-      }
-      ri[tid] = ii;
-    }
-    DirectAcc<REC> acc;
-    for (int k0 = 0; k0 < dim; k0 += CB_KD) {
-      const int kn = min(CB_KD, dim - k0);
-      __syncthreads();  // ri and cj written, the previous slab consumed
-      if (dim > CB_KD || staged != g) {
-        for (int e = tid; e < 8 * CB_KD; e += 256) {
-          const int cr = e / CB_KD, kk = e % CB_KD;
-          const int jj = cj[cr];
-          cs[cr][kk] = (jj >= 0 && kk < kn) ? __ldg(a.C + static_cast<int64_t>(jj) * dim + k0 + kk) : 0.f;
-        }
-      }
-      for (int e = tid; e < 32 * CB_KD; e += 256) {
-        const int pr = e / CB_KD, kk = e % CB_KD;
-        const long long ii = ri[pr];
-        ps[pr][kk] = (ii >= 0 && kk < kn) ? __ldg(a.P + ii * dim + k0 + kk) : 0.f;
-      }
-      __syncthreads();
-      for (int kk = 0; kk < kn; ++kk) acc.add(ps[r][kk], cs[c][kk]);
-    }
-    staged = g;
-    const long long i = ri[r];
-    const int jc = cj[c];
-    unsigned long long key = ~0ull;
-    if (i >= 0 && jc >= 0) {
-      key = make_key(static_cast<float>(acc.get()), static_cast<uint32_t>(jc));
-      ++evals;
-    }
+  unsigned int win0 = 0xffffffffu;
+  auto window = [&](unsigned int p0) {  // every thread; a barrier must follow
+    for (int t = tid; t < CB_WIN; t += 256) rs[t] = p0 + t < ntot ? a.srow[p0 + t] : 0xffffffffu;
+    win0 = p0;
+  };
+  auto first = [&](unsigned int q, int gg) { return a.goff[gg] + (q - a.boff[gg]) * 32u; };
+  // registers of the slab loaded ahead
+  float pv[32 * CB_KD / 256], cv[8 * CB_KD / 256];
+  bool cst = false;
+  uint32_t row_n = 0xffffffffu;
+  int jc_n = -1, g_cs = -1;
+  auto issue = [&](unsigned int q, int gg, int kc) {
+    const unsigned int q0 = first(q, gg), q1 = min(q0 + 32u, a.goff[gg + 1]);
+    const int k0 = kc * CB_KD, kn = min(CB_KD, dim - k0);
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-      key = other < key ? other : key;
+    for (int u = 0; u < 32 * CB_KD / 256; ++u) {
+      const int e = tid + u * 256, pr = e / CB_KD, kk = e % CB_KD;
+      const uint32_t row = q0 + pr < q1 ? rs[q0 + pr - win0] : 0xffffffffu;
+      pv[u] = (row != 0xffffffffu && kk < kn) ? __ldg(a.P + static_cast<int64_t>(row) * dim + k0 + kk) : 0.f;
     }
-    if (c == 0 && i >= 0) atomicMin(a.row_key + i, key);
-    __syncthreads();  // cj and ri are rewritten for the next batch
+    cst = nk > 1 || gg != g_cs;
+    if (cst) {
+#pragma unroll
+      for (int u = 0; u < 8 * CB_KD / 256; ++u) {
+        const int e = tid + u * 256, cr = e / CB_KD, kk = e % CB_KD;
+        const int64_t sp = static_cast<int64_t>(gg) * 8 + cr;
+        const int jj = sp < a.m ? __ldg(a.perm + sp) : -1;
+        cv[u] = (jj >= 0 && kk < kn) ? __ldg(a.C + static_cast<int64_t>(jj) * dim + k0 + kk) : 0.f;
+      }
+    }
+    row_n = q0 + r < q1 ? rs[q0 + r - win0] : 0xffffffffu;
+    const int64_t sc = static_cast<int64_t>(gg) * 8 + c;
+    jc_n = sc < a.m ? __ldg(a.perm + sc) : -1;
+  };
+
+  unsigned int q = qlo;
+  int kc = 0;
+  window(first(q, g));
+  __syncthreads();
+  issue(q, g, kc);
+  DirectAcc<REC> acc;
+  unsigned long long evals = 0;
+  while (true) {
+    __syncthreads();  // the previous slab is summed: ps and cs are free
+#pragma unroll
+    for (int u = 0; u < 32 * CB_KD / 256; ++u) {
+      const int e = tid + u * 256;
+      ps[e / CB_KD][e % CB_KD] = pv[u];
+    }
+    if (cst) {
+#pragma unroll
+      for (int u = 0; u < 8 * CB_KD / 256; ++u) {
+        const int e = tid + u * 256;
+        cs[e / CB_KD][e % CB_KD] = cv[u];
+      }
+      g_cs = g;
+    }
+    const uint32_t row = row_n;
+    const int jc = jc_n;
+    const int kn = min(CB_KD, dim - kc * CB_KD);
+    const bool last = kc == nk - 1;
+    // the next slab, and the window of its rows
+    unsigned int qn = q;
+    int kcn = kc + 1, gn = g;
+    if (kcn == nk) {
+      kcn = 0;
+      ++qn;
+      while (qn < qhi && a.boff[gn + 1] <= qn) ++gn;
+    }
+    const bool more = qn < qhi;
+    if (more && kcn == 0) {
+      const unsigned int q0n = first(qn, gn), q1n = min(q0n + 32u, a.goff[gn + 1]);
+      if (q0n < win0 || q1n > win0 + CB_WIN) window(q0n);
+    }
+    __syncthreads();  // the slab and the window are in shared memory
+    if (more) issue(qn, gn, kcn);
+    for (int kk = 0; kk < kn; ++kk) acc.add(ps[r][kk], cs[c][kk]);
+    if (last) {
+      unsigned long long key = ~0ull;
+      if (row != 0xffffffffu && jc >= 0) {
+        key = make_key(static_cast<float>(acc.get()), static_cast<uint32_t>(jc));
+        ++evals;
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other < key ? other : key;
+      }
+      if (c == 0 && row != 0xffffffffu) atomicMin(a.row_key + row, key);
+      acc = DirectAcc<REC>();
+    }
+    if (!more) break;
+    q = qn;
+    kc = kcn;
+    g = gn;
   }
   evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned int>(evals));
   if ((tid & 31) == 0 && evals) atomicAdd(a.count, evals);

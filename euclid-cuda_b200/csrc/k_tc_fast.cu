@@ -784,10 +784,11 @@ static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, con
   const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res, FUSED ? tf_xstage_bytes(args.dim) : 0);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  timing_begin(st, "dist_tc_fast_kernel");
+  // the kernel timing hook times the screen over all rows (not the certified second screen)
+  if (CERT != 2) timing_begin(st, "dist_tc_fast_kernel");
   kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, tba, args);
   e = cudaGetLastError();
-  timing_end(st);
+  if (CERT != 2) timing_end(st);
   return e;
 }
 

@@ -223,10 +223,12 @@ EUC_API int euc_update_centers_fp64(const double* X, const int64_t* labels, int6
  *               arithmetic (the value `op` stores for a pair it flags), and min_dist is
  *               that distance -- the reference's labels when every pair of the row is
  *               flagged.  The tensor-core screen bounds every pair; only the
- *               centers that can win are recomputed (the 8 of the best group of 8
- *               norm-sorted centers when the bounds separate it from the rest, else all
- *               of the row's).  d_count receives the number of direct distances
- *               evaluated.  Other operators return EUC_ERR_UNSUPPORTED.
+ *               centers that can win are recomputed: the 8 of the best group of 8
+ *               norm-sorted centers when the bounds separate it from the rest, else
+ *               those of every group a second screen finds within reach (all of the
+ *               row's when the norms give no bound).  d_count receives the number of
+ *               direct distances evaluated.  Other operators return
+ *               EUC_ERR_UNSUPPORTED.
  *   exact != 0 (other values): every pair's distance is formed exactly as `op` forms
  *               D, and the label is torch.argmin(D, 1) of that D (first index of the
  *               minimum).
