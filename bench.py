@@ -197,7 +197,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "lloyd"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "lloyd", "c5a"],
+                    help="c5a: the D-materialising small-dimension sweep (one GPU, one line per operator and d)")
     ap.add_argument("--mode", default="fast", choices=["fast", "exact", "certified"],
                     help="argmin mode of euc_argmin (the headline line uses the default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -225,6 +226,8 @@ def main():
     import _ops
     from _lib import OPS, check, lib, ptr, stream_of, workspace
     hbm, tc_peak, tc_sus, peak_src = peaks()
+    if a.workload == "c5a":
+        return run_c5a(a, dev, hbm)
 
     def barrier():
         if world > 1:
@@ -366,6 +369,63 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_c5a(a, dev, hbm):
+    """C5a: D = distances of n = 2^27 rows to k = 64 centers at d = 2, 4, 8 (fp32), through
+    the D-materialising operators pairwise_euclidean_fp32_fp32 (GEMM form, cancellation
+    test, direct recompute) and pairwise_euclidean_uniform_fp32_direct.  HBM-bound on the
+    D store: GB/s = 4 (n d + k d + n k) / t, one JSON line per operator and d.  D (32 GiB)
+    is written once per step, far larger than L2."""
+    import ctypes
+
+    import torch
+    from _lib import OPS, check, lib, ptr, stream_of, workspace
+    L = lib()
+    n, k = a.rows or (1 << 27), 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    D = torch.empty((n, k), dtype=torch.float32, device=dev)
+    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    for d in (2, 4, 8):
+        X = torch.randn(n, d, generator=g, device=dev)
+        C = torch.randn(k, d, generator=g, device=dev)
+        sp = stream_of(X)
+        for op in ("fp32_fp32", "uniform_fp32_direct"):
+            if op == "fp32_fp32":
+                ws = workspace(L.euc_workspace_bytes(OPS[op], n, k, d), dev)
+
+                def step():
+                    check(L.euc_mix_fp32_fp32(ptr(X), ptr(C), n, k, d, ctypes.c_float(5.0), ptr(D), ptr(cnt),
+                                              ptr(ws), ws.numel(), sp))
+            else:
+                def step():
+                    check(L.euc_uniform_fp32_direct(ptr(X), ptr(C), n, k, d, ptr(D), sp))
+            for _ in range(a.warmup):
+                step()
+            torch.cuda.synchronize()
+            launches = count_launches(step, torch)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with Clocks(dev.index) as clk:
+                e0.record()
+                for _ in range(a.steps):
+                    step()
+                e1.record()
+                torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / a.steps
+            gbs = 4.0 * (n * d + k * d + n * k) / (ms / 1e3) / 1e9
+            print(json.dumps({"metric": "C5a D GB/s = 4(nd+kd+nk)/t", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                              "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+                              "dtype": "fp32", "data": "synthetic",
+                              "config": {"workload": f"c5a: D of n={n} x d={d} to k={k}, {op}", "op": op, "d": d,
+                                         "l2": "D (32 GiB) far larger than L2"},
+                              "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                           "frac": gbs / hbm},
+                              "flagged_last_step": int(cnt.item()) if op == "fp32_fp32" else None,
+                              "gpu_launches": None if launches is None else launches * a.steps,
+                              "clocks": clk.summary()}), flush=True)
+        del X, C
+    return 0
 
 
 def run_e2e(a, cfg, X, Cm, dev, st, barrier, max_over_ranks, world):

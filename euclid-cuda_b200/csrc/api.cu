@@ -350,6 +350,13 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     if (e == cudaSuccess) e = cudaMemsetAsync(j.cert_gcnt, 0, static_cast<size_t>(j.cert_ng) * 4, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "memset");
+  if (!argmin && !is_tc(s) && thin_d_ok(s, m, j.dim, o.D)) {
+    // D of a small dim: the centers' norms, then one kernel that forms, tests, recomputes
+    // the flagged pairs in place and stores (the rows' norms are formed in it)
+    e = launch_prep(j, false, false);
+    if (e == cudaSuccess) e = launch_thin_d(s, P, C, j.cc, n, m, j.dim, j.kf, o.D, j.count, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, s->name);
+  }
   if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
   if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
   if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);

@@ -176,6 +176,10 @@ cudaError_t launch_cert_compact(const DistJob& j);
 // ... and, after the second screen, its listed groups and the rows evaluated whole
 cudaError_t launch_cert_finish(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
 cudaError_t launch_simt(const DistJob& j);
+// D of small dim (k_simt.cu): whether thin_d_kernel serves the call, and its launch
+bool thin_d_ok(const OpSpec* s, int64_t m, int dim, const void* D);
+cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const void* cc, int64_t n, int64_t m,
+                          int dim, float kf, void* D, unsigned long long* count, cudaStream_t st);
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);
 cudaError_t launch_recompute(const DistJob& j);

@@ -351,8 +351,193 @@ static cudaError_t go_direct(const void* P, const void* C, int64_t n, int64_t m,
   return e;
 }
 
+// ------------------------------------------------------------- small dim, D
+// D for dim <= THIN_MAX_DIM, where the store of D is the whole cost (4 m bytes per row
+// against 4 dim read).  The dimension is padded to DIM in {2, 4, 8, 16} with zeros
+// (a zero term adds exactly nothing to any of the sums below), so every loop is unrolled.
+// A block walks chunks of THIN_RB consecutive rows: the chunk's points arrive in shared
+// memory with coalesced loads (the next chunk's are loaded into registers while the
+// current one is formed), the centers sit in shared memory k-major (CsT[k][j]); each
+// half-warp forms one row at a time, lane l the 4 columns 4 l .. 4 l + 3 of each
+// 64-column pass, stored with one 16-byte store (256 contiguous bytes per half-warp).
+// Every value is formed with the arithmetic of the tiled kernels above:
+//   THIN_DIRECT  sum_k (p_k - c_k)^2, fused multiply-adds in k order (direct_kernel);
+//   THIN_FORM    s = sum_k p_k c_k in k order, d = max((pp - 2 s) + cc, 0), pp the
+//                row's fmaf norm in k order and cc the prepared center norm
+//                (simt_dist_kernel, FM_F32), and with FLAG the cancellation test
+//                d <= K (pp + cc): a flagged pair stores its direct distance in the REC
+//                arithmetic here, and is counted (no list).
+constexpr int THIN_MAX_DIM = 16;
+constexpr int THIN_MAX_CF = 10240;  // m * padded dim floats of centers in shared memory (40 KB)
+constexpr int THIN_RB = 128;       // rows per chunk
+enum ThinMode { THIN_DIRECT = 0, THIN_FORM = 1 };
+
+// a flagged pair's direct distance from the staged row and the k-major center column
+// (out of line: it is rare, and keeps the common path's registers free)
+template <int DIM, int REC>
+__device__ __noinline__ float thin_recompute(const float* prow, const float* ccol, int m) {
+  DirectAcc<REC> r;
+#pragma unroll
+  for (int k = 0; k < DIM; ++k) r.add(prow[k], ccol[k * m]);
+  return static_cast<float>(r.get());
+}
+
+template <int DIM, int MODE, bool FLAG, int REC>
+__global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict__ P, const float* __restrict__ C,
+                                                        const float* __restrict__ cc, int64_t n, int m, int dim,
+                                                        float kf, float* __restrict__ D,
+                                                        unsigned long long* __restrict__ count) {
+  constexpr int PER = THIN_RB * DIM / 256;  // a thread's share of a chunk's values, at most
+  __shared__ __align__(16) float ps[THIN_RB * DIM];
+  extern __shared__ __align__(16) float csT[];  // [DIM][m], rows dim .. DIM-1 zero
+  for (int e = threadIdx.x; e < m * DIM; e += blockDim.x) {
+    const int k = e / m, j = e % m;
+    csT[e] = k < dim ? C[static_cast<int64_t>(j) * dim + k] : 0.f;
+  }
+  for (int e = threadIdx.x; e < THIN_RB * DIM; e += blockDim.x) ps[e] = 0.f;  // padding stays zero
+  const int lane = threadIdx.x & 31, hl = lane & 15, hw = threadIdx.x >> 4;  // 16 half-warps
+  const int64_t nchunk = (n + THIN_RB - 1) / THIN_RB;
+  const int cvals = THIN_RB * dim;  // values of a whole chunk
+  float pre[PER];
+  auto load = [&](int64_t ch) {  // the chunk's values, coalesced (rows are contiguous)
+    const int64_t base = ch * THIN_RB * dim, lim = n * dim;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = threadIdx.x + u * 256;
+      pre[u] = (ch < nchunk && e < cvals && base + e < lim) ? __ldg(P + base + e) : 0.f;
+    }
+  };
+  int64_t ch = blockIdx.x;
+  load(ch);
+  unsigned int flagged = 0;
+  for (; ch < nchunk; ch += gridDim.x) {
+    __syncthreads();  // the previous chunk is formed (the first time: centers and padding in)
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = threadIdx.x + u * 256;
+      if (e < cvals) ps[(e / dim) * DIM + e % dim] = pre[u];
+    }
+    __syncthreads();
+    load(ch + gridDim.x);
+    const int64_t row0 = ch * THIN_RB;
+#pragma unroll 1
+    for (int rr = hw; rr < THIN_RB; rr += 16) {
+      const int64_t i = row0 + rr;
+      if (i >= n) break;
+      float p[DIM];
+#pragma unroll
+      for (int k = 0; k < DIM; k += 2) {
+        const float2 v = *reinterpret_cast<const float2*>(ps + rr * DIM + k);
+        p[k] = v.x;
+        p[k + 1] = v.y;
+      }
+      float pp = 0.f;
+      if constexpr (MODE == THIN_FORM) {
+#pragma unroll
+        for (int k = 0; k < DIM; ++k) pp = __fmaf_rn(p[k], p[k], pp);
+      }
+      for (int j0 = hl * 4; j0 < m; j0 += 64) {
+        float v[4];
+        if constexpr (MODE == THIN_DIRECT) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int k = 0; k < DIM; ++k) {
+            const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
+            const float cvs[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float d = p[k] - cvs[c];
+              acc[c] = __fmaf_rn(d, d, acc[c]);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v[c] = acc[c];
+        } else {
+          float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int k = 0; k < DIM; ++k) {
+            const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
+            sacc[0] = __fmaf_rn(p[k], cv.x, sacc[0]);
+            sacc[1] = __fmaf_rn(p[k], cv.y, sacc[1]);
+            sacc[2] = __fmaf_rn(p[k], cv.z, sacc[2]);
+            sacc[3] = __fmaf_rn(p[k], cv.w, sacc[3]);
+          }
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cc + j0));
+          const float ccs[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float d = fmaxf(__fadd_rn(__fmaf_rn(-2.f, sacc[c], pp), ccs[c]), 0.f);
+            v[c] = d;
+            if constexpr (FLAG) {
+              if (d <= __fmul_rn(kf, __fadd_rn(pp, ccs[c]))) {  // the direct recompute
+                v[c] = thin_recompute<DIM, REC>(ps + rr * DIM, csT + j0 + c, m);
+                ++flagged;
+              }
+            }
+          }
+        }
+        *reinterpret_cast<float4*>(D + i * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  }
+  if constexpr (FLAG) {
+    const unsigned int tot = __reduce_add_sync(0xffffffffu, flagged);
+    if (lane == 0 && tot) atomicAdd(count, static_cast<unsigned long long>(tot));
+  }
+}
+
+// Whether thin_d_kernel serves this D-mode call: fp32 in and out, dim <= 16, m a multiple
+// of 4 with the centers in 40 KB of shared memory, D 16-byte aligned.
+bool thin_d_ok(const OpSpec* s, int64_t m, int dim, const void* D) {
+  if (s->in != IN_F32 || s->out != OUT_F32 || D == nullptr) return false;
+  if (dim < 1 || dim > THIN_MAX_DIM || m < 4 || (m & 3) != 0) return false;
+  const int pd = dim <= 2 ? 2 : (dim <= 4 ? 4 : (dim <= 8 ? 8 : 16));
+  if (m * pd > THIN_MAX_CF) return false;
+  if ((reinterpret_cast<uintptr_t>(D) & 15u) != 0) return false;
+  if (s->gemm == G_DIRECT) return true;
+  // the fp32 form with fmaf norms: single, and the mix operators on an fp32 GEMM
+  return s->gemm == G_SIMT_F32 && s->form == FM_F32 && s->norm == NM_F32_FMA &&
+         (s->flag == FL_NONE || (s->flag == FL_F32 && (s->rec == RC_F32 || s->rec == RC_F64)));
+}
+
+cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const void* cc, int64_t n, int64_t m,
+                          int dim, float kf, void* D, unsigned long long* count, cudaStream_t st) {
+  if (!thin_d_ok(s, m, dim, D)) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  const int64_t nchunk = (n + THIN_RB - 1) / THIN_RB;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(nchunk, num_sms() * 8)));
+  const float* Pf = static_cast<const float*>(P);
+  const float* Cf = static_cast<const float*>(C);
+  const float* ccf = static_cast<const float*>(cc);
+  float* Df = static_cast<float*>(D);
+  const int mi = static_cast<int>(m);
+  timing_begin(st, "thin_d_kernel");
+  const int pd = dim <= 2 ? 2 : (dim <= 4 ? 4 : (dim <= 8 ? 8 : 16));
+  const size_t smem = static_cast<size_t>(m) * pd * 4;
+#define THIN_GO(DIM_)                                                                                         \
+  if (pd == DIM_) {                                                                                           \
+    if (s->gemm == G_DIRECT)                                                                                  \
+      thin_d_kernel<DIM_, THIN_DIRECT, false, RC_NONE><<<blocks, 256, smem, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count); \
+    else if (s->flag == FL_NONE)                                                                              \
+      thin_d_kernel<DIM_, THIN_FORM, false, RC_NONE><<<blocks, 256, smem, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count);   \
+    else if (s->rec == RC_F32)                                                                                \
+      thin_d_kernel<DIM_, THIN_FORM, true, RC_F32><<<blocks, 256, smem, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count);     \
+    else                                                                                                      \
+      thin_d_kernel<DIM_, THIN_FORM, true, RC_F64><<<blocks, 256, smem, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count);     \
+  }
+  THIN_GO(2)
+  THIN_GO(4)
+  THIN_GO(8)
+  THIN_GO(16)
+#undef THIN_GO
+  cudaError_t e = cudaGetLastError();
+  timing_end(st);
+  return e;
+}
+
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim, void* D,
                           cudaStream_t st) {
+  if (thin_d_ok(s, m, dim, D)) return launch_thin_d(s, P, C, nullptr, n, m, dim, 0.f, D, nullptr, st);
   switch (s->in) {
     case IN_F16: return go_direct<__half, float, __half>(P, C, n, m, dim, D, st);
     case IN_BF16: return go_direct<__nv_bfloat16, float, __nv_bfloat16>(P, C, n, m, dim, D, st);
