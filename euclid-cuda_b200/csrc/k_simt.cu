@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
                                                         float kf, float* __restrict__ D,
                                                         unsigned long long* __restrict__ count) {
   constexpr int PER = THIN_RB * DIM / 256;  // a thread's share of a chunk's values, at most
+  constexpr int R = DIM <= 8 ? 2 : 1;        // rows a half-warp forms together
   __shared__ __align__(16) float ps[THIN_RB * DIM];
   extern __shared__ __align__(16) float csT[];  // [DIM][m], rows dim .. DIM-1 zero
   for (int e = threadIdx.x; e < m * DIM; e += blockDim.x) {
@@ -421,62 +422,85 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
     load(ch + gridDim.x);
     const int64_t row0 = ch * THIN_RB;
 #pragma unroll 1
-    for (int rr = hw; rr < THIN_RB; rr += 16) {
-      const int64_t i = row0 + rr;
-      if (i >= n) break;
-      float p[DIM];
+    for (int rr = hw; rr < THIN_RB; rr += 16 * R) {
+      // R rows at a time (rr, rr + 16, ...): the centers' values are read once for all
+      float p[R][DIM], pp[R];
+      bool ok[R];
 #pragma unroll
-      for (int k = 0; k < DIM; k += 2) {
-        const float2 v = *reinterpret_cast<const float2*>(ps + rr * DIM + k);
-        p[k] = v.x;
-        p[k + 1] = v.y;
-      }
-      float pp = 0.f;
-      if constexpr (MODE == THIN_FORM) {
+      for (int t = 0; t < R; ++t) {
+        const int rt = rr + 16 * t;
+        ok[t] = row0 + rt < n;
 #pragma unroll
-        for (int k = 0; k < DIM; ++k) pp = __fmaf_rn(p[k], p[k], pp);
+        for (int k = 0; k < DIM; k += 2) {
+          const float2 v = *reinterpret_cast<const float2*>(ps + rt * DIM + k);
+          p[t][k] = v.x;
+          p[t][k + 1] = v.y;
+        }
+        pp[t] = 0.f;
+        if constexpr (MODE == THIN_FORM) {
+#pragma unroll
+          for (int k = 0; k < DIM; ++k) pp[t] = __fmaf_rn(p[t][k], p[t][k], pp[t]);
+        }
       }
+      if (!ok[0]) break;
       for (int j0 = hl * 4; j0 < m; j0 += 64) {
-        float v[4];
-        if constexpr (MODE == THIN_DIRECT) {
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[R][4];
 #pragma unroll
-          for (int k = 0; k < DIM; ++k) {
-            const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
-            const float cvs[4] = {cv.x, cv.y, cv.z, cv.w};
+        for (int t = 0; t < R; ++t)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[t][c] = 0.f;
+#pragma unroll
+        for (int k = 0; k < DIM; ++k) {
+          const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
+          const float cvs[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+          for (int t = 0; t < R; ++t)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-              const float d = p[k] - cvs[c];
-              acc[c] = __fmaf_rn(d, d, acc[c]);
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) v[c] = acc[c];
-        } else {
-          float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int k = 0; k < DIM; ++k) {
-            const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
-            sacc[0] = __fmaf_rn(p[k], cv.x, sacc[0]);
-            sacc[1] = __fmaf_rn(p[k], cv.y, sacc[1]);
-            sacc[2] = __fmaf_rn(p[k], cv.z, sacc[2]);
-            sacc[3] = __fmaf_rn(p[k], cv.w, sacc[3]);
-          }
-          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cc + j0));
-          const float ccs[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float d = fmaxf(__fadd_rn(__fmaf_rn(-2.f, sacc[c], pp), ccs[c]), 0.f);
-            v[c] = d;
-            if constexpr (FLAG) {
-              if (d <= __fmul_rn(kf, __fadd_rn(pp, ccs[c]))) {  // the direct recompute
-                v[c] = thin_recompute<DIM, REC>(ps + rr * DIM, csT + j0 + c, m);
-                ++flagged;
+              if constexpr (MODE == THIN_DIRECT) {
+                const float d = p[t][k] - cvs[c];
+                acc[t][c] = __fmaf_rn(d, d, acc[t][c]);
+              } else {
+                acc[t][c] = __fmaf_rn(p[t][k], cvs[c], acc[t][c]);
               }
             }
+        }
+        float ccs[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (MODE == THIN_FORM) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cc + j0));
+          ccs[0] = c4.x;
+          ccs[1] = c4.y;
+          ccs[2] = c4.z;
+          ccs[3] = c4.w;
+        }
+        uint32_t fmask = 0;  // flagged pairs (bit 4 t + c)
+#pragma unroll
+        for (int t = 0; t < R; ++t) {
+          if (!ok[t]) continue;
+          const int rt = rr + 16 * t;
+          float v[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if constexpr (MODE == THIN_DIRECT) {
+              v[c] = acc[t][c];
+            } else {
+              const float d = fmaxf(__fadd_rn(__fmaf_rn(-2.f, acc[t][c], pp[t]), ccs[c]), 0.f);
+              v[c] = d;
+              if constexpr (FLAG) fmask |= static_cast<uint32_t>(d <= __fmul_rn(kf, __fadd_rn(pp[t], ccs[c]))) << (4 * t + c);
+            }
+          }
+          *reinterpret_cast<float4*>(D + (row0 + rt) * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        if constexpr (FLAG) {
+          // flagged pairs (rare): their direct distance replaces the stored value
+          while (fmask) {
+            const int b = __ffs(fmask) - 1;
+            fmask &= fmask - 1u;
+            const int rt = rr + 16 * (b >> 2), c = b & 3;
+            D[(row0 + rt) * m + j0 + c] = thin_recompute<DIM, REC>(ps + rt * DIM, csT + j0 + c, m);
+            ++flagged;
           }
         }
-        *reinterpret_cast<float4*>(D + i * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
       }
     }
   }
