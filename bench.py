@@ -418,7 +418,7 @@ def run_c5a(a, dev, hbm):
                               "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
                               "dtype": "fp32", "data": "synthetic",
                               "config": {"workload": f"c5a: D of n={n} x d={d} to k={k}, {op}", "op": op, "d": d,
-                                         "l2": "D (32 GiB) far larger than L2"},
+                                         "l2": f"D ({n * k * 4 / 2 ** 30:.1f} GiB) larger than L2"},
                               "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
                                            "frac": gbs / hbm},
                               "flagged_last_step": int(cnt.item()) if op == "fp32_fp32" else None,
