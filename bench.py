@@ -197,8 +197,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "lloyd", "c5a"],
-                    help="c5a: the D-materialising small-dimension sweep (one GPU, one line per operator and d)")
+    ap.add_argument("--workload", default="c2", choices=["c2", "lloyd", "c5a", "configs"],
+                    help="c5a: the D-materialising small-dimension sweep; configs: C1, C3 and C5b (one GPU, "
+                         "one line per measurement)")
     ap.add_argument("--mode", default="fast", choices=["fast", "exact", "certified"],
                     help="argmin mode of euc_argmin (the headline line uses the default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -228,6 +229,8 @@ def main():
     hbm, tc_peak, tc_sus, peak_src = peaks()
     if a.workload == "c5a":
         return run_c5a(a, dev, hbm)
+    if a.workload == "configs":
+        return run_configs(a, dev, tc_peak)
 
     def barrier():
         if world > 1:
@@ -369,6 +372,121 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_configs(a, dev, tc_peak):
+    """The other benchmark configurations, each timed with CUDA events (inputs resident,
+    larger than L2 except C1's 12.8 MB, whose step reads them once):
+      C1  one fp64 Lloyd iteration, n = 100 000, d = 32, k = 64 (iter/s);
+      C3  the cancellation regime, n = 2^22, d = 64, k = 256 at offset 1000, bf16_fp64:
+          D with every pair recomputed in fp64, and the fused argmin (exact and certified);
+      C5b d = 1024, n = 2^21, k = 8192, fp16-representable values: the tensorcore_fp16_fp32
+          D (64 GiB) and the fused argmin (TFLOP/s = 2 n k d / t)."""
+    import ctypes
+
+    import torch
+    import _ops
+    from _lib import OPS, check, lib, ptr, stream_of, workspace
+    from kmeans import LloydKMeans
+    L = lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(dev.index) as clk:
+            e0.record()
+            for _ in range(steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps, clk.summary()
+
+    def emit(cfg, value, unit, ms, clk, extra):
+        line = {"metric": f"{cfg} {unit}", "value": value, "unit": unit, "n_gpus": 1, "ms_per_step": ms,
+                "higher_is_better": True, "data": "synthetic", "clocks": clk}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+
+    # C1
+    n, d, k = 100_000, 32, 64
+    true_c = torch.rand(k, d, generator=g, device=dev, dtype=torch.float64) * 20 - 10
+    X = true_c[torch.randint(0, k, (n,), generator=g, device=dev)] + torch.randn(n, d, generator=g, device=dev,
+                                                                                 dtype=torch.float64)
+    C0 = X[torch.randperm(n, generator=g, device=dev)[:k]].contiguous()
+    km = LloydKMeans(k, op="double", kappa=5.0)
+    ms, clk = timed(lambda: km.step(X, C0), 20, 5)
+    emit("C1", 1e3 / ms, "iter/s", ms, clk, {"dtype": "fp64", "config": {"workload": "c1: Lloyd n=100000 x d=32, "
+                                                                          "k=64, fp64", "op": "double"}})
+    del X, C0, true_c
+    # C3
+    n, d, k = 1 << 22, 64, 256
+    mu = torch.randn(k, d, generator=g, device=dev) * 0.1
+    X = 1000.0 + mu[torch.randint(0, k, (n,), generator=g, device=dev)] + 0.01 * torch.randn(n, d, generator=g,
+                                                                                             device=dev)
+    C = X[torch.randperm(n, generator=g, device=dev)[:k]].contiguous()
+    D = torch.empty((n, k), dtype=torch.float32, device=dev)
+    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    ws = workspace(L.euc_workspace_bytes(OPS["bf16_fp64"], n, k, d), dev)
+    sp = stream_of(X)
+
+    def c3_d():
+        check(L.euc_mix_bf16_fp64(ptr(X), ptr(C), n, k, d, ctypes.c_float(5.0), ptr(D), ptr(cnt), ptr(ws),
+                                  ws.numel(), sp))
+    ms, clk = timed(c3_d, 3, 2)
+    emit("C3", 2.0 * n * k * d / (ms / 1e3) / 1e9, "GFLOP/s", ms, clk,
+         {"dtype": "bf16", "recomputed": int(cnt.item()), "recompute_rate": int(cnt.item()) / (n * k),
+          "config": {"workload": "c3: D of n=4194304 x d=64 to k=256 at offset 1000, bf16_fp64 (fp64 recompute)",
+                     "op": "bf16_fp64"}})
+    del D, ws
+    for mode in ("exact", "certified"):
+        ex = True if mode == "exact" else "certified"
+        out = {}
+
+        def c3_a():
+            out["r"] = _ops.run_argmin("bf16_fp64", X, C, 5.0, exact=ex, labels_dtype=torch.int32, min_dist=False)
+        ms, clk = timed(c3_a, 3, 2)
+        emit("C3 argmin", 2.0 * n * k * d / (ms / 1e3) / 1e9, "GFLOP/s", ms, clk,
+             {"dtype": "bf16", "count": int(out["r"][2].item()),
+              "config": {"workload": f"c3: argmin n=4194304 x d=64, k=256, bf16_fp64, {mode}", "op": "bf16_fp64",
+                         "argmin_mode": mode}})
+    del X, C
+    # C5b
+    n, d, k = 1 << 21, 1024, 8192
+    X = torch.randn(n, d, generator=g, device=dev).half().float()
+    C = torch.randn(k, d, generator=g, device=dev).half().float()
+    D = torch.empty((n, k), dtype=torch.float32, device=dev)
+    ws = workspace(L.euc_workspace_bytes(OPS["tensorcore_fp16_fp32"], n, k, d), dev)
+    sp = stream_of(X)
+
+    def c5b_d():
+        check(L.euc_tensorcore_fp16_fp32(ptr(X), ptr(C), n, k, d, ctypes.c_float(5.0), 32, ptr(D), None, ptr(ws),
+                                         ws.numel(), sp))
+    ms, clk = timed(c5b_d, 3, 2)
+    tf = 2.0 * n * k * d / (ms / 1e3) / 1e12
+    emit("C5b", tf * 1e3, "GFLOP/s", ms, clk,
+         {"dtype": "fp16", "roofline": {"bound": "tensor", "achieved": tf, "peak": tc_peak, "unit": "TFLOP/s",
+                                        "frac": tf / tc_peak},
+          "config": {"workload": "c5b: D (64 GiB) of n=2097152 x d=1024 to k=8192, tensorcore_fp16_fp32",
+                     "op": "tensorcore_fp16_fp32"}})
+    del D, ws
+    for mode in ("fast", "exact"):
+        out = {}
+
+        def c5b_a():
+            out["r"] = _ops.run_argmin("tensorcore_fp16_fp32", X, C, 5.0, exact=(mode == "exact"),
+                                       labels_dtype=torch.int32, min_dist=False)
+        ms, clk = timed(c5b_a, 3, 2)
+        tf = 2.0 * n * k * d / (ms / 1e3) / 1e12
+        emit("C5b argmin", tf * 1e3, "GFLOP/s", ms, clk,
+             {"dtype": "fp16", "count": int(out["r"][2].item()),
+              "roofline": {"bound": "tensor", "achieved": tf, "peak": tc_peak, "unit": "TFLOP/s", "frac": tf / tc_peak},
+              "config": {"workload": f"c5b: argmin n=2097152 x d=1024, k=8192, tensorcore_fp16_fp32, {mode}",
+                         "op": "tensorcore_fp16_fp32", "argmin_mode": mode}})
+    return 0
 
 
 def run_c5a(a, dev, hbm):
