@@ -57,8 +57,9 @@ __global__ void __launch_bounds__(256) recompute_kernel(const RecArgs a) {
         static_cast<TOUT*>(a.D)[i * a.m + j] = static_cast<TOUT>(v);
       }
     }
-  } else if constexpr (!ARGMIN) {
+  } else if constexpr (!ARGMIN && REC != RC_F32 && REC != RC_F64) {
     // overflow: dense sweep, flag re-derived from the stored (pre-recompute) distance
+    // (fp32 and fp64 recomputes take recompute_dense_tiled_kernel instead)
     const uint64_t total = static_cast<uint64_t>(a.n) * static_cast<uint64_t>(a.m);
     for (uint64_t t = t0; t < total; t += stride) {
       const int64_t i = static_cast<int64_t>(t / static_cast<uint64_t>(a.m));
@@ -144,6 +145,104 @@ __global__ void __launch_bounds__(RW_WARPS * 32, 4) recompute_argmin_rows_kernel
   }
 }
 
+// D mode, list overflowed (more flagged pairs than it holds), fp32 or fp64 recompute:
+// every flagged pair recomputed by tiles.  A block takes 64 x 64 tiles of D (grid-stride);
+// each thread re-derives the flags of its 4 x 4 elements from the stored distance and
+// the norms (the test of the distance kernel, bit-identical), a tile without a flag is
+// skipped, and otherwise the rows and centers are staged through shared memory 16
+// dimensions at a time and every element's direct sum is formed in the operator's
+// arithmetic and dimension order (direct_dist); flagged elements are stored.  The
+// kernel returns at once when the list held every flagged pair.
+constexpr int RT_B = 64, RT_K = 16;
+
+template <typename TIN, int REC, typename TOUT, int FLAG>
+__global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArgs a) {
+  using TACC = typename std::conditional<REC == RC_F64, double, float>::type;
+  if (*a.count <= a.cap) return;  // the list path has done it
+  __shared__ TACC As[RT_K][RT_B + 1];
+  __shared__ TACC Bs[RT_K][RT_B + 1];
+  const TIN* P = static_cast<const TIN*>(a.P);
+  const TIN* C = static_cast<const TIN*>(a.C);
+  TOUT* D = static_cast<TOUT*>(a.D);
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t nrt = (a.n + RT_B - 1) / RT_B, nct = (a.m + RT_B - 1) / RT_B;
+  for (int64_t tile = blockIdx.x; tile < nrt * nct; tile += gridDim.x) {
+    const int64_t row0 = (tile / nct) * RT_B, col0 = (tile % nct) * RT_B;
+    uint32_t fmask = 0;  // bit 4 r + c: element (row0 + 4 ty + r, col0 + 4 tx + c) is flagged
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t i = row0 + ty * 4 + r;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int64_t j = col0 + tx * 4 + c;
+        if (i >= a.n || j >= a.m) continue;
+        bool flag;
+        if constexpr (FLAG == FL_F32) {
+          const float pp = static_cast<const float*>(a.pp)[i], cc = static_cast<const float*>(a.cc)[j];
+          flag = static_cast<float>(D[i * a.m + j]) <= __fmul_rn(a.kf, __fadd_rn(pp, cc));
+        } else {
+          const double pp = static_cast<const double*>(a.pp)[i], cc = static_cast<const double*>(a.cc)[j];
+          flag = static_cast<double>(D[i * a.m + j]) <= a.kd * (pp + cc);
+        }
+        fmask |= static_cast<uint32_t>(flag) << (4 * r + c);
+      }
+    }
+    if (!__syncthreads_or(fmask != 0)) continue;  // block-uniform
+    TACC acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[r][c] = 0;
+    for (int k0 = 0; k0 < a.dim; k0 += RT_K) {
+      for (int t = threadIdx.x; t < RT_B * RT_K; t += 256) {
+        const int rr = t / RT_K, kk = t % RT_K;
+        const int64_t gi = row0 + rr, gj = col0 + rr;
+        const int gk = k0 + kk;
+        TACC pv = 0, cv = 0;
+        if (gk < a.dim) {
+          if constexpr (REC == RC_F64) {
+            if (gi < a.n) pv = wide(P[gi * a.dim + gk]);
+            if (gj < a.m) cv = wide(C[gj * a.dim + gk]);
+          } else {
+            if (gi < a.n) pv = narrow(P[gi * a.dim + gk]);
+            if (gj < a.m) cv = narrow(C[gj * a.dim + gk]);
+          }
+        }
+        As[kk][rr] = pv;
+        Bs[kk][rr] = cv;
+      }
+      __syncthreads();
+      const int kend = min(RT_K, a.dim - k0);  // padded dimensions must not add a term
+      for (int kk = 0; kk < kend; ++kk) {
+        TACC av[4], bv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) av[r] = As[kk][ty * 4 + r];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) bv[c] = Bs[kk][tx * 4 + c];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if constexpr (REC == RC_F64) {
+              const double d = av[r] - bv[c];
+              acc[r][c] = fma(d, d, acc[r][c]);
+            } else {
+              const float d = __fsub_rn(av[r], bv[c]);
+              acc[r][c] = __fmaf_rn(d, d, acc[r][c]);
+            }
+          }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if ((fmask >> (4 * r + c)) & 1u)
+          D[(row0 + ty * 4 + r) * a.m + col0 + tx * 4 + c] = static_cast<TOUT>(static_cast<double>(acc[r][c]));
+  }
+}
+
 template <typename TIN, int REC, typename TOUT, int FLAG, bool ARGMIN>
 static cudaError_t go_rec(const DistJob& j) {
   RecArgs a{};
@@ -167,6 +266,8 @@ static cudaError_t go_rec(const DistJob& j) {
   }
   const int blocks = num_sms() * 8;
   recompute_kernel<TIN, REC, TOUT, FLAG, ARGMIN><<<blocks, 256, 0, j.stream>>>(a);
+  if constexpr (!ARGMIN && (REC == RC_F32 || REC == RC_F64))
+    recompute_dense_tiled_kernel<TIN, REC, TOUT, FLAG><<<blocks, 256, 0, j.stream>>>(a);
   return cudaGetLastError();
 }
 
