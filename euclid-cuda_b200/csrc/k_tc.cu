@@ -68,6 +68,13 @@ struct TcArgs {
   const float* C;
 };
 
+// a pair's direct distance when the recompute list is full (out of line: the epilogue's
+// registers stay its own; 16-byte loads when the rows allow them)
+template <int REC>
+__device__ __noinline__ float overflow_direct(const float* p, const float* c, int dim) {
+  return static_cast<float>(direct_dist<float, REC>(p, c, dim));
+}
+
 template <int KIND, int SROUND, int FLAG, int MODE, int REC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     dist_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -317,9 +324,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     a.list[pos] = (static_cast<unsigned long long>(i) << 32) | jo;
                   } else if constexpr (ARGMIN) {
                     // list full: recompute in place and fold into the row minimum
-                    const float dd = static_cast<float>(direct_dist_scalar<float, REC>(a.P + i * a.dim,
-                                                                               a.C + static_cast<int64_t>(jo) * a.dim,
-                                                                               a.dim));
+                    const float dd = overflow_direct<REC>(a.P + i * a.dim, a.C + static_cast<int64_t>(jo) * a.dim,
+                                                          a.dim);
                     if (dd < bestv || (dd == bestv && jo < besti)) { bestv = dd; besti = jo; }
                   }
                   ++pos;
