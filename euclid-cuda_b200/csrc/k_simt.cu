@@ -413,10 +413,15 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
   unsigned int flagged = 0;
   for (; ch < nchunk; ch += gridDim.x) {
     __syncthreads();  // the previous chunk is formed (the first time: centers and padding in)
+    if (dim == DIM) {  // no padding: the chunk is a straight copy
 #pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      const int e = threadIdx.x + u * 256;
-      if (e < cvals) ps[(e / dim) * DIM + e % dim] = pre[u];
+      for (int u = 0; u < PER; ++u) ps[threadIdx.x + u * 256] = pre[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int e = threadIdx.x + u * 256;
+        if (e < cvals) ps[(e / dim) * DIM + e % dim] = pre[u];
+      }
     }
     __syncthreads();
     load(ch + gridDim.x);
