@@ -152,6 +152,13 @@ def count_launches(step, torch):
         return None
 
 
+def workload_name(workload, n):
+    """The config's workload string, the same on both arms."""
+    if workload == "c2":
+        return f"c2: distance+argmin n={n} x d=128, k=1024, fp16 GEMM + fp32 recompute, kappa=5"
+    return f"c4: Lloyd n={n} x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1"
+
+
 def run_reference(a):
     """--impl reference: the reference path's CPU implementation (the oracle port; the
     reference itself is CUDA-only) on the host cores, rank 0 only."""
@@ -183,9 +190,10 @@ def run_reference(a):
         unit = "iter/s"
     sample = f"{rows} of {cfg['n']} rows x {cfg['k']} centers x {cfg['d']} dims per step, fp64 distance+argmin"
     line = {"metric": METRIC, "value": val, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": tot / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": tot / a.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
             "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": {"workload": a.workload, **{k: v for k, v in cfg.items() if k != "op"}, "sample_rows": rows},
+            "config": {"workload": workload_name(a.workload, cfg["n"]), **cfg, "sample_rows": rows},
             "cpu_baseline": {"value": val, "unit": unit, "cores": used, "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -359,9 +367,7 @@ def main():
                 "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
                 "dtype": "fp16" if cfg["op"].startswith("fp16") else "bf16", "data": "synthetic",
-                "config": {"workload": f"c2: distance+argmin n={n} x d=128, k=1024, fp16 GEMM + fp32 recompute, "
-                                       "kappa=5" if a.workload == "c2" else
-                           f"c4: Lloyd n={n} x d=64, k=4096, bf16 GEMM + fp32 recompute, kappa=0.1",
+                "config": {"workload": workload_name(a.workload, n),
                            "n_per_rank": n_local, "k": k, "d": d, "op": cfg["op"], "kappa": cfg["kappa"],
                            "l2": "inputs larger than L2 (X fp32 >= 512 MiB per rank)",
                            "parallelism": f"dp{world}", "argmin_mode": a.mode},
