@@ -40,6 +40,8 @@ _SIGS = {
     "euc_workspace_bytes": ([_I, _I64, _I64, _I64], _SZ),
     "euc_argmin_workspace_bytes": ([_I, _I64, _I64, _I64], _SZ),
     "euc_set_kernel_timing": ([_I], None),
+    "euc_set_wait_limit_ns": ([ctypes.c_uint64], None),
+    "euc_test_withhold_arrival": ([], None),
     "euc_last_kernel_ms": ([], ctypes.c_float),
     "euc_last_kernel_name": ([], ctypes.c_char_p),
     "euc_pairwise_single": ([_V, _V, _I64, _I64, _I64, _V, _V, _SZ, _V], _I),

@@ -6,8 +6,10 @@
 // distance entries go through run_distance(): prep (norms, low copies) ->
 // tensor-core or CUDA-core distance kernel -> compacted recompute -> labels.
 #include "engine.h"
+#include "common.cuh"
 #include "../../include/euclid_b200.h"
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -99,6 +101,12 @@ bool device_is_sm100() {
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
   return major == 10;
 }
+
+// ------------------------------------------------------------------ wait limit
+static std::atomic<unsigned long long> g_wait_ns{kWaitLimitNs};
+static std::atomic<int> g_withhold{0};
+unsigned long long wait_limit_ns() { return g_wait_ns.load(); }
+bool take_withhold() { return g_withhold.exchange(0) != 0; }
 
 // ------------------------------------------------------------------ timing
 static bool g_timing = false;
@@ -205,6 +213,10 @@ static float k_float(const OpSpec* s, float kappa, int64_t dim) {
   return 0.f;
 }
 
+// K at or above which the cancellation test flags every pair with norms in the safe
+// range (run_distance, the all-flagged route)
+constexpr float kAllFlaggedK = 2.5f;
+
 struct RunOut {
   int mode = 0;                      // argmin mode: 0 screen, 1 exact epilogue, 2 certified
   void* D = nullptr;                 // D mode
@@ -234,8 +246,9 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     cudaError_t e = launch_direct(s, P, C, n, m, static_cast<int>(dim), o.D, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, s->name);
   }
-  const bool cert = argmin && o.mode == 2;
-  if (cert && !(is_tc(s) && s->flag != FL_NONE && s->in == IN_F32 && (s->rec == RC_F32 || s->rec == RC_F64)))
+  const bool cert_capable = is_tc(s) && s->flag != FL_NONE && s->in == IN_F32 && (s->rec == RC_F32 || s->rec == RC_F64);
+  bool cert = argmin && o.mode == 2;
+  if (cert && !cert_capable)
     return fail(EUC_ERR_UNSUPPORTED,
                 std::string(s->name) + ": no certified argmin (tensor-core operators with an fp32 or fp64 recompute)");
   const Layout L = layout_for(s, n, m, dim, argmin);
@@ -243,6 +256,38 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     return fail(EUC_ERR_WORKSPACE, std::string(s->name) + ": workspace of " + std::to_string(L.total) +
                                        " bytes required, got " + std::to_string(ws_bytes));
   uint8_t* w = static_cast<uint8_t*>(ws);
+  // All-flagged route.  With K >= kAllFlaggedK the cancellation test flags every pair
+  // whose norms lie in a safe range, and the reference's D is then the direct recompute
+  // of every pair: its argmin (first index of the smallest stored value) is exactly what
+  // the certified argmin computes, recomputing only the centers that can win, and the
+  // flagged count is n * m.  Proof of "every pair": with e the low format's unit
+  // roundoff (at most 2^-8), the rounded operands give |s| <= |p~||c~| (1 + d 2^-23)
+  // (1 + e) <= (pp + cc) / 2 (1 + 2 d 2^-23 + 2e + ...) because pp and cc are the rounded
+  // squared norms of the same operands, so d_exp = fl(fl(pp - 2s) + cc) <=
+  // (pp + cc)(2 + 2 d 2^-23 + 2^-7 + 2^-22) < 2.5 (pp + cc) <= fl(K (pp + cc)) for
+  // dim <= 2^20.  The range excludes what this bound does not cover: non-finite values
+  // (NaN rows are never flagged), sums below 2^-13 (the absolute error of subnormal
+  // fp16 S and norms, 2^-25, stays under 2^-12 of pp + cc), and for the operators that
+  // round S or the norms to fp16, sums above 6.0e4 (fp16 overflows at 65520).  The
+  // range test reads P and C once and costs one stream synchronisation; a call that
+  // fails it takes the exact path below.
+  bool all_flagged = false;
+  if (argmin && o.mode != 2 && cert_capable && k_float(s, kappa, dim) >= kAllFlaggedK) {
+    Phase ph("euc:range_check");
+    int* dflag = reinterpret_cast<int*>(w + L.hdr + 40);
+    const bool f16 = s->sround == SR_F16 || s->norm == NM_LOW_F16;
+    const float lo = 0x1p-13f, hi = f16 ? 6.0e4f : 1.0e37f;
+    int bad = 1;
+    cudaError_t e = cudaMemsetAsync(dflag, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = launch_norm_range_check(static_cast<const float*>(P), n, static_cast<int>(dim), lo, hi,
+                                                      dflag, st);
+    if (e == cudaSuccess) e = launch_norm_range_check(static_cast<const float*>(C), m, static_cast<int>(dim), lo, hi,
+                                                      dflag, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, dflag, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "range check");
+    if (bad == 0) all_flagged = cert = true;
+  }
   DistJob j{};
   j.spec = s;
   j.P = P;
@@ -357,13 +402,20 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     if (e == cudaSuccess) e = launch_thin_d(s, P, C, j.cc, n, m, j.dim, j.kf, o.D, j.count, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, s->name);
   }
-  if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
-  if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
-  if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
+  {
+    Phase ph("euc:prep");
+    if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
+    if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
+    if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "prep");
-  e = j.fast_argmin ? launch_tc_fast(j, cert ? 1 : 0) : (is_tc(s) ? launch_tc(j) : launch_simt(j));
+  {
+    Phase ph(j.fast_argmin ? "euc:screen" : "euc:distance");
+    e = j.fast_argmin ? launch_tc_fast(j, cert ? 1 : 0) : (is_tc(s) ? launch_tc(j) : launch_simt(j));
+  }
   if (e != cudaSuccess) return cuda_fail(e, s->name);
   if (cert) {
+    Phase ph("euc:certified");
     // rows the first screen decides; a second screen lists the candidate groups of the
     // others; their direct distances, and the rows evaluated whole
     float* md = static_cast<float*>(o.min_dist);
@@ -382,12 +434,23 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
       e = launch_tc_fast(j, 2);
     }
     if (e == cudaSuccess) e = launch_cert_finish(j, o.labels, o.labels32, md);
+    // all-flagged route: the count is that of the reference's list, every pair
+    if (e == cudaSuccess && all_flagged)
+      e = launch_fill_u64(j.count, 1, static_cast<unsigned long long>(n) * static_cast<unsigned long long>(m), st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "certified rows");
   }
-  if (j.fast_argmin) e = launch_eval_chunks(j);
-  if (e == cudaSuccess) e = launch_recompute(j);
-  if (e == cudaSuccess && j.fast_argmin)
+  if (j.fast_argmin) {
+    Phase ph("euc:eval_chunks");
+    e = launch_eval_chunks(j);
+  }
+  if (e == cudaSuccess) {
+    Phase ph("euc:recompute");
+    e = launch_recompute(j);
+  }
+  if (e == cudaSuccess && j.fast_argmin) {
+    Phase ph("euc:redo_rows");
     e = launch_redo_rows(j, o.labels, o.labels32, static_cast<float*>(o.min_dist));
+  }
   if (e != cudaSuccess) return cuda_fail(e, "recompute");
   if (argmin && !j.fast_argmin) {  // the fast path's redo pass has written the outputs
     if (j.row_key) {
@@ -461,6 +524,10 @@ size_t euc_argmin_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim) {
 }
 
 void euc_set_kernel_timing(int enable) { g_timing = enable != 0; }
+
+void euc_set_wait_limit_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kWaitLimitNs); }
+
+void euc_test_withhold_arrival(void) { g_withhold.store(1); }
 
 float euc_last_kernel_ms(void) {
   if (!g_ev_recorded) return -1.f;
@@ -670,6 +737,7 @@ int euc_center_stats(const void* X, int x_is_f64, const void* labels, int labels
   if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
   if (ws_bytes < center_ws_bytes(n, dim, k) || !ws)
     return fail(EUC_ERR_WORKSPACE, "center_stats: workspace too small");
+  Phase ph("euc:center_stats");
   cudaError_t e = launch_center_stats(X, x_is_f64 != 0, labels, labels_are_i64 != 0, n, dim, k, stats, ws, ws_bytes,
                                       static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? EUC_OK : cuda_fail(e, "center_stats");
@@ -680,6 +748,7 @@ int euc_center_finalize(const double* stats, int64_t dim, int64_t k, void* cente
   if (dim <= 0 || k <= 0) return fail(EUC_ERR_SHAPE, "bad size");
   if (!stats || !centers) return fail(EUC_ERR_ARG, "null pointer");
   if (empty_policy == 1 && !prev) return fail(EUC_ERR_ARG, "empty_policy 1 needs prev centers");
+  Phase ph("euc:center_finalize");
   cudaError_t e = launch_center_finalize(stats, dim, k, centers, centers_are_f64 != 0, prev, empty_policy,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? EUC_OK : cuda_fail(e, "center_finalize");

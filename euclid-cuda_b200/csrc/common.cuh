@@ -22,7 +22,8 @@ enum DevErr : int {
 };
 
 // A wait that has not completed after this many nanoseconds is treated as a hang:
-// the waiting role records DEV_TIMEOUT_* and the whole CTA winds down.
+// the waiting role records DEV_TIMEOUT_* and the whole CTA winds down.  The kernels
+// take the limit as an argument (euc_set_wait_limit_ns); this is the default.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s; a healthy stage wait takes microseconds
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -64,15 +65,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait on phase `parity`.  Returns false if the wait gave up, either
-// because it exceeded kWaitLimitNs or because another role raised `*abort`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// because it exceeded `limit_ns` or because another role raised `*abort`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      if (globaltimer_ns() - t0 > limit_ns) return false;
     }
   }
 }

@@ -5,10 +5,20 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cuda.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 #include <stddef.h>
 
 namespace euc {
+
+// NVTX range over the host-side enqueue of one phase (a profiler attributes the kernels
+// launched inside it to the phase); without an attached tool a push/pop costs a check.
+struct Phase {
+  explicit Phase(const char* name) { nvtxRangePushA(name); }
+  ~Phase() { nvtxRangePop(); }
+  Phase(const Phase&) = delete;
+  Phase& operator=(const Phase&) = delete;
+};
 
 enum InType { IN_F32 = 0, IN_F16 = 1, IN_BF16 = 2, IN_F64 = 3 };
 // How S = P.C^T is produced.
@@ -188,6 +198,9 @@ cudaError_t launch_keys_to_labels(const unsigned long long* keys, int64_t n, int
 cudaError_t launch_f64_to_labels(const long long* idx, int64_t n, int64_t* labels, int32_t* labels32,
                                  cudaStream_t st);
 cudaError_t launch_fill_u64(unsigned long long* p, int64_t n, unsigned long long v, cudaStream_t st);
+// *flag |= 1 if some row's fp32 sum of squares is not finite or outside [lo, hi] (k_prep.cu)
+cudaError_t launch_norm_range_check(const float* X, int64_t rows, int dim, float lo, float hi, int* flag,
+                                    cudaStream_t st);
 
 // Center statistics (k x (dim+1) fp64 rows: sums then count).
 size_t center_ws_bytes(int64_t n, int64_t dim, int64_t k);
@@ -201,6 +214,11 @@ cudaError_t launch_center_finalize(const double* stats, int64_t dim, int64_t k, 
 size_t seed_ws_bytes(int64_t n);
 cudaError_t launch_kmeanspp(const void* X, bool x_f64, int64_t n, int64_t dim, int64_t k, uint64_t seed,
                             int64_t* idx, void* centers, void* ws, cudaStream_t st);
+
+// Bound of the pipeline waits of the tensor-core kernels (api.cu, euc_set_wait_limit_ns),
+// and the one-shot failure injection of euc_test_withhold_arrival: true once per arming.
+unsigned long long wait_limit_ns();
+bool take_withhold();
 
 // Kernel timing hook (api.cu).
 void timing_begin(cudaStream_t st, const char* name);

@@ -301,6 +301,35 @@ cudaError_t launch_prep(const DistJob& j, bool points, bool make_low) {
   return cudaErrorNotSupported;
 }
 
+// ------------------------------------------------ norm range check
+// Sets *flag to 1 if some row's fp32 sum of squares is not finite or lies outside
+// [lo, hi] (a NaN sum fails the test too).  One warp per row, grid-stride; the lanes
+// read consecutive values, so a warp's loads of a row are coalesced.  Used to decide,
+// before any distance is formed, whether the cancellation test provably flags every
+// pair (api.cu, the all-flagged route).
+__global__ void __launch_bounds__(256) norm_range_kernel(const float* __restrict__ X, int64_t rows, int dim,
+                                                         float lo, float hi, int* flag) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * 8;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); r < rows; r += warps) {
+    const float* x = X + r * dim;
+    float acc = 0.f;
+    for (int k = lane; k < dim; k += 32) acc = __fmaf_rn(__ldg(x + k), __ldg(x + k), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0 && !(acc >= lo && acc <= hi)) atomicOr(flag, 1);
+  }
+}
+
+cudaError_t launch_norm_range_check(const float* X, int64_t rows, int dim, float lo, float hi, int* flag,
+                                    cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const int64_t want = (rows + 7) / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms()) * 8));
+  norm_range_kernel<<<blocks, 256, 0, st>>>(X, rows, dim, lo, hi, flag);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------ fast argmin: sorted centers
 // Stable rank sort of the centers by norm (ties kept in index order, NaN as +inf):
 // rank_j = #{i : key_i < key_j or (key_i == key_j and i < j)}.  One warp per center,

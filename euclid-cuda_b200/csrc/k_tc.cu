@@ -66,6 +66,7 @@ struct TcArgs {
   int64_t tiles_j;
   const float* P;  // fp32 originals (inline recompute when the list is full)
   const float* C;
+  unsigned long long wait_ns;  // bound of every wait of the pipeline
 };
 
 // a pair's direct distance when the recompute list is full (out of line: the epilogue's
@@ -145,7 +146,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         if (a_res) {
           // the whole 128-row A tile once per row tile, into its own buffer
-          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           mbar_arrive_expect_tx(&afull[abuf], a_bytes);
           uint8_t* sA = smem + abuf * a_bytes;
           for (int kb = 0; kb < a.kblocks; ++kb)
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int ct = 0; ct < a.n_ct && ok; ++ct) {
           for (int kb = 0; kb < a.kblocks; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
             uint8_t* st = stage_base + stage * stage_bytes;
             mbar_arrive_expect_tx(&full[stage], stage_bytes);
             if (a_res) {
@@ -192,15 +193,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
         if (a_res) {
-          if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&afull[abuf], ause, abort_flag, a.wait_ns)) { ok = false; break; }
         }
         for (int ct = 0; ct < a.n_ct && ok; ++ct) {
           const uint32_t buf = acc_i & 1u, use = (acc_i >> 1) & 1u;
-          if (!mbar_wait(&acce[buf], use ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&acce[buf], use ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + buf * static_cast<uint32_t>(bn);
           for (int kb = 0; kb < a.kblocks; ++kb) {
-            if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&full[stage], phase, abort_flag, a.wait_ns)) { ok = false; break; }
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
             const uint32_t sA = a_res ? sAres + kb * TC_A_BYTES : st;
@@ -285,7 +286,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           prefetch(rt, ct + 1);
         else
           prefetch(rt + gridDim.x, 0);
-        if (!mbar_wait(&accf[buf], use, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&accf[buf], use, abort_flag, a.wait_ns)) { ok = false; break; }
         tc_fence_after();
 
         // one 32-column chunk: the reference's form and flag per pair
@@ -401,13 +402,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // merge the two column halves of each row: upper half publishes, lower half combines
         const uint32_t par = rt_i & 1u;
         if (half == 1) {
-          if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag)) { ok = false; break; }
+          if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           mv[128 + row_local] = bestv;
           mi[128 + row_local] = besti;
           __syncwarp();
           if (lane == 0) mbar_arrive(mfull);
         } else {
-          if (!mbar_wait(mfull, par, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(mfull, par, abort_flag, a.wait_ns)) { ok = false; break; }
           const float ov = mv[128 + row_local];
           const uint32_t oi = mi[128 + row_local];
           __syncwarp();
@@ -549,6 +550,7 @@ cudaError_t launch_tc(const DistJob& j) {
   a.tiles_j = j.tiles_j;
   a.P = static_cast<const float*>(j.P);
   a.C = static_cast<const float*>(j.C);
+  a.wait_ns = wait_limit_ns();
 
   CUtensorMap ta, tb;
   if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TC_BM, kind == 2, kind == 1)) return cudaErrorInvalidValue;

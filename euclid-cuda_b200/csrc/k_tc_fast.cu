@@ -99,6 +99,9 @@ struct TfArgs {
   const float* cert_thr;         // certified, second screen: per row, the largest screened distance of a
                                  // center that can win (-inf: the row is decided)
   const uint8_t* tile_on;        // null, or per row tile: whether it is screened
+  unsigned long long wait_ns;    // bound of every wait of the pipeline
+  int withhold;                  // failure injection: CTA 0's first epilogue warp keeps its first
+                                 // accumulator (its MMA warp's wait then runs out)
 };
 
 // The CTA's next row tile at or after rt (same stride as the persistent loop), skipping
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const int row0 = static_cast<int>(rt * TF_BM);
         if (!FUSED && a_res) {
-          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           mbar_arrive_expect_tx(&afull[abuf], a_bytes);
           uint8_t* sA = smem + abuf * a_bytes;
           for (int kb = 0; kb < KB; ++kb)
@@ -254,14 +257,14 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         }
         for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
           const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
-          if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&metae[slot], su ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           uint8_t* ms = meta + slot * TF_META_BYTES;
           mbar_arrive_expect_tx(&metaf[slot], TF_META_BYTES);
           bulk_load_1d(ms, a.ccs + static_cast<int64_t>(ct) * TF_BN, TF_BN * 4, &metaf[slot]);
           m_issued |= 1u << slot;
           m_last = (m_last & ~(1u << slot)) | (su << slot);
           for (int kb = 0; kb < KB; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
             uint8_t* st = stage_base + stage * stage_bytes;
             const bool last_kb = kb == KB - 1;
             mbar_arrive_expect_tx(&full[stage], last_kb ? stage_bytes : ab_bytes);
@@ -302,13 +305,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
         const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux + abuf * TF_AAUX_BYTES));
         // the row tile's extra-K rows (and its resident A)
-        if (!mbar_wait(&afull[abuf], ause, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&afull[abuf], ause, abort_flag, a.wait_ns)) { ok = false; break; }
         for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
           const uint32_t b = t & 1u, use = (t >> 1) & 1u;
-          if (!mbar_wait(&acce[b], use ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&acce[b], use ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           tc_fence_after();
           for (int kb = 0; kb < KB; ++kb) {
-            if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&full[stage], phase, abort_flag, a.wait_ns)) { ok = false; break; }
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
             const uint32_t sA = a_res ? sAres + kb * TF_A_KB : st;
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const int64_t i = rt * TF_BM + row_local;
       // the row's norm and Br from the row warps (Br NaN: past n, or redone whole)
       const uint32_t abuf = rt_i & 1u;
-      if (!mbar_wait(&afull[abuf], (rt_i >> 1) & 1u, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&afull[abuf], (rt_i >> 1) & 1u, abort_flag, a.wait_ns)) { ok = false; break; }
       const float pp = rowbuf[abuf * 2 * TF_BM + row_local];
       const float br = rowbuf[abuf * 2 * TF_BM + TF_BM + row_local];
       __syncwarp();
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         ++uses;
         const uint32_t slot = t & (TF_SLOTS - 1), su = (t / TF_SLOTS) & 1u;
         const int64_t jt = static_cast<int64_t>(ct) * TF_BN + hc * 128;  // first (sorted) column of this warp
-        if (!mbar_wait(&metaf[slot], su, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&metaf[slot], su, abort_flag, a.wait_ns)) { ok = false; break; }
         const float* mcc = reinterpret_cast<const float*>(meta + slot * TF_META_BYTES) + hc * 128;
         const int64_t remt = a.m - jt;
         const int nvt = remt <= 0 ? 0 : (remt >= 128 ? 128 : static_cast<int>(remt));
@@ -427,7 +430,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (force) a.redo[i] = 1;  // the certified pass evaluates this row whole
         }
         const int nch = (nvt + 31) >> 5;
-        if (!mbar_wait(&accf[b], use, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&accf[b], use, abort_flag, a.wait_ns)) { ok = false; break; }
         tc_fence_after();
 
         uint32_t cmask = 0;  // this lane's candidate chunks of the tile
@@ -550,7 +553,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&acce[b]);
+          if (!(a.withhold && blockIdx.x == 0 && ew == 0 && t == 0)) mbar_arrive(&acce[b]);
           mbar_arrive(&metae[slot]);
         }
       }
@@ -586,13 +589,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       // merge the four (parity, column half) partial minima of each row
       const uint32_t par = rt_i & 1u;
       if (g != 0) {
-        if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag)) { ok = false; break; }
+        if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
         mv[(g - 1) * TF_BM + row_local] = bestv;
         mi[(g - 1) * TF_BM + row_local] = besti;
         __syncwarp();
         if (lane == 0) mbar_arrive(mfull);
       } else {
-        if (!mbar_wait(mfull, par, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(mfull, par, abort_flag, a.wait_ns)) { ok = false; break; }
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
           const float ov = mv[p * TF_BM + row_local];
@@ -639,13 +642,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
       // the MMAs of the buffer's previous row tile are done, and the epilogue has read
       // its pp and Br
-      if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag) || !mbar_wait(&pempty[abuf], ause ^ 1u, abort_flag)) {
+      if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns) || !mbar_wait(&pempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) {
         ok = false;
         break;
       }
       float acc0 = 0.f, acc1 = 0.f;
       if constexpr (FUSED) {
-        if (!mbar_wait(xfull, rt_i & 1u, abort_flag)) {
+        if (!mbar_wait(xfull, rt_i & 1u, abort_flag, a.wait_ns)) {
           ok = false;
           break;
         }
@@ -669,7 +672,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         // the CTA's next row tile into the staging buffer, once every row thread is done
         const int64_t nrt = tf_next_tile(a, rt + gridDim.x);
         if (c == 0 && nrt < a.n_rt) {
-          if (!mbar_wait(xempty, rt_i & 1u, abort_flag)) {
+          if (!mbar_wait(xempty, rt_i & 1u, abort_flag, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -753,6 +756,11 @@ static size_t tf_xstage_bytes(int dim) { return static_cast<size_t>((dim + 31) /
 // (A B) stages; FUSED needs resident A.
 static void tf_pipeline(int kblocks, size_t xbytes, int* nst, int* a_res) {
   const size_t abytes = static_cast<size_t>(kblocks) * TF_A_KB;
+  if (TF_FIXED + xbytes > TF_SMEM_LIMIT) {  // the staging buffer alone does not fit (FUSED at large dim)
+    *a_res = 0;
+    *nst = 0;
+    return;
+  }
   const size_t avail = TF_SMEM_LIMIT - TF_FIXED - xbytes;
   const size_t bst = TF_B_KB + TF_STAGE_EXTRA;
   const size_t min_st = xbytes ? 2 : 3;
@@ -847,6 +855,8 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   a.redo = j.redo;
   a.cert_key = j.cert_key;
   a.cert_d2 = j.cert_d2;
+  a.wait_ns = wait_limit_ns();
+  a.withhold = (cert_pass == 0 && take_withhold()) ? 1 : 0;
   const int grid = j.regions;
   if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
   // A: the low-precision copy, or with FUSED the fp32 points in 32-value x 128-row boxes

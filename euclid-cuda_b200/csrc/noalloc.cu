@@ -2,23 +2,30 @@
 //
 // euc_argmin_noalloc runs exactly the kernels of euc_argmin, but instead of a
 // caller-owned workspace it uses one file-scope __device__ array of NOALLOC_SCRATCH_BYTES
-// (one instance per device).  Nothing here calls cudaMalloc, cudaFree or any
+// (one instance per device and context).  Nothing here calls cudaMalloc, cudaFree or any
 // allocating routine.
 //
-// Set-up: the first call on each device (with that device current) takes the array's
-// address with cudaGetSymbolAddress, which also loads this module onto the device,
-// and caches it.  That first call should come before any stream capture.
+// Set-up: this file's module holds no kernel, only the array, so it is loaded into a
+// context the first time the array's address is taken there: lazily (CUDA's default
+// module loading) on the first call on each device, with that device current, or at
+// context creation under CUDA_MODULE_LOADING=EAGER.  From then on the array holds its
+// 32 MiB of that device's memory until the context ends, in every process that loads
+// it.  The first call on a device should come before any stream capture.
+//
+// Every call takes the array's address in the current context with
+// cudaGetSymbolAddress (a host-side lookup that allocates nothing), so the address
+// follows the context: a cudaDeviceReset, or a caller's own driver-API context, gets
+// its own array rather than a stale address.
 //
 // What must start at zero: the flag counter inside the scratch; euc_argmin clears it
-// with cudaMemsetAsync on `stream` at the start of every call.  Every other scratch
-// word is written before it is read within the call, so the scratch needs no zeroing
-// at set-up.
+// with cudaMemsetAsync on `stream` at the start of every call (and clears the certified
+// mode's counters and switches the same way).  Every other scratch word is written
+// before it is read within the call, so the scratch needs no zeroing at set-up.
 //
-// All calls on one device share the one scratch: calls that overlap in time (on
+// All calls in one context share the one scratch: calls that overlap in time (on
 // different streams, or from different host threads without ordering) race on it.
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <string>
 
 #include "../../include/euclid_b200.h"
@@ -27,28 +34,16 @@
 namespace euc {
 
 constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(32) << 20;
-constexpr int NOALLOC_MAX_DEVICES = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
-static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[NOALLOC_MAX_DEVICES];
-
-// address of this device's scratch array, taken once per device
+// address of the scratch array in the current context
 static int noalloc_scratch(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(EUC_ERR_DEVICE, cudaGetErrorString(e));
-  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return set_error(EUC_ERR_DEVICE, "device ordinal out of range");
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return set_error(EUC_ERR_LAUNCH, (std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e)).c_str());
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return set_error(EUC_ERR_LAUNCH, (std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e)).c_str());
+  *out = p;
   return EUC_OK;
 }
 
@@ -61,6 +56,13 @@ size_t euc_argmin_noalloc_max_bytes(void) { return euc::NOALLOC_SCRATCH_BYTES; }
 int euc_argmin_noalloc(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa,
                        int exact, int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count,
                        void* stream) {
+  // the argument checks euc_argmin makes, before the size test and the array's address
+  // (a negative size must not read as a huge workspace, a wrong device must not try to
+  // load the module)
+  if (!euc::find_op(op)) return euc::set_error(EUC_ERR_ARG, "unknown operator id");
+  if (n < 0 || m < 0 || dim < 0) return euc::set_error(EUC_ERR_SHAPE, "negative size");
+  if (!euc::device_is_sm100())
+    return euc::set_error(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
   const size_t need = euc_argmin_workspace_bytes(op, n, m, dim);
   if (need > euc::NOALLOC_SCRATCH_BYTES)
     return euc::set_error(EUC_ERR_WORKSPACE,

@@ -23,6 +23,22 @@ import _ops
 from _lib import check, lib, ptr, stream_of, workspace
 
 EMPTY_POLICY = {"zero": 0, "keep": 1}
+
+
+class _phase:
+    """NVTX range around one phase of an iteration (a no-op without CUDA)."""
+
+    def __init__(self, name):
+        self.name = name
+        self.on = torch.cuda.is_available()
+
+    def __enter__(self):
+        if self.on:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if self.on:
+            torch.cuda.nvtx.range_pop()
 # labels: the screen (exact wherever the top-two gap exceeds its resolution), the exact
 # epilogue, or the certified first index of the smallest direct distance
 ASSIGN_MODE = {"fast": False, "exact": True, "certified": "certified"}
@@ -72,12 +88,17 @@ class LloydKMeans:
 
     def step(self, X, C):
         """One iteration on the local shard X; returns (new centers, labels int32,
-        flagged-pair count of this shard as a 0-d device tensor)."""
-        labels, cnt = self.assign(X, C)
-        stats = self.center_stats(X, labels)
+        flagged-pair count of this shard as a 0-d device tensor).  Each phase is an NVTX
+        range (lloyd:assign, lloyd:center_stats, lloyd:all_reduce, lloyd:finalize)."""
+        with _phase("lloyd:assign"):
+            labels, cnt = self.assign(X, C)
+        with _phase("lloyd:center_stats"):
+            stats = self.center_stats(X, labels)
         if self._world() > 1:
-            dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=self.group)
-        return self.finalize(stats, C), labels, cnt
+            with _phase("lloyd:all_reduce"):
+                dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=self.group)
+        with _phase("lloyd:finalize"):
+            return self.finalize(stats, C), labels, cnt
 
     def fit(self, X, C0, n_iter):
         C = C0.contiguous()

@@ -56,6 +56,20 @@ EUC_API const char* euc_last_error(void);
  * EUC_OK otherwise. */
 EUC_API int euc_device_check(void);
 
+/* No counterpart in the reference (it bounds no device wait).  Bound, in nanoseconds,
+ * of every pipeline wait of the tensor-core kernels launched after this call (default
+ * 2e9; 0 restores it).  A wait that runs out makes the kernel record the error, stop
+ * its pipeline, let its copies and MMAs in flight land, free its tensor memory and
+ * return; euc_device_check() then reports EUC_ERR_TIMEOUT and the context stays
+ * usable.  Process-wide. */
+EUC_API void euc_set_wait_limit_ns(uint64_t ns);
+/* No counterpart in the reference.  Failure injection for tests, made on the host: the
+ * next launch of the screening kernel (euc_argmin's default mode) runs with one
+ * arrival withheld (its first CTA's first epilogue warp keeps its first accumulator),
+ * so that CTA's MMA warp waits until the wait limit and the launch ends as above.
+ * One-shot; the outputs of that call are not meaningful. */
+EUC_API void euc_test_withhold_arrival(void);
+
 /* Operator identifiers, used by euc_workspace_bytes() and the generic entries. */
 typedef enum {
   /* euclidean_cuda.cpp:26-32 */
@@ -252,11 +266,18 @@ EUC_API int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t 
 /* No counterpart in the reference.  euc_argmin without a workspace, for callers that
  * cannot allocate device memory (a host binding with no device allocator, or a
  * process whose memory pool already holds the device's memory): the scratch is one
- * static device array of euc_argmin_noalloc_max_bytes() (32 MiB) per device; nothing
- * is allocated.  A shape whose euc_argmin_workspace_bytes() exceeds that is rejected
- * with EUC_ERR_WORKSPACE.  The first call on each device takes the array's address
- * (with that device current) and should come before any stream capture.  Calls that
- * overlap in time on one device race on the shared scratch. */
+ * static device array of euc_argmin_noalloc_max_bytes() (32 MiB) per device and
+ * context; nothing is allocated.  The array takes its device memory when its module
+ * loads into a context: on the first call on that device under CUDA's default lazy
+ * loading, at context creation under CUDA_MODULE_LOADING=EAGER (then in every process
+ * that loads this library, whether or not it calls this entry); it holds it until the
+ * context ends.  The first call on each device should come before any stream capture.
+ * Every call takes the array's address in the current context, so it follows a reset
+ * or a caller's own context.  Arguments are checked first (unknown op EUC_ERR_ARG,
+ * negative sizes EUC_ERR_SHAPE, no sm_100 device EUC_ERR_DEVICE); a shape whose
+ * euc_argmin_workspace_bytes() exceeds the array is rejected with EUC_ERR_WORKSPACE
+ * before any launch.  Calls that overlap in time in one context race on the shared
+ * scratch. */
 EUC_API size_t euc_argmin_noalloc_max_bytes(void);
 EUC_API int euc_argmin_noalloc(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
                        float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,

@@ -317,6 +317,64 @@ int orc_dist_argmin_f64(const double* P, const double* C, int64_t n, int64_t m, 
   return used;
 }
 
+/* ----------------------------------------------------------- CPU baseline
+ * One Lloyd iteration in fp64 on the host cores: the distance + argmin above for every
+ * row, each thread adding its rows into a private k x (d+1) table (sums, count), then
+ * the tables added in thread order and the means formed (an empty cluster gets 0, as
+ * update_centers_* gives it, center_kernels.cu:52,116).  ms[0] receives the time of
+ * the per-row part, ms[1] that of the reduction and means, whose cost does not grow
+ * with n.  Returns the number of threads used. */
+int orc_lloyd_step_f64(const double* X, const double* C, int64_t n, int64_t k, int64_t d, int64_t* labels,
+                       double* newC, int threads, double* ms) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+  const int nt = omp_get_max_threads();
+  const double t0 = omp_get_wtime();
+#else
+  const int nt = 1;
+#endif
+  const int64_t w = d + 1;
+  double* part = (double*)calloc((size_t)nt * (size_t)(k * w), sizeof(double));
+  double* mind = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
+  const int used = orc_dist_argmin_f64(X, C, n, k, d, labels, mind, nt);
+#pragma omp parallel num_threads(nt)
+  {
+#ifdef _OPENMP
+    double* t = part + (size_t)omp_get_thread_num() * (size_t)(k * w);
+#else
+    double* t = part;
+#endif
+#pragma omp for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+      double* row = t + labels[i] * w;
+      for (int64_t j = 0; j < d; ++j) row[j] += X[i * d + j];
+      row[d] += 1.0;
+    }
+  }
+#ifdef _OPENMP
+  const double t1 = omp_get_wtime();
+#endif
+  for (int64_t c = 0; c < k; ++c) {
+    for (int64_t j = 0; j < w; ++j) {
+      double s = 0.0;
+      for (int q = 0; q < nt; ++q) s += part[(size_t)q * (size_t)(k * w) + c * w + j];
+      part[c * w + j] = s;
+    }
+    const double cnt = part[c * w + d];
+    for (int64_t j = 0; j < d; ++j) newC[c * d + j] = cnt > 0.0 ? part[c * w + j] / cnt : 0.0;
+  }
+#ifdef _OPENMP
+  const double t2 = omp_get_wtime();
+  ms[0] = (t1 - t0) * 1e3;
+  ms[1] = (t2 - t1) * 1e3;
+#else
+  ms[0] = ms[1] = 0.0;
+#endif
+  free(part);
+  free(mind);
+  return used;
+}
+
 int orc_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

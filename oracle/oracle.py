@@ -45,6 +45,8 @@ def lib():
         L.orc_center_stats.argtypes = [P, I, P, I64, I64, I64, P]
         L.orc_dist_argmin_f64.argtypes = [P, P, I64, I64, I64, P, P, I]
         L.orc_dist_argmin_f64.restype = I
+        L.orc_lloyd_step_f64.argtypes = [P, P, I64, I64, I64, P, P, I, P]
+        L.orc_lloyd_step_f64.restype = I
         L.orc_max_threads.restype = I
         _LIB = L
     return _LIB
@@ -445,6 +447,18 @@ def dist_argmin_f64(P, C, threads=0):
     md = np.empty(P.shape[0], np.float64)
     used = lib().orc_dist_argmin_f64(_p(P), _p(C), P.shape[0], C.shape[0], P.shape[1], _p(lab), _p(md), threads)
     return lab, md, used
+
+
+def lloyd_step_f64(X, C, threads=0):
+    """One fp64 Lloyd iteration on the host cores (CPU baseline): returns (new centers,
+    labels, threads used, ms of the per-row part, ms of the reduction and means)."""
+    X, C = _c(X, np.float64), _c(C, np.float64)
+    lab = np.empty(X.shape[0], np.int64)
+    out = np.empty_like(C)
+    ms = np.zeros(2, np.float64)
+    used = lib().orc_lloyd_step_f64(_p(X), _p(C), X.shape[0], C.shape[0], X.shape[1], _p(lab), _p(out), threads,
+                                    _p(ms))
+    return out, lab, used, float(ms[0]), float(ms[1])
 
 
 def max_threads():

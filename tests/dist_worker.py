@@ -1,7 +1,10 @@
 """One rank of the data-parallel Lloyd loop on CPU tensors over gloo (test helper).
 
 Run by tests/test_dist_gloo.py as `python tests/dist_worker.py OUT.npy` with RANK,
-WORLD_SIZE, MASTER_ADDR and MASTER_PORT in the environment.  The host logic under test
+WORLD_SIZE, MASTER_ADDR and MASTER_PORT in the environment.  With LEAVE_AFTER=s the last
+rank exits after step s (between steps: nothing of it is in flight); every other rank
+must then see its next step raise within the process group's timeout (PG_TIMEOUT
+seconds) instead of waiting for good: it writes the error to OUT.npy.err and exits 3.  The host logic under test
 is kmeans.LloydKMeans.step and kmeans.shard_rows (sharding, the one all-reduce of the
 k x (d+1) statistics, identical finalisation on every rank); the per-rank compute is
 the oracle's (assignment by fp64 distance, fp64 center statistics), standing in for
@@ -57,15 +60,25 @@ def main():
     n, d, k, iters = 3001, 8, 7, 4
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    leave_after = int(os.environ.get("LEAVE_AFTER", "0"))
     if world > 1:
-        dist.init_process_group("gloo", timeout=timedelta(seconds=60))
+        dist.init_process_group("gloo", timeout=timedelta(seconds=float(os.environ.get("PG_TIMEOUT", "60"))))
     X, C0 = data(n, d, k, seed=12)
     lo, hi = kmeans.shard_rows(n, rank, world)
     km = HostLloyd(k, op="double", empty="keep")
     C = torch.from_numpy(C0)
     Xl = torch.from_numpy(X[lo:hi].copy())
-    for _ in range(iters):
-        C, _, _ = km.step(Xl, C)
+    for step in range(iters):
+        if leave_after and rank == world - 1 and step == leave_after:
+            os._exit(0)  # this rank leaves between steps
+        try:
+            C, _, _ = km.step(Xl, C)
+        except Exception as e:  # a peer is gone: the collective ended with an error
+            if not leave_after:
+                raise
+            with open(out + ".err", "w") as f:
+                f.write(f"step {step}: {type(e).__name__}: {e}")
+            os._exit(3)
     np.save(out, C.numpy())
     if world > 1:
         dist.barrier()

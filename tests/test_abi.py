@@ -110,3 +110,25 @@ def test_kmeanspp_entry_checks_shapes_before_the_device(lib):
         pytest.skip("GPU present")
     assert lib.euc_kmeanspp(ctypes.c_void_p(16), 0, n, 8, 10, 1, ctypes.c_void_p(16), None, ctypes.c_void_p(16),
                             1 << 20, None) == 8  # EUC_ERR_DEVICE
+
+
+def test_noalloc_entry_checks_arguments_before_the_scratch(lib):
+    """euc_argmin_noalloc checks its arguments before the scratch-size test and before it
+    takes the array's address: an unknown operator is EUC_ERR_ARG, a negative size
+    EUC_ERR_SHAPE (not a wrapped, huge workspace), and without an sm_100 device a valid
+    call is EUC_ERR_DEVICE (no module load is attempted)."""
+    import torch
+    f = lib.euc_argmin_noalloc
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                  ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                  ctypes.c_void_p]
+    lib.euc_last_error.restype = ctypes.c_char_p
+    assert f(999, None, None, 10, 10, 4, 5.0, 0, None, None, None, None, None) == 7  # EUC_ERR_ARG
+    for n, m, d in ((-1, 10, 4), (10, -3, 4), (10, 10, -2)):
+        assert f(15, None, None, n, m, d, 5.0, 0, None, None, None, None, None) == 1  # EUC_ERR_SHAPE
+        assert b"negative" in lib.euc_last_error()
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    assert f(15, None, None, 10, 10, 4, 5.0, 0, None, None, None, None, None) == 8  # EUC_ERR_DEVICE
+    assert b"sm_100" in lib.euc_last_error()

@@ -24,5 +24,5 @@ def test_reference_arm_line(workload, unit):
     assert line["e2e"] == {"value": line["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     sys.path.insert(0, REPO)
     import bench
-    assert line["config"]["workload"] == bench.workload_name(workload, line["config"]["n"])
+    assert line["config"] == bench.workload_config(workload, line["config"]["n"], 1)
     assert line["metric"] == bench.METRIC

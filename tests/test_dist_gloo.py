@@ -5,6 +5,7 @@ import os
 import socket
 import subprocess
 import sys
+import time
 
 import numpy as np
 import pytest
@@ -21,13 +22,13 @@ def free_port():
     return port
 
 
-def run_ranks(world, tmp_path):
+def run_ranks(world, tmp_path, **extra_env):
     port = free_port()
     procs, outs = [], []
     for r in range(world):
         out = str(tmp_path / f"c_{world}_{r}.npy")
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
-                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES="")
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES="", **extra_env)
         procs.append(subprocess.Popen([sys.executable, WORKER, out], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT))
         outs.append(out)
@@ -47,6 +48,31 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
     two = run_ranks(2, tmp_path)
     np.testing.assert_array_equal(two[0], two[1])
     np.testing.assert_array_equal(two[0], single)
+
+
+def test_rank_leaving_between_steps_ends_the_others_next_step(tmp_path):
+    """Failure detection of the data-parallel loop, made on the host: rank 1 exits after
+    its first Lloyd step.  Rank 0's next step (its all-reduce) must end with an error
+    within the process group's timeout (10 s here), not wait for good."""
+    port = free_port()
+    procs, t0 = [], time.monotonic()
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES="", LEAVE_AFTER="1", PG_TIMEOUT="10")
+        procs.append(subprocess.Popen([sys.executable, WORKER, str(tmp_path / f"leave_{r}.npy")], env=env,
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
+    try:
+        logs = [p.communicate(timeout=120)[0].decode() for p in procs]
+    except subprocess.TimeoutExpired:
+        for q in procs:
+            q.kill()
+        pytest.fail("the surviving rank waited for good")
+    elapsed = time.monotonic() - t0
+    assert procs[1].returncode == 0, logs[1][-2000:]
+    assert procs[0].returncode == 3, logs[0][-2000:]
+    err = (tmp_path / "leave_0.npy.err").read_text()
+    assert err.startswith("step 1:"), err
+    assert elapsed < 60, elapsed
 
 
 def test_shard_rows_cover_every_row_once():

@@ -164,3 +164,69 @@ def test_certified_oracle_rejects_half_arithmetic_recompute():
     P = np.ones((2, 3), np.float32)
     with pytest.raises(ValueError):
         O.certified_argmin("fp16_fp16", P, P)
+
+
+def _kappa_for(K, dim, u):
+    # the smallest float kappa whose K = kappa * ((2 dim + 4) u) (the reference's float
+    # expression) reaches K
+    kappa = np.float32(K / ((2 * dim + 4) * u))
+    while O._k_float(0, kappa, dim, u) < np.float32(K):
+        kappa = np.nextafter(kappa, np.float32(np.inf))
+    return kappa
+
+
+ALL_FLAGGED_OPS = [("mix", n) for n in ("fp16_fp64", "fp16_fp32", "bf16_fp64", "bf16_fp32", "tf32_fp64")] + \
+                  [("tiled", n) for n in ("fp16_fp64", "fp16_fp32", "bf16_fp64", "bf16_fp32")]
+
+
+def _adversarial(rng, dim, lo, hi):
+    """Rows whose fp32 norms span [lo, hi] (log-uniform, ends included) and centers that
+    are the rows negated and rescaled (anti-aligned pairs: the most negative s, so the
+    largest distance relative to pp + cc), plus Gaussian rows."""
+    n = 96
+    P = rng.normal(size=(n, dim))
+    P /= np.linalg.norm(P, axis=1, keepdims=True)
+    tgt = np.exp(rng.uniform(np.log(lo), np.log(hi), n))
+    tgt[:4] = [lo, lo, hi, hi]
+    P *= np.sqrt(tgt)[:, None] * (1 + 2.0 ** -20)
+    C = -P[rng.permutation(n)[:48]] * rng.uniform(0.5, 1.0, (48, 1))
+    C = np.concatenate([C, -P[:8], rng.normal(size=(8, dim))])
+    P = P.astype(np.float32)
+    C = C.astype(np.float32)
+    norms = np.concatenate([O.norms_f32(P, "sumsq"), O.norms_f32(C, "sumsq")])
+    keep = (norms >= lo) & (norms <= hi)  # what the engine's range check lets through
+    return P[keep[:len(P)]], C[keep[len(P):]]
+
+
+@pytest.mark.parametrize("kind,name", ALL_FLAGGED_OPS)
+@pytest.mark.parametrize("dim", [3, 64, 1024])
+def test_all_flagged_route_flags_every_pair(kind, name, dim):
+    """The engine's all-flagged route (fused argmin with K >= 2.5 and every norm in
+    [2^-13, hi], hi = 6.0e4 where S or the norms are rounded to fp16) replaces the
+    exact epilogue by the certified argmin and reports n * m flagged pairs.  That needs
+    the reference's cancellation test to flag every such pair, anti-aligned pairs at the
+    ends of the range included."""
+    rng = np.random.default_rng(dim)
+    f16 = name.startswith("fp16")
+    lo, hi = 2.0 ** -13, (6.0e4 if f16 else 1.0e30)
+    P, C = _adversarial(rng, dim, lo, hi)
+    if kind == "mix":
+        _, _, _, u, _, _ = O.MIX[name]
+        D, flag, cnt = O.mix(name, P, C, kappa=_kappa_for(2.5, dim, u))
+    else:
+        _, u, _ = O.TILED[name]
+        D, flag, cnt, _ = O.tiled(name, P, C, _kappa_for(2.5, dim, u))
+    assert flag.all() and cnt == P.shape[0] * C.shape[0]
+    lab, md = O.certified_argmin(("" if kind == "mix" else "tiled_") + name, P, C)
+    np.testing.assert_array_equal(lab, O.argmin_first(D))
+    np.testing.assert_array_equal(md, D[np.arange(P.shape[0]), lab])
+
+
+def test_all_flagged_route_needs_its_threshold():
+    # below the route's K an anti-aligned pair (s < 0) escapes the test: d_exp is about
+    # 2 (pp + cc) there, so K = 1.9 leaves it unflagged
+    rng = np.random.default_rng(0)
+    P = rng.normal(size=(16, 32)).astype(np.float32)
+    _, _, _, u, _, _ = O.MIX["bf16_fp32"]
+    _, flag, _ = O.mix("bf16_fp32", P, -P, kappa=_kappa_for(1.9, 32, u))
+    assert not flag[np.arange(16), np.arange(16)].any()

@@ -16,9 +16,9 @@ from _lib import lib
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 EUC_ERR_WORKSPACE = 6
-# (op id, exact): fp16 tensor-core mix op (fast screen and exact epilogue), the bf16
-# one, and the fp32 CUDA-core mix op
-CASES = [(15, 0), (15, 1), (17, 0), (18, 1)]
+# (op id, exact): fp16 tensor-core mix op (fast screen, exact epilogue, certified
+# labels), the bf16 one (fast, certified), and the fp32 CUDA-core mix op
+CASES = [(15, 0), (15, 1), (15, 2), (17, 0), (17, 2), (18, 1)]
 
 
 def _inputs(n, m, d, seed):
@@ -80,3 +80,38 @@ def test_noalloc_rejects_oversized_shape():
     assert b"static scratch" in L.euc_last_error()
     torch.cuda.synchronize()
     assert (lab == -7).all()  # nothing launched
+
+
+def _with_workspace(L, op, P, C, exact, kappa, stream):
+    """euc_argmin on a freshly allocated workspace filled with junk bytes."""
+    n, d = P.shape
+    m = C.shape[0]
+    ws_bytes = L.euc_argmin_workspace_bytes(op, n, m, d)
+    ws = torch.full((ws_bytes,), 0xAB, dtype=torch.uint8, device=DEV)
+    out = _outs(n)
+    lab, lab32, md, cnt = out
+    rc = L.euc_argmin(op, _p(P), _p(C), n, m, d, kappa, exact, _p(lab), _p(lab32), _p(md), _p(cnt), _p(ws),
+                      ws_bytes, stream)
+    assert rc == 0, L.euc_last_error()
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("op,exact", [(15, 0), (15, 2)])
+def test_noalloc_after_larger_and_smaller_calls(op, exact):
+    """A call after a larger one (whose leftovers fill the scratch) and after a smaller one
+    gives the same outputs as euc_argmin on a fresh workspace: nothing of an earlier
+    call's scratch leaks into a later result."""
+    L = lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    shapes = [(40000, 700, 96), (1000, 40, 16), (40000, 700, 96), (777, 300, 64)]
+    for i, (n, m, d) in enumerate(shapes):
+        assert L.euc_argmin_workspace_bytes(op, n, m, d) <= L.euc_argmin_noalloc_max_bytes()
+        P, C = _inputs(n, m, d, seed=100 + i)
+        ref = _with_workspace(L, op, P, C, exact, 5.0, stream)
+        got = _outs(n)
+        rc = L.euc_argmin_noalloc(op, _p(P), _p(C), n, m, d, 5.0, exact, *(_p(t) for t in got), stream)
+        assert rc == 0, L.euc_last_error()
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b), (i, n, m, d)
