@@ -353,7 +353,7 @@ def main():
                 "argmin_mode": a.mode, "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"),
                 "clocks": head["clocks"], "gpu_launches": head["gpu_launches"],
                 "launches_per_step": head["launches_per_step"]}
-        for key in ("phases_ms", "flagged_last_step"):
+        for key in ("phases_ms", "per_rank", "flagged_last_step"):
             if key in head:
                 line[key] = head[key]
         line.update(extras)
@@ -431,10 +431,11 @@ def bench_lloyd(ctx):
     for _ in range(a.warmup):
         step()
     ctx["barrier"]()
-    launches_per_step = count_launches(step, torch)
-    ctx["barrier"]()
     ms, clk = _time_steps(step, a.steps, st, dev.index, torch)
     ctx["barrier"]()
+    launches_per_step = count_launches(step, torch)  # after the timed region
+    ctx["barrier"]()
+    ms_own = ms
     ms = ctx["max_over_ranks"](ms)
     ms_step = ms / a.steps
     phases = lloyd_phases(km, X, state["C"], st, torch)
@@ -453,11 +454,19 @@ def bench_lloyd(ctx):
     roof = _screen_roofline(L, launch, 2.0 * n_local * k * d, ctx["tc_peak"], ctx["peak_src"], "lloyd", n_local,
                             min(a.steps, 20))
     del ws, labels
+    # what each rank saw: its own timed step, its phases, its screening kernel and clock
+    mine = {"rank": rank, "ms_per_step": ms_own / a.steps, "phases_ms": phases, "screen_ms": roof["kernel_ms"],
+            "sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons")}
+    per_rank = [mine]
+    if world > 1:
+        import torch.distributed as dist
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
     e2e = None if a.no_e2e else lloyd_e2e(ctx, km, X, C0)
     return {"value": 1e3 / ms_step, "unit": "iter/s", "ms_per_step": ms_step, "n_local": n_local, "roofline": roof,
             "e2e": e2e, "clocks": clk,
             "gpu_launches": None if launches_per_step is None else launches_per_step * a.steps,
-            "launches_per_step": launches_per_step, "phases_ms": phases,
+            "launches_per_step": launches_per_step, "phases_ms": phases, "per_rank": per_rank,
             "flagged_last_step": int(state["cnt"].item())}
 
 
@@ -560,10 +569,10 @@ def bench_c2(ctx, weak):
     for _ in range(a.warmup):
         step()
     barrier()
-    launches_per_step = count_launches(step, torch)
     steps = a.steps if weak else max(a.steps, 50)
     ms, clk = _time_steps(step, steps, st, dev.index, torch)
     barrier()
+    launches_per_step = count_launches(step, torch)  # after the timed region
     ms_step = mor(ms) / steps
     flop = 2.0 * n * k * d
     out = {"value": flop * world / (ms_step / 1e3) / 1e9, "unit": "GFLOP/s", "ms_per_step": ms_step, "n_local": n,

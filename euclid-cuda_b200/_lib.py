@@ -42,6 +42,7 @@ _SIGS = {
     "euc_set_kernel_timing": ([_I], None),
     "euc_set_wait_limit_ns": ([ctypes.c_uint64], None),
     "euc_test_withhold_arrival": ([], None),
+    "euc_set_screen_pairs": ([_I], None),
     "euc_last_kernel_ms": ([], ctypes.c_float),
     "euc_last_kernel_name": ([], ctypes.c_char_p),
     "euc_pairwise_single": ([_V, _V, _I64, _I64, _I64, _V, _V, _SZ, _V], _I),

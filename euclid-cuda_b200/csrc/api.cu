@@ -322,7 +322,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.chunk_list = L.clist ? reinterpret_cast<unsigned long long*>(w + L.clist) : nullptr;
   j.chunk_s = L.cs ? reinterpret_cast<float*>(w + L.cs) : nullptr;
   j.chunk_cap = L.ccap;
-  j.regions = j.fast_argmin ? tc_fast_regions(n) : 0;
+  j.regions = j.fast_argmin ? tc_fast_job_regions(j) : 0;
   j.b_aux_sorted = L.baux ? w + L.baux : nullptr;
   j.aux_e = reinterpret_cast<int*>(w + L.hdr + 16);
   j.ccmax = reinterpret_cast<float*>(w + L.hdr + 20);

@@ -171,7 +171,11 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass = 0);
 cudaError_t launch_eval_chunks(const DistJob& j);
 // ... and writes every row's outputs from its key (labels, labels32, mind nullable)
 cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels32, float* mind);
-int tc_fast_regions(int64_t n);  // CTAs (= list regions) of the screening kernel
+// CTAs (= list regions) of the screening kernel; the fast argmin's screen (not the
+// certified passes) runs on CTA pairs where the device can hold them
+int tc_fast_regions(int64_t n, bool cert, int kblocks);
+bool tc_fast_pairs(bool cert, int kblocks);
+int tc_fast_job_regions(const DistJob& j);  // the above for a prepared job (spec, n, ldlow, cert)
 bool tc_make_tmap(CUtensorMap* map, const void* base, int64_t rows, int ld, int esize, int box_rows, bool is_f32,
                   bool is_bf16);
 bool tc_make_tmap_sw32(CUtensorMap* map, const void* base, int64_t rows, int esize, int box_rows, bool is_f32,

@@ -40,11 +40,13 @@
 // copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
 #include "engine.h"
+#include "../../include/euclid_b200.h"
 #include "direct.cuh"
 #include "aux.cuh"
 
 #include <cudaTypedefs.h>
 #include <algorithm>
+#include <atomic>
 
 namespace euc {
 
@@ -154,19 +156,30 @@ __device__ __forceinline__ float convert_box(const uint8_t* box, int r, uint8_t*
   return acc;
 }
 
-template <int KIND, bool FUSED, int CERT>
+// PAIR: the CTAs run in pairs (clusters of 2) with M = 256 MMAs across both SMs.  CTA
+// rank r owns row tile 2 p + r of pair tile p and loads centers [128 r, 128 r + 128) of
+// every 256-center tile, so each SM streams half of each center tile; rank 0 issues the
+// MMAs and commits to both CTAs' barriers, and the barriers that collect both CTAs'
+// events (stage full, A ready, accumulator read) are rank 0's.
+template <int KIND, bool FUSED, int CERT, bool PAIR>
 __global__ void __launch_bounds__(TF_THREADS, 1)
     dist_tc_fast_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmBaux, const TfArgs a) {
+  static_assert(!PAIR || CERT == 0, "the certified passes run unpaired");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = a.nst;
   const bool a_res = a.a_res != 0;
   const int KB = a.kblocks;
+  constexpr int BNL = PAIR ? TF_BN / 2 : TF_BN;        // center rows this CTA loads per tile
+  constexpr uint32_t B_KB_L = BNL * 128;               // its part of one K block of B
+  constexpr uint32_t BAUX_L = BNL * 32;                // its part of the tile's extra-K rows
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
   const uint32_t a_bytes = static_cast<uint32_t>(KB) * TF_A_KB;                   // all K blocks of A
   // a stage: B  |  A B, then room for the tile's extra-K rows (used by its last K block)
-  const uint32_t ab_bytes = a_res ? TF_B_KB : static_cast<uint32_t>(TF_A_KB + TF_B_KB);
-  const uint32_t stage_bytes = ab_bytes + TF_BAUX_BYTES;
+  const uint32_t ab_bytes = a_res ? B_KB_L : static_cast<uint32_t>(TF_A_KB + B_KB_L);
+  const uint32_t stage_bytes = ab_bytes + BAUX_L;
   uint8_t* stage_base = smem + (a_res ? 2 * a_bytes : 0);
   uint8_t* meta = stage_base + NST * stage_bytes;  // TF_SLOTS x 256 sorted norms
   const int nbox = (a.dim + 31) >> 5;              // FUSED: staged 32-value boxes per row
@@ -201,8 +214,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    // afull: the row warps' arrivals, plus the producer's A copy when A comes by TMA
-    const uint32_t afull_count = TF_ROW_THREADS + ((!FUSED && a_res) ? 1u : 0u);
+    // afull: the row warps' arrivals (rank 0's also the other CTA's), plus the producer's
+    // A copy when A comes by TMA (rank 0's producer expects both CTAs' bytes)
+    const uint32_t afull_count = (PAIR && leader ? 2u : 1u) * TF_ROW_THREADS + ((!FUSED && a_res && leader) ? 1u : 0u);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&afull[s], afull_count);
       mbar_init(&aempty[s], 1);
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         mbar_init(xempty, TF_ROW_THREADS);
       }
       mbar_init(&accf[s], 1);
-      mbar_init(&acce[s], TF_EPI_WARPS / 2);
+      mbar_init(&acce[s], (PAIR ? 2 : 1) * TF_EPI_WARPS / 2);
     }
     for (int s = 0; s < TF_SLOTS; ++s) {
       mbar_init(&metaf[s], 1);
@@ -225,7 +239,12 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == TF_W_MMA) tmem_alloc(tmem_slot, kCols);
+  if (warp == TF_W_MMA) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, kCols);
+    else
+      tmem_alloc(tmem_slot, kCols);
+  }
   if (warp == TF_W_PRODUCER && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -233,7 +252,12 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers are initialised before any remote use
   tc_fence_after();
+  // rank 0's copies of the barriers that collect both CTAs' events
+  const uint32_t full_c0 = PAIR ? cluster_addr(full, 0) : 0u;
+  const uint32_t afull_c0 = PAIR ? cluster_addr(afull, 0) : 0u;
+  const uint32_t acce_c0 = PAIR ? cluster_addr(acce, 0) : 0u;
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == TF_W_PRODUCER) {
@@ -247,11 +271,21 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const int row0 = static_cast<int>(rt * TF_BM);
         if (!FUSED && a_res) {
-          if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
-          mbar_arrive_expect_tx(&afull[abuf], a_bytes);
+          if (!(PAIR ? mbar_wait_cluster(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)
+                     : mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns))) {
+            ok = false;
+            break;
+          }
           uint8_t* sA = smem + abuf * a_bytes;
-          for (int kb = 0; kb < KB; ++kb)
-            tma_load_2d(sA + kb * TF_A_KB, &tmA, &afull[abuf], kb * kelems, row0);
+          if constexpr (PAIR) {
+            if (leader) mbar_arrive_expect_tx(&afull[abuf], 2 * a_bytes);
+            for (int kb = 0; kb < KB; ++kb)
+              tma_load_2d_pair(sA + kb * TF_A_KB, &tmA, afull_c0 + 8u * abuf, kb * kelems, row0);
+          } else {
+            mbar_arrive_expect_tx(&afull[abuf], a_bytes);
+            for (int kb = 0; kb < KB; ++kb)
+              tma_load_2d(sA + kb * TF_A_KB, &tmA, &afull[abuf], kb * kelems, row0);
+          }
           a_issued |= 1u << abuf;
           a_last = (a_last & ~(1u << abuf)) | (ause << abuf);
         }
@@ -264,17 +298,35 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           m_issued |= 1u << slot;
           m_last = (m_last & ~(1u << slot)) | (su << slot);
           for (int kb = 0; kb < KB; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
+            if (!(PAIR ? mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, a.wait_ns)
+                       : mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.wait_ns))) {
+              ok = false;
+              break;
+            }
             uint8_t* st = stage_base + stage * stage_bytes;
             const bool last_kb = kb == KB - 1;
-            mbar_arrive_expect_tx(&full[stage], last_kb ? stage_bytes : ab_bytes);
-            if (a_res) {
-              tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+            if constexpr (PAIR) {
+              // this CTA's half of the center tile, completing on rank 0's stage barrier
+              const uint32_t fb = full_c0 + 8u * stage;
+              const int yb = ct * TF_BN + static_cast<int>(rank) * BNL;
+              if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (last_kb ? stage_bytes : ab_bytes));
+              if (a_res) {
+                tma_load_2d_pair(st, &tmB, fb, kb * kelems, yb);
+              } else {
+                tma_load_2d_pair(st, &tmA, fb, kb * kelems, row0);
+                tma_load_2d_pair(st + TF_A_KB, &tmB, fb, kb * kelems, yb);
+              }
+              if (last_kb) tma_load_2d_pair(st + ab_bytes, &tmBaux, fb, 0, yb);
             } else {
-              tma_load_2d(st, &tmA, &full[stage], kb * kelems, row0);
-              tma_load_2d(st + TF_A_KB, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+              mbar_arrive_expect_tx(&full[stage], last_kb ? stage_bytes : ab_bytes);
+              if (a_res) {
+                tma_load_2d(st, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+              } else {
+                tma_load_2d(st, &tmA, &full[stage], kb * kelems, row0);
+                tma_load_2d(st + TF_A_KB, &tmB, &full[stage], kb * kelems, ct * TF_BN);
+              }
+              if (last_kb) tma_load_2d(st + ab_bytes, &tmBaux, &full[stage], 0, ct * TF_BN);
             }
-            if (last_kb) tma_load_2d(st + ab_bytes, &tmBaux, &full[stage], 0, ct * TF_BN);
             issued_mask |= 1u << stage;
             last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
@@ -286,32 +338,36 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         atomicExch(&s_tf_err, DEV_TIMEOUT_PRODUCER);
       }
       volatile int no_abort = 0;
-      for (int s = 0; s < NST; ++s)
-        if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_phase >> s) & 1u, &no_abort);
-      for (int s = 0; s < 2; ++s)
-        if (a_issued & (1u << s)) mbar_wait(&afull[s], (a_last >> s) & 1u, &no_abort);
+      // copies in flight land before the CTA exits (rank 1's copies complete on rank 0's
+      // barriers, which rank 0 drains before the closing cluster barrier)
+      if (!PAIR || leader) {
+        for (int s = 0; s < NST; ++s)
+          if (issued_mask & (1u << s)) mbar_wait_cluster(&full[s], (last_phase >> s) & 1u, &no_abort);
+        for (int s = 0; s < 2; ++s)
+          if (a_issued & (1u << s)) mbar_wait_cluster(&afull[s], (a_last >> s) & 1u, &no_abort);
+      }
       for (int s = 0; s < TF_SLOTS; ++s)
         if (m_issued & (1u << s)) mbar_wait(&metaf[s], (m_last >> s) & 1u, &no_abort);
     }
   } else if (warp == TF_W_MMA) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       constexpr uint32_t fmt = (KIND == 0) ? 0u : (KIND == 1 ? 1u : 2u);
-      constexpr uint32_t idesc = umma_idesc(fmt, 128, TF_BN);
+      constexpr uint32_t idesc = umma_idesc(fmt, PAIR ? 256 : 128, TF_BN);
       uint32_t stage = 0, phase = 0, t = 0, rt_i = 0;
       bool ok = true;
       for (int64_t rt = tf_next_tile(a, blockIdx.x); rt < a.n_rt && ok; rt = tf_next_tile(a, rt + gridDim.x), ++rt_i) {
         const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
         const uint32_t sAres = smem_u32(smem + abuf * a_bytes);
         const uint64_t aux_ad = sw32_kmajor_desc(smem_u32(aaux + abuf * TF_AAUX_BYTES));
-        // the row tile's extra-K rows (and its resident A)
-        if (!mbar_wait(&afull[abuf], ause, abort_flag, a.wait_ns)) { ok = false; break; }
+        // the row tile's extra-K rows (and its resident A), in both CTAs with PAIR
+        if (!mbar_wait_cluster(&afull[abuf], ause, abort_flag, a.wait_ns)) { ok = false; break; }
         for (int ct = 0; ct < a.n_ct && ok; ++ct, ++t) {
           const uint32_t b = t & 1u, use = (t >> 1) & 1u;
-          if (!mbar_wait(&acce[b], use ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
+          if (!mbar_wait_cluster(&acce[b], use ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
           tc_fence_after();
           for (int kb = 0; kb < KB; ++kb) {
-            if (!mbar_wait(&full[stage], phase, abort_flag, a.wait_ns)) { ok = false; break; }
+            if (!mbar_wait_cluster(&full[stage], phase, abort_flag, a.wait_ns)) { ok = false; break; }
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * stage_bytes);
             const uint32_t sA = a_res ? sAres + kb * TF_A_KB : st;
@@ -321,34 +377,50 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
               const uint64_t bd = sw128_kmajor_desc(sB + kk * 32);
-              if constexpr (KIND == 2)
-                umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-              else
-                umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+              if constexpr (KIND == 2) {
+                if constexpr (PAIR) umma_tf32_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+                else umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+              } else {
+                if constexpr (PAIR) umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+                else umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+              }
             }
             if (kb == KB - 1) {
               // the extra K block: adds (cc_j + Br_i) / 2 to the accumulator of pair (i, j)
               const uint64_t bd = sw32_kmajor_desc(st + ab_bytes);
-              if constexpr (KIND == 2)
-                umma_tf32(d_tmem, aux_ad, bd, idesc, 1u);
-              else
-                umma_f16(d_tmem, aux_ad, bd, idesc, 1u);
+              if constexpr (KIND == 2) {
+                if constexpr (PAIR) umma_tf32_pair(d_tmem, aux_ad, bd, idesc, 1u);
+                else umma_tf32(d_tmem, aux_ad, bd, idesc, 1u);
+              } else {
+                if constexpr (PAIR) umma_f16_pair(d_tmem, aux_ad, bd, idesc, 1u);
+                else umma_f16(d_tmem, aux_ad, bd, idesc, 1u);
+              }
             }
-            umma_commit(&empty[stage]);
+            if constexpr (PAIR) umma_commit_pair(&empty[stage]);
+            else umma_commit(&empty[stage]);
             if (++stage == static_cast<uint32_t>(NST)) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          umma_commit(&accf[b]);
+          if constexpr (PAIR) umma_commit_pair(&accf[b]);
+          else umma_commit(&accf[b]);
         }
-        if (ok) umma_commit(&aempty[abuf]);
+        if (ok) {
+          if constexpr (PAIR) umma_commit_pair(&aempty[abuf]);
+          else umma_commit(&aempty[abuf]);
+        }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(&s_tf_err, DEV_TIMEOUT_MMA);
       }
-      umma_commit(drain);
+      if constexpr (PAIR) umma_commit_pair(drain);
+      else umma_commit(drain);
+    }
+    if (lane == 0) {
+      // every MMA of the CTA (with PAIR: of the pair) has completed
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort);
+      if (PAIR) mbar_wait_cluster(drain, 0, &no_abort);
+      else mbar_wait(drain, 0, &no_abort);
     }
   } else if (warp >= TF_W_EPI0 && warp < TF_W_EPI0 + TF_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
@@ -430,7 +502,11 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
           if (force) a.redo[i] = 1;  // the certified pass evaluates this row whole
         }
         const int nch = (nvt + 31) >> 5;
-        if (!mbar_wait(&accf[b], use, abort_flag, a.wait_ns)) { ok = false; break; }
+        if (!(PAIR ? mbar_wait_cluster(&accf[b], use, abort_flag, a.wait_ns)
+                   : mbar_wait(&accf[b], use, abort_flag, a.wait_ns))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 
         uint32_t cmask = 0;  // this lane's candidate chunks of the tile
@@ -553,7 +629,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (!(a.withhold && blockIdx.x == 0 && ew == 0 && t == 0)) mbar_arrive(&acce[b]);
+          if (!(a.withhold && blockIdx.x == 0 && ew == 0 && t == 0)) {
+            if constexpr (PAIR) mbar_arrive_cluster(acce_c0 + 8u * b);  // rank 0's MMA waits for both CTAs
+            else mbar_arrive(&acce[b]);
+          }
           mbar_arrive(&metae[slot]);
         }
       }
@@ -642,7 +721,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       const uint32_t abuf = rt_i & 1u, ause = (rt_i >> 1) & 1u;
       // the MMAs of the buffer's previous row tile are done, and the epilogue has read
       // its pp and Br
-      if (!mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns) || !mbar_wait(&pempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) {
+      if (!(PAIR ? mbar_wait_cluster(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)
+                 : mbar_wait(&aempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) ||
+          !mbar_wait(&pempty[abuf], ause ^ 1u, abort_flag, a.wait_ns)) {
         ok = false;
         break;
       }
@@ -719,6 +800,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       }
       fence_async_shared();  // the MMA reads A and the extra-K rows through the async proxy
       mbar_arrive(&afull[abuf]);
+      if (PAIR && !leader) mbar_arrive_cluster(afull_c0 + 8u * abuf);  // for rank 0's MMA
     }
     if (!ok) {
       *abort_flag = 1;
@@ -733,12 +815,20 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // PAIR: neither CTA leaves while the other may still read its shared memory (MMA
+  // operands) or arrive on its barriers
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   if (threadIdx.x == 0) {
     const unsigned long long c = *lcount;
     a.region_cnt[blockIdx.x] = static_cast<uint32_t>(c < a.region_cap ? c : a.region_cap);
   }
-  if (warp == TF_W_MMA) tmem_dealloc(tmem_base, kCols);
+  if (warp == TF_W_MMA) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, kCols);
+    else
+      tmem_dealloc(tmem_base, kCols);
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -751,10 +841,13 @@ constexpr size_t TF_STAGE_EXTRA = TF_BAUX_BYTES;  // a stage's room for the tile
 // FUSED staging: the row tile's fp32 points, 32 values of each row per box
 static size_t tf_xstage_bytes(int dim) { return static_cast<size_t>((dim + 31) / 32) * TF_XBOX_BYTES; }
 
+// one stage's B part (and the tile's extra-K rows): with CTA pairs each CTA holds half
+static size_t tf_bstage_bytes(bool pair) { return (TF_B_KB + TF_STAGE_EXTRA) / (pair ? 2 : 1); }
+
 // Resident A (the row tile, double-buffered) with B-only stages when that leaves room
 // for 3 stages (2 when the staging buffer of FUSED takes its share), else streaming
 // (A B) stages; FUSED needs resident A.
-static void tf_pipeline(int kblocks, size_t xbytes, int* nst, int* a_res) {
+static void tf_pipeline(int kblocks, size_t xbytes, bool pair, int* nst, int* a_res) {
   const size_t abytes = static_cast<size_t>(kblocks) * TF_A_KB;
   if (TF_FIXED + xbytes > TF_SMEM_LIMIT) {  // the staging buffer alone does not fit (FUSED at large dim)
     *a_res = 0;
@@ -762,7 +855,7 @@ static void tf_pipeline(int kblocks, size_t xbytes, int* nst, int* a_res) {
     return;
   }
   const size_t avail = TF_SMEM_LIMIT - TF_FIXED - xbytes;
-  const size_t bst = TF_B_KB + TF_STAGE_EXTRA;
+  const size_t bst = tf_bstage_bytes(pair);
   const size_t min_st = xbytes ? 2 : 3;
   if (2 * abytes + min_st * bst <= avail) {
     *a_res = 1;
@@ -772,30 +865,94 @@ static void tf_pipeline(int kblocks, size_t xbytes, int* nst, int* a_res) {
     *nst = xbytes ? 0 : static_cast<int>(std::min<size_t>(8, avail / (TF_A_KB + bst)));
   }
 }
-static size_t tf_smem_bytes(int kblocks, int nst, int a_res, size_t xbytes) {
-  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TF_A_KB + nst * (TF_B_KB + TF_STAGE_EXTRA)
-                            : nst * (TF_A_KB + TF_B_KB + TF_STAGE_EXTRA);
+static size_t tf_smem_bytes(int kblocks, int nst, int a_res, size_t xbytes, bool pair) {
+  const size_t body = a_res ? 2 * static_cast<size_t>(kblocks) * TF_A_KB + nst * tf_bstage_bytes(pair)
+                            : nst * (TF_A_KB + tf_bstage_bytes(pair));
   return TF_FIXED + xbytes + body;
 }
 
-int tc_fast_regions(int64_t n) {
+// CTA pairs for the screen of the fast argmin: process-wide switch (euc_set_screen_pairs)
+// and, per device, how many pairs of this kernel's size can be resident at once.
+static std::atomic<int> g_pairs_on{1};
+static int g_pair_slots[64];
+static int tf_pair_slots() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (g_pair_slots[dev] == 0) {
+    auto kern = dist_tc_fast_kernel<0, true, 0, true>;
+    int clusters = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(TF_SMEM_LIMIT)) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * 1024);
+      cfg.blockDim = dim3(TF_THREADS);
+      cfg.dynamicSmemBytes = TF_SMEM_LIMIT;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) clusters = 0;
+    }
+    cudaGetLastError();  // a failed query leaves no error behind
+    g_pair_slots[dev] = clusters > 0 ? clusters : -1;
+  }
+  return g_pair_slots[dev] > 0 ? g_pair_slots[dev] : 0;
+}
+
+// Pairs halve each SM's share of the center tiles streamed from L2, but make one MMA
+// issuer wait for both CTAs' epilogues.  Measured on one B200: at 16 K blocks per tile
+// (d = 1024, fp16) the screen runs 6 % faster paired; at 1 or 2 K blocks (d = 64, 128),
+// where the epilogue sets the pace, 18-26 % slower.  So only tiles of 8 or more K blocks
+// (d >= 512 for 16-bit operands) pair.
+constexpr int TF_PAIR_MIN_KBLOCKS = 8;
+
+bool tc_fast_pairs(bool cert, int kblocks) {
+  return !cert && kblocks >= TF_PAIR_MIN_KBLOCKS && g_pairs_on.load() != 0 && tf_pair_slots() > 0;
+}
+
+int tc_fast_regions(int64_t n, bool cert, int kblocks) {
+  if (tc_fast_pairs(cert, kblocks)) {
+    const int64_t n_pt = (n + 2 * TF_BM - 1) / (2 * TF_BM);
+    const int64_t clusters = std::min<int64_t>(tf_pair_slots(), std::max<int64_t>(n_pt, 1));
+    return static_cast<int>(2 * clusters);
+  }
   const int64_t n_rt = (n + TF_BM - 1) / TF_BM;
   int grid = num_sms();
   if (static_cast<int64_t>(grid) > n_rt) grid = static_cast<int>(n_rt);
   return grid < 1 ? 1 : grid;
 }
 
-template <int KIND, bool FUSED, int CERT>
+template <int KIND, bool FUSED, int CERT, bool PAIR>
 static cudaError_t launch_tf_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tba,
                                const TfArgs& args, int grid, cudaStream_t st) {
-  auto kern = dist_tc_fast_kernel<KIND, FUSED, CERT>;
-  const size_t smem = tf_smem_bytes(args.kblocks, args.nst, args.a_res, FUSED ? tf_xstage_bytes(args.dim) : 0);
+  auto kern = dist_tc_fast_kernel<KIND, FUSED, CERT, PAIR>;
+  const size_t smem =
+      tf_smem_bytes(args.kblocks, args.nst, args.a_res, FUSED ? tf_xstage_bytes(args.dim) : 0, PAIR);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   // the kernel timing hook times the screen over all rows (not the certified second screen)
   if (CERT != 2) timing_begin(st, "dist_tc_fast_kernel");
-  kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, tba, args);
-  e = cudaGetLastError();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(TF_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tba, args);
+  } else {
+    kern<<<grid, TF_THREADS, smem, st>>>(ta, tb, tba, args);
+    e = cudaGetLastError();
+  }
   if (CERT != 2) timing_end(st);
   return e;
 }
@@ -807,6 +964,8 @@ static int tf_kblocks(const DistJob& j) {
   return static_cast<int>((static_cast<int64_t>(j.ldlow) * esize) / 128);
 }
 
+int tc_fast_job_regions(const DistJob& j) { return tc_fast_regions(j.n, j.cert, tf_kblocks(j)); }
+
 // The row warps read the fp32 points themselves when the operator's norm is that of
 // the fp16 / bf16 rounded values, the rows are whole 16-byte vectors, and A stays
 // resident in shared memory.
@@ -816,7 +975,7 @@ bool tc_fast_can_fuse_rows(const DistJob& j) {
   if (!recipe || s->in != IN_F32) return false;
   if (j.dim % 4 != 0 || (reinterpret_cast<uintptr_t>(j.P) & 15u) != 0) return false;
   int nst = 0, a_res = 0;
-  tf_pipeline(tf_kblocks(j), tf_xstage_bytes(j.dim), &nst, &a_res);
+  tf_pipeline(tf_kblocks(j), tf_xstage_bytes(j.dim), false, &nst, &a_res);  // unpaired stages are the larger
   return a_res != 0 && nst >= 2;
 }
 
@@ -830,8 +989,10 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   a.m = j.m;
   a.kblocks = tf_kblocks(j);
   a.n_ct = static_cast<int>((j.m + TF_BN - 1) / TF_BN);
-  a.n_rt = (j.n + TF_BM - 1) / TF_BM;
-  tf_pipeline(a.kblocks, j.fused_rows ? tf_xstage_bytes(j.dim) : 0, &a.nst, &a.a_res);
+  // the fast argmin's screen runs on CTA pairs (row tiles counted in whole pairs)
+  const bool pair = cert_pass == 0 && tc_fast_pairs(j.cert, a.kblocks);
+  a.n_rt = pair ? 2 * ((j.n + 2 * TF_BM - 1) / (2 * TF_BM)) : (j.n + TF_BM - 1) / TF_BM;
+  tf_pipeline(a.kblocks, j.fused_rows ? tf_xstage_bytes(j.dim) : 0, pair, &a.nst, &a.a_res);
   if (a.nst < 2) return cudaErrorInvalidValue;
   if (j.fused_rows && !tc_fast_can_fuse_rows(j)) return cudaErrorInvalidValue;
   a.pp = static_cast<float*>(j.pp);
@@ -858,7 +1019,8 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   a.wait_ns = wait_limit_ns();
   a.withhold = (cert_pass == 0 && take_withhold()) ? 1 : 0;
   const int grid = j.regions;
-  if (grid != tc_fast_regions(j.n)) return cudaErrorInvalidValue;
+  if (grid != tc_fast_regions(j.n, j.cert, a.kblocks) || (pair && (grid & 1))) return cudaErrorInvalidValue;
+  const int bn_load = pair ? TF_BN / 2 : TF_BN;  // center rows one CTA loads per tile
   // A: the low-precision copy, or with FUSED the fp32 points in 32-value x 128-row boxes
   CUtensorMap ta, tb;
   if (j.fused_rows) {
@@ -866,30 +1028,34 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   } else if (!tc_make_tmap(&ta, j.Plow, j.n, j.ldlow, esize, TF_BM, kind == 2, kind == 1)) {
     return cudaErrorInvalidValue;
   }
-  if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, TF_BN, kind == 2, kind == 1))
+  if (!tc_make_tmap(&tb, j.Clow_sorted, j.m, j.ldlow, esize, bn_load, kind == 2, kind == 1))
     return cudaErrorInvalidValue;
   CUtensorMap tba;
   const int64_t mpad = (j.m + TF_BN - 1) / TF_BN * TF_BN;
-  if (!tc_make_tmap_sw32(&tba, j.b_aux_sorted, mpad, esize, TF_BN, kind == 2, kind == 1)) return cudaErrorInvalidValue;
-#define TF_LAUNCH(CM_)                                                          \
+  if (!tc_make_tmap_sw32(&tba, j.b_aux_sorted, mpad, esize, bn_load, kind == 2, kind == 1))
+    return cudaErrorInvalidValue;
+#define TF_LAUNCH(CM_, PR_)                                                     \
   if (j.fused_rows) {                                                           \
-    if (kind == 0) return launch_tf_t<0, true, CM_>(ta, tb, tba, a, grid, j.stream); \
-    return launch_tf_t<1, true, CM_>(ta, tb, tba, a, grid, j.stream);           \
+    if (kind == 0) return launch_tf_t<0, true, CM_, PR_>(ta, tb, tba, a, grid, j.stream); \
+    return launch_tf_t<1, true, CM_, PR_>(ta, tb, tba, a, grid, j.stream);      \
   }                                                                             \
-  if (kind == 0) return launch_tf_t<0, false, CM_>(ta, tb, tba, a, grid, j.stream);  \
-  if (kind == 1) return launch_tf_t<1, false, CM_>(ta, tb, tba, a, grid, j.stream);  \
-  return launch_tf_t<2, false, CM_>(ta, tb, tba, a, grid, j.stream);
+  if (kind == 0) return launch_tf_t<0, false, CM_, PR_>(ta, tb, tba, a, grid, j.stream);  \
+  if (kind == 1) return launch_tf_t<1, false, CM_, PR_>(ta, tb, tba, a, grid, j.stream);  \
+  return launch_tf_t<2, false, CM_, PR_>(ta, tb, tba, a, grid, j.stream);
   if (cert_pass == 1) {
     if (!j.cert_key || !j.cert_d2) return cudaErrorInvalidValue;
-    TF_LAUNCH(1)
+    TF_LAUNCH(1, false)
   }
   if (cert_pass == 2) {
     if (!j.cert_thr || !j.cert_tiles) return cudaErrorInvalidValue;
     a.cert_thr = j.cert_thr;
     a.tile_on = j.cert_tiles;
-    TF_LAUNCH(2)
+    TF_LAUNCH(2, false)
   }
-  TF_LAUNCH(0)
+  if (pair) {
+    TF_LAUNCH(0, true)
+  }
+  TF_LAUNCH(0, false)
 #undef TF_LAUNCH
 }
 
@@ -1252,3 +1418,5 @@ cudaError_t launch_redo_rows(const DistJob& j, int64_t* labels, int32_t* labels3
 }
 
 }  // namespace euc
+
+extern "C" void euc_set_screen_pairs(int enable) { euc::g_pairs_on.store(enable != 0 ? 1 : 0); }

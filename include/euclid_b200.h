@@ -69,6 +69,11 @@ EUC_API void euc_set_wait_limit_ns(uint64_t ns);
  * so that CTA's MMA warp waits until the wait limit and the launch ends as above.
  * One-shot; the outputs of that call are not meaningful. */
 EUC_API void euc_test_withhold_arrival(void);
+/* No counterpart in the reference.  Whether the screening kernel of euc_argmin's
+ * default mode runs on pairs of SMs (1, the default: clusters of two CTAs, each SM
+ * streaming half of every 256-center tile into one M = 256 tensor-core MMA) or on
+ * single SMs (0).  Both give the same outputs; process-wide. */
+EUC_API void euc_set_screen_pairs(int enable);
 
 /* Operator identifiers, used by euc_workspace_bytes() and the generic entries. */
 typedef enum {
