@@ -256,6 +256,7 @@ def run_reference(a):
         desc = (f"one fp64 Lloyd iteration (distance + argmin + center update) on {rows} of {cfg['n']} rows per "
                 f"step, per-row time scaled to all rows ({ms / 1e3:.1f} s per full iteration)")
     # ms_per_step is the wall time of one sampled step; `value` is scaled to the workload
+    ref_gpu = reference_gpu(a.workload) if not a.no_reference_gpu else None
     line = {"metric": METRIC, "value": val, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": wall_ms, "higher_is_better": True,
             "scaling": "weak" if a.workload == "c2" else "strong", "vs_baseline": None,
@@ -263,7 +264,73 @@ def run_reference(a):
             "config": workload_config(a.workload, cfg["n"], world), "sample_rows": rows,
             "cpu_baseline": {"value": val, "unit": unit, "cores": used, "kind": "port", "sample": desc},
             "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu(workload):
+    """The reference's own CUDA operators on the same workload (informational; the line's
+    value is the CPU implementation): its extensions as built from its sources into
+    oracle/_ref, one B200.  c2: pairwise_euclidean_fp16_fp32(X, C, 5) + D.argmin(1) (in
+    two row halves: its form kernel's grid.y exceeds 65535 at n = 2^20).  lloyd: one
+    iteration, pairwise_euclidean_bf16_fp32(kappa 0.1) in 2^18-row chunks (N*M < 2^32)
+    + argmin per chunk, then update_centers_fp32 timed on the first 2^20 points and
+    scaled linearly in n (its cost is k * n * d).  None when the extensions are absent."""
+    ref = os.path.join(REPO, "oracle", "_ref")
+    if not os.path.exists(os.path.join(ref, "ref_euclidean_mix.so")):
+        return None
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+        sys.path.insert(0, ref)
+        import ref_center_kernels as rcen
+        import ref_euclidean_mix as rmix
+        dev = torch.device("cuda", 0)
+
+        def timed(fn, iters):
+            fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / iters
+
+        if workload == "c2":
+            g = torch.Generator(device=dev).manual_seed(C2["seed"])
+            X = torch.randn(C2["n"], C2["d"], generator=g, device=dev)
+            C = torch.randn(C2["k"], C2["d"], generator=g, device=dev)
+            half = X.shape[0] // 2
+            ms = timed(lambda: torch.cat([rmix.pairwise_euclidean_fp16_fp32(X[:half], C, 5.0).argmin(1),
+                                          rmix.pairwise_euclidean_fp16_fp32(X[half:], C, 5.0).argmin(1)]), 5)
+            return {"op": "pairwise_euclidean_fp16_fp32 + argmin", "ms_per_step": ms,
+                    "value": 2.0 * C2["n"] * C2["k"] * C2["d"] / (ms / 1e3) / 1e9, "unit": "GFLOP/s"}
+        n, d, k = LLOYD["n"], LLOYD["d"], LLOYD["k"]
+        g = torch.Generator(device=dev).manual_seed(LLOYD["seed"])
+        true_c = torch.rand(k, d, generator=g, device=dev) * 10 - 5
+        X = true_c[torch.randint(0, k, (n,), generator=g, device=dev)] + 0.5 * torch.randn(n, d, generator=g,
+                                                                                           device=dev)
+        del true_c
+        C = X[torch.randperm(n, generator=g, device=dev)[:k]].contiguous()
+        chunk = 1 << 18
+        labels = torch.empty(n, dtype=torch.int64, device=dev)
+
+        def dist():
+            for r0 in range(0, n, chunk):
+                labels[r0:r0 + chunk] = rmix.pairwise_euclidean_bf16_fp32(X[r0:r0 + chunk], C, LLOYD["kappa"]).argmin(1)
+        ms_d = timed(dist, 1)
+        sub = 1 << 20
+        Xs, ls = X[:sub].contiguous(), labels[:sub].contiguous()
+        ms_c = timed(lambda: rcen.update_centers_fp32(Xs, ls, k), 1) * (n / sub)
+        return {"op": "pairwise_euclidean_bf16_fp32 chunks + argmin + update_centers_fp32",
+                "ms_distance": ms_d, "ms_centers_scaled": ms_c, "ms_per_step": ms_d + ms_c,
+                "value": 1e3 / (ms_d + ms_c), "unit": "iter/s", "centers_timed_rows": sub}
+    except Exception as e:  # informational only: never fail the arm
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 # ------------------------------------------------------------------ our arm
@@ -279,6 +346,8 @@ def main():
     ap.add_argument("--mode", default="fast", choices=["fast", "exact", "certified"],
                     help="argmin mode of euc_argmin (the headline line uses the default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="reference arm: skip the reference's own CUDA operators (the reference_gpu key)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end legs (profiling runs)")
     ap.add_argument("--no-extras", action="store_true", help="skip the c2 and configs keys of the N = 1 line")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

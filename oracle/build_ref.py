@@ -19,7 +19,10 @@ ref_euclidean_uniform  euclidean_cuda_uniform.cpp, euclidean_kernels_uniform.cu
 ref_euclidean_advanced euclidean_cuda_advanced.cpp, euclidean_kernels_advanced.cu
 ref_center_kernels     center_kernels.cu (its PYBIND11_MODULE is in the .cu, center_kernels.cu:252)
 
-Usage:  python oracle/build_ref.py [--src /root/reference] [--only NAME ...]
+Usage:  python oracle/build_ref.py [--src DIR] [--only NAME ...]
+
+The sources are read from --src, else $EUCLID_REFERENCE_SRC, else the reference checkout
+beside this repository (../reference); without them the recipe skips itself.
 """
 import argparse
 import os
@@ -68,7 +71,8 @@ def build_one(name, src_dir, verbose=False):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default="/root/reference")
+    ap.add_argument("--src", default=os.environ.get("EUCLID_REFERENCE_SRC",
+                                                   os.path.join(os.path.dirname(HERE), "..", "reference")))
     ap.add_argument("--only", nargs="*")
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
