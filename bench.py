@@ -422,7 +422,7 @@ def main():
                 "argmin_mode": a.mode, "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"),
                 "clocks": head["clocks"], "gpu_launches": head["gpu_launches"],
                 "launches_per_step": head["launches_per_step"]}
-        for key in ("phases_ms", "per_rank", "flagged_last_step"):
+        for key in ("phases_ms", "per_rank", "store_low", "flagged_last_step"):
             if key in head:
                 line[key] = head[key]
         line.update(extras)
@@ -509,6 +509,22 @@ def bench_lloyd(ctx):
     ms_step = ms / a.steps
     phases = lloyd_phases(km, X, state["C"], st, torch)
 
+    # the same iterations screening from a low-precision copy of the points stored once
+    # (LloydKMeans(store_low=True)): the fp32 points are read only for the recompute and
+    # the center statistics
+    prep = km.prepare(X)
+    state_low = {"C": C0}
+
+    def step_low():
+        state_low["C"], _, _ = km.step(X, state_low["C"], prep)
+    for _ in range(a.warmup):
+        step_low()
+    ctx["barrier"]()
+    ms_low, _ = _time_steps(step_low, a.steps, st, dev.index, torch)
+    ctx["barrier"]()
+    ms_low = ctx["max_over_ranks"](ms_low) / a.steps
+    del prep
+
     # the screening kernel alone (CUDA events around its launch, same stream)
     op_id = OPS[cfg["op"]]
     labels = torch.empty(n_local, dtype=torch.int32, device=dev)
@@ -536,6 +552,8 @@ def bench_lloyd(ctx):
             "e2e": e2e, "clocks": clk,
             "gpu_launches": None if launches_per_step is None else launches_per_step * a.steps,
             "launches_per_step": launches_per_step, "phases_ms": phases, "per_rank": per_rank,
+            "store_low": {"value": 1e3 / ms_low, "unit": "iter/s", "ms_per_step": ms_low,
+                          "note": "X screened from a stored bf16 copy, fp32 read for recompute and centers"},
             "flagged_last_step": int(state["cnt"].item())}
 
 

@@ -55,6 +55,10 @@ _SIGS = {
     "euc_update_centers_fp32": ([_V, _V, _I64, _I64, _I64, _V, _V, _V, _SZ, _V], _I),
     "euc_update_centers_fp64": ([_V, _V, _I64, _I64, _I64, _V, _V, _V, _SZ, _V], _I),
     "euc_argmin": ([_I, _V, _V, _I64, _I64, _I64, _F, _I, _V, _V, _V, _V, _V, _SZ, _V], _I),
+    "euc_prepared_points_bytes": ([_I, _I64, _I64], _SZ),
+    "euc_prepare_points": ([_I, _V, _I64, _I64, _V, _SZ, _V], _I),
+    "euc_argmin_prepared_workspace_bytes": ([_I, _I64, _I64, _I64], _SZ),
+    "euc_argmin_prepared": ([_I, _V, _V, _V, _I64, _I64, _I64, _F, _I, _V, _V, _V, _V, _V, _SZ, _V], _I),
     "euc_argmin_noalloc_max_bytes": ([], _SZ),
     "euc_argmin_noalloc": ([_I, _V, _V, _I64, _I64, _I64, _F, _I, _V, _V, _V, _V, _V], _I),
     "euc_center_stats_workspace_bytes": ([_I64, _I64, _I64], _SZ),

@@ -141,7 +141,23 @@ _LAST_COUNT = [None]
 ARGMIN_CERTIFIED = 2  # EUC_ARGMIN_CERTIFIED
 
 
-def run_argmin(op_name, P, C, kappa=5.0, exact=False, labels_dtype=torch.int64, min_dist=True):
+def prepare_points(op_name, P):
+    """The points' low-precision copy and norms for tensor-core operator `op_name`
+    (euc_prepare_points): a uint8 device buffer for run_argmin(..., prepared=...)."""
+    check_input(P, "P")
+    if P.dtype != torch.float32 or P.dim() != 2:
+        raise RuntimeError("P must be a 2D float32 tensor")
+    P = P.contiguous()
+    n, d = P.shape
+    nbytes = lib().euc_prepared_points_bytes(OPS[op_name], n, d)
+    if nbytes == 0 and n > 0:
+        raise RuntimeError(f"{op_name}: no prepared points (tensor-core operators only)")
+    buf = workspace(nbytes, P.device)
+    check(lib().euc_prepare_points(OPS[op_name], ptr(P), n, d, ptr(buf), buf.numel(), stream_of(P)))
+    return buf
+
+
+def run_argmin(op_name, P, C, kappa=5.0, exact=False, labels_dtype=torch.int64, min_dist=True, prepared=None):
     """Fused distance + argmin for distance operator `op_name` (a key of _lib.OPS):
     returns (labels, min_dist, flagged-pair count as a 0-d device tensor).  `exact`
     True selects the epilogue that forms every distance exactly as the D-producing
@@ -157,11 +173,16 @@ def run_argmin(op_name, P, C, kappa=5.0, exact=False, labels_dtype=torch.int64, 
     labels = torch.empty(n, dtype=labels_dtype, device=dev)
     md = torch.empty(n, dtype=want, device=dev) if min_dist else None
     cnt = torch.zeros(1, dtype=torch.int64, device=dev)
-    ws = workspace(lib().euc_argmin_workspace_bytes(OPS[op_name], n, m, d), dev)
     st = stream_of(P)
     l64 = labels if labels_dtype == torch.int64 else None
     l32 = labels if labels_dtype == torch.int32 else None
     mode = ARGMIN_CERTIFIED if isinstance(exact, str) and exact == "certified" else int(bool(exact))
+    if prepared is not None:
+        ws = workspace(lib().euc_argmin_prepared_workspace_bytes(OPS[op_name], n, m, d), dev)
+        check(lib().euc_argmin_prepared(OPS[op_name], ptr(P), ptr(prepared), ptr(C), n, m, d, ctypes.c_float(kappa),
+                                        mode, ptr(l64), ptr(l32), ptr(md), ptr(cnt), ptr(ws), ws.numel(), st))
+        return labels, md, cnt[0]
+    ws = workspace(lib().euc_argmin_workspace_bytes(OPS[op_name], n, m, d), dev)
     check(lib().euc_argmin(OPS[op_name], ptr(P), ptr(C), n, m, d, ctypes.c_float(kappa), mode,
                            ptr(l64), ptr(l32),
                            ptr(md), ptr(cnt), ptr(ws), ws.numel(), st))

@@ -142,7 +142,9 @@ constexpr int kMaxRegions = 1024;  // CTAs of the fast argmin screen: at most on
 static int low_esize(const OpSpec* s) { return s->gemm == G_TC_TF32 ? 4 : 2; }
 static bool is_tc(const OpSpec* s) { return s->gemm == G_TC_F16 || s->gemm == G_TC_BF16 || s->gemm == G_TC_TF32; }
 
-static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, bool argmin) {
+// `prepared`: the points' low-precision copy and norms come from the caller
+// (euc_argmin_prepared), so the workspace holds neither
+static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, bool argmin, bool prepared = false) {
   Layout L{};
   const size_t nsz = (s->form == FM_F64) ? 8 : 4;
   const int es = low_esize(s);
@@ -150,10 +152,10 @@ static Layout layout_for(const OpSpec* s, int64_t n, int64_t m, int64_t dim, boo
   L.ldlow = static_cast<int>(((dim + per_box - 1) / per_box) * per_box);
   size_t off = 0;
   L.hdr = off; off += 256;
-  L.pp = off; off += al(static_cast<size_t>(n) * nsz);
+  L.pp = off; if (!prepared) off += al(static_cast<size_t>(n) * nsz);
   L.cc = off; off += al(static_cast<size_t>(m) * nsz);
   if (is_tc(s)) {
-    L.plow = off; off += al(static_cast<size_t>(n) * L.ldlow * es);
+    L.plow = off; if (!prepared) off += al(static_cast<size_t>(n) * L.ldlow * es);
     L.clow = off; off += al(static_cast<size_t>(m) * L.ldlow * es);
     if (argmin && s->flag != FL_NONE) {  // norm-sorted centers for the fast argmin screen
       // norms and original indices padded to whole 256-center tiles (copied tile by tile)
@@ -217,8 +219,18 @@ static float k_float(const OpSpec* s, float kappa, int64_t dim) {
 // range (run_distance, the all-flagged route)
 constexpr float kAllFlaggedK = 2.5f;
 
+// the points' low-precision copy (n x ldlow) followed by their norms (fp32[n]), as
+// euc_prepare_points writes them
+static size_t prepared_plow_bytes(const OpSpec* s, int64_t n, int64_t dim) {
+  const int es = low_esize(s);
+  const int per_box = 128 / es;
+  const int64_t ld = ((dim + per_box - 1) / per_box) * per_box;
+  return al(static_cast<size_t>(n) * static_cast<size_t>(ld) * es);
+}
+
 struct RunOut {
   int mode = 0;                      // argmin mode: 0 screen, 1 exact epilogue, 2 certified
+  const void* prep = nullptr;        // argmin: prepared points (euc_prepare_points)
   void* D = nullptr;                 // D mode
   int64_t* labels = nullptr;         // argmin mode
   int32_t* labels32 = nullptr;
@@ -251,7 +263,11 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   if (cert && !cert_capable)
     return fail(EUC_ERR_UNSUPPORTED,
                 std::string(s->name) + ": no certified argmin (tensor-core operators with an fp32 or fp64 recompute)");
-  const Layout L = layout_for(s, n, m, dim, argmin);
+  const bool prepared = o.prep != nullptr;
+  if (prepared && (!argmin || !is_tc(s) || s->in != IN_F32 || s->form != FM_F32 || o.mode == 2))
+    return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) +
+                                         ": prepared points serve the tensor-core screen and exact argmin only");
+  const Layout L = layout_for(s, n, m, dim, argmin, prepared);
   if (!ws || ws_bytes < L.total)
     return fail(EUC_ERR_WORKSPACE, std::string(s->name) + ": workspace of " + std::to_string(L.total) +
                                        " bytes required, got " + std::to_string(ws_bytes));
@@ -272,7 +288,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   // range test reads P and C once and costs one stream synchronisation; a call that
   // fails it takes the exact path below.
   bool all_flagged = false;
-  if (argmin && o.mode != 2 && cert_capable && k_float(s, kappa, dim) >= kAllFlaggedK) {
+  if (argmin && !prepared && o.mode != 2 && cert_capable && k_float(s, kappa, dim) >= kAllFlaggedK) {
     Phase ph("euc:range_check");
     int* dflag = reinterpret_cast<int*>(w + L.hdr + 40);
     const bool f16 = s->sround == SR_F16 || s->norm == NM_LOW_F16;
@@ -308,6 +324,10 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.pp = w + L.pp;
   j.cc = w + L.cc;
   j.Plow = is_tc(s) ? w + L.plow : nullptr;
+  if (prepared) {
+    j.Plow = const_cast<void*>(o.prep);
+    j.pp = static_cast<uint8_t*>(const_cast<void*>(o.prep)) + prepared_plow_bytes(s, n, dim);
+  }
   j.Clow = is_tc(s) ? w + L.clow : nullptr;
   j.ldlow = L.ldlow;
   // the screen bounds flagged pairs through 1 - K > 0
@@ -377,7 +397,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   j.stream = st;
   if (j.fast_argmin && j.regions > kMaxRegions) return fail(EUC_ERR_UNSUPPORTED, "more SMs than list regions");
   // the screening kernel prepares the points itself where it can (no low-precision copy)
-  j.fused_rows = j.fast_argmin && tc_fast_can_fuse_rows(j);
+  j.fused_rows = j.fast_argmin && !prepared && tc_fast_can_fuse_rows(j);
   // certified, points read by the screen itself: the second screen runs on a gathered
   // low-precision copy of the undecided rows (the copy region is free)
   j.cert_gather = cert && j.cert_ng > 0 && j.fused_rows && j.cert_F != nullptr && j.Plow != nullptr;
@@ -404,7 +424,7 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
   }
   {
     Phase ph("euc:prep");
-    if (!j.fused_rows) e = launch_prep(j, true, is_tc(s));
+    if (!j.fused_rows && !prepared) e = launch_prep(j, true, is_tc(s));
     if (e == cudaSuccess) e = launch_prep(j, false, is_tc(s));
     if (e == cudaSuccess && j.fast_argmin) e = launch_sort_centers(j);
   }
@@ -774,6 +794,64 @@ int euc_kmeanspp(const void* X, int x_is_f64, int64_t n, int64_t dim, int64_t k,
 }
 
 // ------------------------------------------------------------------ fused argmin
+// ------------------------------------------------------------------ prepared points
+size_t euc_prepared_points_bytes(int op, int64_t n, int64_t dim) {
+  const OpSpec* s = find_op(op);
+  if (!s || !is_tc(s) || n < 0 || dim <= 0) return 0;
+  return prepared_plow_bytes(s, n, dim) + al(static_cast<size_t>(n) * 4);
+}
+
+int euc_prepare_points(int op, const float* P, int64_t n, int64_t dim, void* prep, size_t prep_bytes, void* stream) {
+  const OpSpec* s = find_op(op);
+  if (!s) return fail(EUC_ERR_ARG, "unknown operator id");
+  if (!is_tc(s) || s->in != IN_F32 || s->form != FM_F32)
+    return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) + ": no prepared points (tensor-core operators only)");
+  if (n < 0 || dim <= 0) return fail(EUC_ERR_SHAPE, "bad size");
+  if (dim > (1 << 20) || n > 0xffffffffll) return fail(EUC_ERR_SHAPE, "shape too large");
+  if (!device_is_sm100()) return fail(EUC_ERR_DEVICE, "euclid_b200 requires an sm_100 (B200) device");
+  if (n == 0) return ok();
+  if (!P || !prep) return fail(EUC_ERR_ARG, "null pointer");
+  if (prep_bytes < euc_prepared_points_bytes(op, n, dim))
+    return fail(EUC_ERR_WORKSPACE, std::string(s->name) + ": prepared-points buffer too small");
+  DistJob j{};
+  j.spec = s;
+  j.P = P;
+  j.n = n;
+  j.dim = static_cast<int>(dim);
+  j.ldlow = layout_for(s, n, 1, dim, true).ldlow;
+  j.Plow = prep;
+  j.pp = static_cast<uint8_t*>(prep) + prepared_plow_bytes(s, n, dim);
+  j.stream = static_cast<cudaStream_t>(stream);
+  Phase ph("euc:prepare_points");
+  const cudaError_t e = launch_prep(j, true, true);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "prepare_points");
+}
+
+size_t euc_argmin_prepared_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim) {
+  const OpSpec* s = find_op(op);
+  if (!s || !is_tc(s)) return 0;
+  return layout_for(s, n, m, dim, true, true).total;
+}
+
+int euc_argmin_prepared(int op, const float* P, const void* prep, const float* C, int64_t n, int64_t m, int64_t dim,
+                        float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count,
+                        void* ws, size_t ws_bytes, void* stream) {
+  const OpSpec* s = find_op(op);
+  if (!s) return fail(EUC_ERR_ARG, "unknown operator id");
+  if (!is_tc(s)) return fail(EUC_ERR_UNSUPPORTED, std::string(s->name) + ": no prepared points (tensor-core operators only)");
+  if (exact == EUC_ARGMIN_CERTIFIED)
+    return fail(EUC_ERR_UNSUPPORTED, "prepared points serve the screen and the exact argmin, not the certified mode");
+  if (n > 0 && m > 0 && !prep) return fail(EUC_ERR_ARG, "null prepared points");
+  RunOut o;
+  o.mode = exact != 0 ? 1 : 0;
+  o.prep = prep;
+  o.labels = labels;
+  o.labels32 = labels32;
+  o.min_dist = min_dist;
+  o.d_count = d_count;
+  return run_distance(s, P, C, n, m, dim, kappa, o, ws, ws_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t m, int64_t dim, float kappa, int exact,
                int64_t* labels, int32_t* labels32, void* min_dist, uint64_t* d_count, void* ws, size_t ws_bytes,
                void* stream) {

@@ -49,13 +49,17 @@ class LloydKMeans:
     'fp16_fp32', 'double') whose cancellation test and recompute define the labels;
     `mode` ('fast', 'exact', 'certified') is the argmin mode of euc_argmin."""
 
-    def __init__(self, n_clusters, op="bf16_fp32", kappa=5.0, empty="zero", group=None, mode="fast"):
+    def __init__(self, n_clusters, op="bf16_fp32", kappa=5.0, empty="zero", group=None, mode="fast",
+                 store_low=False):
         self.k = int(n_clusters)
         self.op = op
         self.kappa = float(kappa)
         self.empty = EMPTY_POLICY[empty]
         self.group = group
         self.mode = ASSIGN_MODE[mode]
+        # screen from a low-precision copy of the points made once per fit (prepare), the
+        # fp32 points read only for the recompute and the center statistics
+        self.store_low = bool(store_low)
         self._ws = None
 
     def _world(self):
@@ -79,19 +83,25 @@ class LloydKMeans:
                                         ptr(prev), self.empty, stream_of(stats)))
         return out
 
-    def assign(self, X, C):
+    def prepare(self, X):
+        """The points' low-precision copy and norms for the screen (store_low); reuse it
+        for every iteration over the same X."""
+        return _ops.prepare_points(self.op, X)
+
+    def assign(self, X, C, prepared=None):
         """Labels (int32) of the local rows and the flagged-pair count (0-d tensor; the
         number of direct distances taken in the certified mode)."""
         labels, _, cnt = _ops.run_argmin(self.op, X, C, self.kappa, exact=self.mode, labels_dtype=torch.int32,
-                                         min_dist=False)
+                                         min_dist=False, prepared=prepared)
         return labels, cnt
 
-    def step(self, X, C):
+    def step(self, X, C, prepared=None):
         """One iteration on the local shard X; returns (new centers, labels int32,
-        flagged-pair count of this shard as a 0-d device tensor).  Each phase is an NVTX
-        range (lloyd:assign, lloyd:center_stats, lloyd:all_reduce, lloyd:finalize)."""
+        flagged-pair count of this shard as a 0-d device tensor).  `prepared`: the
+        result of prepare(X) (store_low).  Each phase is an NVTX range (lloyd:assign,
+        lloyd:center_stats, lloyd:all_reduce, lloyd:finalize)."""
         with _phase("lloyd:assign"):
-            labels, cnt = self.assign(X, C)
+            labels, cnt = self.assign(X, C, prepared)
         with _phase("lloyd:center_stats"):
             stats = self.center_stats(X, labels)
         if self._world() > 1:
@@ -103,8 +113,9 @@ class LloydKMeans:
     def fit(self, X, C0, n_iter):
         C = C0.contiguous()
         labels = None
+        prepared = self.prepare(X) if self.store_low else None
         for _ in range(int(n_iter)):
-            C, labels, _ = self.step(X, C)
+            C, labels, _ = self.step(X, C, prepared)
         return C, labels
 
 

@@ -268,6 +268,25 @@ EUC_API int euc_argmin(int op, const void* P, const void* C, int64_t n, int64_t 
                float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,
                uint64_t* d_count, void* ws, size_t ws_bytes, void* stream);
 
+/* Prepared points.  The reference casts the fp32 points to the GEMM's low precision on
+ * every call (euclidean_kernels_mix.cu:531-532, P.to(torch::kFloat16)); a caller that
+ * screens the same points many times (Lloyd iterations) can keep that low-precision
+ * copy instead: euc_prepare_points writes, for a tensor-core operator `op`, the points
+ * rounded to its operand type (rows padded to whole 128-byte boxes) followed by their
+ * norms in the operator's recipe, into a caller buffer of euc_prepared_points_bytes().
+ * euc_argmin_prepared then screens from that copy (2 bytes a value for fp16/bf16) and
+ * reads the fp32 points P only for the pairs it recomputes; its outputs equal
+ * euc_argmin's for the same P (modes 0 and 1; the certified mode is rejected).  Its
+ * workspace is euc_argmin_prepared_workspace_bytes(), smaller than euc_argmin's by the
+ * copy and the norms.  No counterpart in the reference beyond the cast it replaces. */
+EUC_API size_t euc_prepared_points_bytes(int op, int64_t n, int64_t dim);
+EUC_API int euc_prepare_points(int op, const float* P, int64_t n, int64_t dim, void* prep, size_t prep_bytes,
+                       void* stream);
+EUC_API size_t euc_argmin_prepared_workspace_bytes(int op, int64_t n, int64_t m, int64_t dim);
+EUC_API int euc_argmin_prepared(int op, const float* P, const void* prep, const float* C, int64_t n, int64_t m,
+                        int64_t dim, float kappa, int exact, int64_t* labels, int32_t* labels32, void* min_dist,
+                        uint64_t* d_count, void* ws, size_t ws_bytes, void* stream);
+
 /* No counterpart in the reference.  euc_argmin without a workspace, for callers that
  * cannot allocate device memory (a host binding with no device allocator, or a
  * process whose memory pool already holds the device's memory): the scratch is one

@@ -30,7 +30,7 @@ from oracle import oracle as O  # noqa: E402
 class HostLloyd(kmeans.LloydKMeans):
     """LloydKMeans with the per-rank compute on the host (oracle)."""
 
-    def assign(self, X, C):
+    def assign(self, X, C, prepared=None):
         lab, _, _ = O.dist_argmin_f64(X.numpy(), C.numpy(), threads=1)
         return torch.from_numpy(lab.astype(np.int32)), torch.zeros((), dtype=torch.int64)
 

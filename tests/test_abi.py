@@ -132,3 +132,26 @@ def test_noalloc_entry_checks_arguments_before_the_scratch(lib):
         pytest.skip("GPU present")
     assert f(15, None, None, 10, 10, 4, 5.0, 0, None, None, None, None, None) == 8  # EUC_ERR_DEVICE
     assert b"sm_100" in lib.euc_last_error()
+
+
+def test_prepared_points_sizes_and_checks(lib):
+    """euc_prepared_points_bytes: the rounded copy (rows padded to whole 128-byte boxes)
+    then fp32 norms, each 256-byte aligned; 0 for operators without a tensor-core GEMM.
+    euc_prepare_points rejects bad sizes before the device check."""
+    import torch
+    al = lambda b: (b + 255) // 256 * 256
+    f = lib.euc_prepared_points_bytes
+    f.restype = ctypes.c_size_t
+    f.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_int64]
+    assert f(17, 1000, 70) == al(1000 * 128 * 2) + al(1000 * 4)    # bf16_fp32: 70 -> 128 per row
+    assert f(12, 1000, 70) == al(1000 * 96 * 4) + al(1000 * 4)     # tf32_fp64: 70 -> 96 per row
+    assert f(18, 1000, 70) == 0                                    # fp32_fp32: CUDA-core GEMM
+    g = lib.euc_prepare_points
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t,
+                  ctypes.c_void_p]
+    assert g(17, None, -1, 8, None, 0, None) == 1   # EUC_ERR_SHAPE
+    assert g(18, None, 10, 8, None, 0, None) == 3   # EUC_ERR_UNSUPPORTED
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    assert g(17, ctypes.c_void_p(16), 10, 8, ctypes.c_void_p(16), 1 << 20, None) == 8  # EUC_ERR_DEVICE
