@@ -448,35 +448,39 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
         }
       }
       if (!ok[0]) break;
+      // each row's values twice in a 64-bit pair, for the packed arithmetic below
+      uint64_t pb[R][DIM];
+#pragma unroll
+      for (int t = 0; t < R; ++t)
+#pragma unroll
+        for (int k = 0; k < DIM; ++k) pb[t][k] = f2_pack(p[t][k], p[t][k]);
       for (int j0 = hl * 4; j0 < m; j0 += 64) {
-        float acc[R][4];
+        // four centers as two pairs (j0, j0+1), (j0+2, j0+3); every lane of a packed
+        // operation is the scalar fused multiply-add / add of that pair, in the same order
+        uint64_t acc[R][2];
 #pragma unroll
-        for (int t = 0; t < R; ++t)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) acc[t][c] = 0.f;
+        for (int t = 0; t < R; ++t) acc[t][0] = acc[t][1] = 0ull;
 #pragma unroll
         for (int k = 0; k < DIM; ++k) {
-          const float4 cv = *reinterpret_cast<const float4*>(csT + k * m + j0);
-          const float cvs[4] = {cv.x, cv.y, cv.z, cv.w};
+          uint64_t c01, c23;
+          lds_f2x2(csT + k * m + j0, c01, c23);
 #pragma unroll
-          for (int t = 0; t < R; ++t)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              if constexpr (MODE == THIN_DIRECT) {
-                const float d = p[t][k] - cvs[c];
-                acc[t][c] = __fmaf_rn(d, d, acc[t][c]);
-              } else {
-                acc[t][c] = __fmaf_rn(p[t][k], cvs[c], acc[t][c]);
-              }
+          for (int t = 0; t < R; ++t) {
+            if constexpr (MODE == THIN_DIRECT) {
+              const uint64_t d01 = f2_sub(pb[t][k], c01), d23 = f2_sub(pb[t][k], c23);
+              acc[t][0] = f2_fma(d01, d01, acc[t][0]);
+              acc[t][1] = f2_fma(d23, d23, acc[t][1]);
+            } else {
+              acc[t][0] = f2_fma(pb[t][k], c01, acc[t][0]);
+              acc[t][1] = f2_fma(pb[t][k], c23, acc[t][1]);
             }
+          }
         }
-        float ccs[4] = {0.f, 0.f, 0.f, 0.f};
+        uint64_t cc2[2] = {0ull, 0ull};
         if constexpr (MODE == THIN_FORM) {
           const float4 c4 = __ldg(reinterpret_cast<const float4*>(cc + j0));
-          ccs[0] = c4.x;
-          ccs[1] = c4.y;
-          ccs[2] = c4.z;
-          ccs[3] = c4.w;
+          cc2[0] = f2_pack(c4.x, c4.y);
+          cc2[1] = f2_pack(c4.z, c4.w);
         }
         uint32_t fmask = 0;  // flagged pairs (bit 4 t + c)
 #pragma unroll
@@ -485,13 +489,25 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
           const int rt = rr + 16 * t;
           float v[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int h = 0; h < 2; ++h) {
             if constexpr (MODE == THIN_DIRECT) {
-              v[c] = acc[t][c];
+              f2_unpack(acc[t][h], v[2 * h], v[2 * h + 1]);
             } else {
-              const float d = fmaxf(__fadd_rn(__fmaf_rn(-2.f, acc[t][c], pp[t]), ccs[c]), 0.f);
-              v[c] = d;
-              if constexpr (FLAG) fmask |= static_cast<uint32_t>(d <= __fmul_rn(kf, __fadd_rn(pp[t], ccs[c]))) << (4 * t + c);
+              // d = max((pp - 2 s) + cc, 0) and the test d <= K (pp + cc), per lane
+              const uint64_t pp2 = f2_pack(pp[t], pp[t]);
+              const uint64_t e = f2_add(f2_fma(f2_pack(-2.f, -2.f), acc[t][h], pp2), cc2[h]);
+              float d0, d1;
+              f2_unpack(e, d0, d1);
+              d0 = fmaxf(d0, 0.f);
+              d1 = fmaxf(d1, 0.f);
+              v[2 * h] = d0;
+              v[2 * h + 1] = d1;
+              if constexpr (FLAG) {
+                float t0, t1;
+                f2_unpack(f2_mul(f2_pack(kf, kf), f2_add(pp2, cc2[h])), t0, t1);
+                fmask |= (static_cast<uint32_t>(d0 <= t0) << (4 * t + 2 * h)) |
+                         (static_cast<uint32_t>(d1 <= t1) << (4 * t + 2 * h + 1));
+              }
             }
           }
           *reinterpret_cast<float4*>(D + (row0 + rt) * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
