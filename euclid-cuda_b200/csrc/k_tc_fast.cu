@@ -76,7 +76,6 @@ constexpr int TF_XBOX_BYTES = 32 * 4 * TF_BM;  // FUSED staging: 32 fp32 values 
 constexpr int TF_AAUX_BYTES = TF_BM * 32;       // per A buffer: the rows' extra-K rows
 constexpr int TF_ROWBUF_BYTES = 2 * TF_BM * 4;  // per A buffer: pp and Br of each row
 constexpr int TF_BAR_BYTES = 512;
-constexpr int TF_EPI_BYTES = 2 * 3 * TF_BM * 4;  // row merge
 
 struct TfArgs {
   int64_t n, m;
@@ -198,12 +197,9 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
   uint64_t* xfull = pempty + 2;         // FUSED staging: the row tile's points have landed
   uint64_t* xempty = xfull + 1;         // FUSED staging: every row thread has read them
   uint64_t* drain = xempty + 1;
-  uint64_t* mfull = drain + 1;   // row merge: groups 1..3 have published their row minima
-  uint64_t* mdone = mfull + 1;   // row merge: group 0 has consumed them
-  unsigned long long* lcount = reinterpret_cast<unsigned long long*>(mdone + 1);  // this CTA's list entries
+  unsigned long long* lcount = reinterpret_cast<unsigned long long*>(drain + 1);  // this CTA's list entries
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lcount + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + TF_BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -233,8 +229,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
       mbar_init(&metae[s], TF_EPI_WARPS / 2);
     }
     mbar_init(drain, 1);
-    mbar_init(mfull, TF_EPI_WARPS - 4);
-    mbar_init(mdone, 4);
     *lcount = 0;
     *abort_flag = 0;
     fence_mbar_init();
@@ -434,8 +428,6 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
     const uint32_t b = static_cast<uint32_t>(g >> 1);
     const int row_local = q * 32 + lane;
     const uint32_t tmem_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * TF_BN + hc * 128;
-    float* mv = epi;                                             // row merge: [3][128] minima
-    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 3 * TF_BM);  //            [3][128] their columns
     unsigned long long* region = a.list + static_cast<unsigned long long>(blockIdx.x) * a.region_cap;
     float* region_s = a.sbuf + static_cast<unsigned long long>(blockIdx.x) * a.region_cap * 32;
     // screen: a pair can only be flagged (d <= K (pp + cc)) where
@@ -665,26 +657,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         bestv = fmaxf(__fadd_rn(__fadd_rn(2.f * __uint_as_float(kb & ~31u), -br), pp), 0.f);
         besti = static_cast<uint32_t>(__ldg(a.perm + static_cast<int64_t>(best_c) + (kb & 31u)));
       }
-      // merge the four (parity, column half) partial minima of each row
-      const uint32_t par = rt_i & 1u;
-      if (g != 0) {
-        if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
-        mv[(g - 1) * TF_BM + row_local] = bestv;
-        mi[(g - 1) * TF_BM + row_local] = besti;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(mfull);
-      } else {
-        if (!mbar_wait(mfull, par, abort_flag, a.wait_ns)) { ok = false; break; }
-#pragma unroll
-        for (int p = 0; p < 3; ++p) {
-          const float ov = mv[p * TF_BM + row_local];
-          const uint32_t oi = mi[p * TF_BM + row_local];
-          if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(mdone);
-        if (row_ok) a.row_key[i] = make_key(bestv, besti);
-      }
+      // the four groups' (parity, column half) partial minima of a row meet in its key:
+      // a 64-bit atomic min of (distance bits, original index), the smaller index among
+      // equal distances, with no barrier between the groups (the key starts at ~0)
+      if (row_ok) atomicMin(&a.row_key[i], make_key(bestv, besti));
     }
     if (!ok) {
       *abort_flag = 1;
@@ -835,7 +811,7 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 
 constexpr size_t TF_SMEM_LIMIT = 232448;
 constexpr size_t TF_FIXED = 1024 + static_cast<size_t>(TF_SLOTS) * TF_META_BYTES + 2 * TF_AAUX_BYTES +
-                            2 * TF_ROWBUF_BYTES + TF_BAR_BYTES + TF_EPI_BYTES;
+                            2 * TF_ROWBUF_BYTES + TF_BAR_BYTES;
 constexpr size_t TF_STAGE_EXTRA = TF_BAUX_BYTES;  // a stage's room for the tile's extra-K rows
 
 // FUSED staging: the row tile's fp32 points, 32 values of each row per box
@@ -1045,6 +1021,11 @@ cudaError_t launch_tc_fast(const DistJob& j, int cert_pass) {
   if (cert_pass == 1) {
     if (!j.cert_key || !j.cert_d2) return cudaErrorInvalidValue;
     TF_LAUNCH(1, false)
+  }
+  if (cert_pass == 0 && j.row_key) {
+    // the screen folds each group's row minimum into the key with an atomic min
+    const cudaError_t e = cudaMemsetAsync(j.row_key, 0xff, static_cast<size_t>(j.n) * sizeof(unsigned long long), j.stream);
+    if (e != cudaSuccess) return e;
   }
   if (cert_pass == 2) {
     if (!j.cert_thr || !j.cert_tiles) return cudaErrorInvalidValue;
