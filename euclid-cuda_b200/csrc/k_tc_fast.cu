@@ -1145,6 +1145,10 @@ template <int SROUND, int REC>
 __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   __shared__ unsigned long long s_buf[8][EV_WBUF];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  // a warp evaluates four entries at a time: the eight lanes sg * 8 .. sg * 8 + 7 take
+  // entry sg, lane sl of them the four columns 4 sl .. 4 sl + 3 (16-byte loads of the
+  // accumulators, norms and original indices)
+  const int sg = lane >> 3, sl = lane & 7;
   unsigned long long* wbuf = s_buf[wib];
   int wcnt = 0;
   const int r = blockIdx.x / EV_BLOCKS_PER_REGION;
@@ -1156,57 +1160,80 @@ __global__ void __launch_bounds__(256) eval_chunks_kernel(const EvArgs a) {
   const uint32_t cnt = static_cast<uint32_t>(cnt64);
   const unsigned long long rbase = static_cast<unsigned long long>(r) * a.region_cap;
   const unsigned long long* cl = a.clist + rbase;
-  const float* sb = a.sbuf + rbase * 32 + lane;
+  const float4* sb = reinterpret_cast<const float4*>(a.sbuf + rbase * 32) + sl;
   const uint32_t n32 = static_cast<uint32_t>(a.n), m32 = static_cast<uint32_t>(a.m);
-  // four entries per iteration: their loads are independent and issue together (eight
-  // measured slower at the Lloyd size: the registers they take halve the resident warps)
-  constexpr int U = 4;
-  for (uint32_t t0 = wr; t0 < cnt; t0 += kStride * U) {
+  // two sets of four entries per iteration: their loads are independent and issue together
+  constexpr int U = 2;
+  for (uint32_t t0 = wr * 4u * U; t0 < cnt; t0 += kStride * 4u * U) {
     unsigned long long e[U];
-    float sv[U];
+    float4 s4[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const uint32_t t = t0 + u * kStride;
+      const uint32_t t = t0 + u * 4u + sg;
       const bool in = t < cnt;
       e[u] = in ? cl[t] : ~0ull;
-      sv[u] = in ? sb[t * 32u] : 0.f;
+      s4[u] = in ? sb[t * 8u] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    uint32_t i[U], jo[U];
-    bool jv[U], skip[U];
-    float pp[U], cc[U];
+    uint32_t i[U], j0[U];
+    bool skip[U];
+    float pp[U];
+    float4 c4[U];
+    int4 p4[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       i[u] = static_cast<uint32_t>(e[u] >> 32);
-      const uint32_t j = static_cast<uint32_t>(e[u]) + lane;
       const bool iv = i[u] < n32;
       skip[u] = !iv || a.redo[iv ? i[u] : 0u] != 0;  // redo rows are evaluated whole
-      jv[u] = iv && j < m32;
-      pp[u] = iv ? __ldg(a.pp + i[u]) : 0.f;
-      cc[u] = jv[u] ? __ldg(a.cc_s + j) : 0.f;
-      jo[u] = jv[u] ? static_cast<uint32_t>(__ldg(a.perm + j)) : 0u;
+      // the chunk's first sorted column is a multiple of 32 and the norms and indices are
+      // padded to whole 256-center tiles, so the 16-byte loads stay in bounds
+      j0[u] = static_cast<uint32_t>(e[u]) + 4u * static_cast<uint32_t>(sl);
+      pp[u] = 0.f;
+      c4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      p4[u] = make_int4(0, 0, 0, 0);
+      if (!skip[u]) {
+        pp[u] = __ldg(a.pp + i[u]);
+        c4[u] = __ldg(reinterpret_cast<const float4*>(a.cc_s + j0[u]));
+        p4[u] = __ldg(reinterpret_cast<const int4*>(a.perm + j0[u]));
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (skip[u]) continue;  // warp-uniform
+      const float sv[4] = {s4[u].x, s4[u].y, s4[u].z, s4[u].w};
+      const float cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w};
+      const uint32_t jo[4] = {static_cast<uint32_t>(p4[u].x), static_cast<uint32_t>(p4[u].y),
+                              static_cast<uint32_t>(p4[u].z), static_cast<uint32_t>(p4[u].w)};
       const float br = __fmul_rn(pp[u], kAuxRowScale);
-      const float y0 = cc[u] < 3.0e38f ? __fadd_rn(0.5f * cc[u], 0.5f * br) : 0.f;
-      const float d = exact_d<SROUND>(y0 - sv[u], pp[u], cc[u]);
-      const bool fl = jv[u] && d <= __fmul_rn(a.K, __fadd_rn(pp[u], cc[u]));
-      const unsigned bal = __ballot_sync(0xffffffffu, fl);
-      if (bal) {
-        if (fl) wbuf[wcnt + __popc(bal & ((1u << lane) - 1u))] = (static_cast<unsigned long long>(i[u]) << 32) | jo[u];
-        wcnt += __popc(bal);
-        __syncwarp();
-        if (wcnt > EV_WBUF - 32) flush_pairs<REC>(a, wbuf, wcnt, lane);
-      }
       // row key of the chunk: smallest unflagged distance (d >= 0, so its bits order as
       // unsigned), then the smallest original index among the columns that reach it
-      const uint32_t dbits = (jv[u] && !fl) ? __float_as_uint(d) : 0xffffffffu;
-      const uint32_t dmin = __reduce_min_sync(0xffffffffu, dbits);
-      if (dmin != 0xffffffffu) {
-        const uint32_t jmin = __reduce_min_sync(0xffffffffu, dbits == dmin ? jo[u] : 0xffffffffu);
-        if (lane == 0) atomicMin(&a.row_key[i[u]], (static_cast<unsigned long long>(dmin) << 32) | jmin);
+      unsigned long long best = ~0ull;
+      uint32_t flm = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const bool jv = !skip[u] && j0[u] + c < m32;
+        const float y0 = cc[c] < 3.0e38f ? __fadd_rn(0.5f * cc[c], 0.5f * br) : 0.f;
+        const float d = exact_d<SROUND>(y0 - sv[c], pp[u], cc[c]);
+        const bool fl = jv && d <= __fmul_rn(a.K, __fadd_rn(pp[u], cc[c]));
+        flm |= static_cast<uint32_t>(fl) << c;
+        const unsigned long long k = (jv && !fl) ? ((static_cast<unsigned long long>(__float_as_uint(d)) << 32) | jo[c]) : ~0ull;
+        best = k < best ? k : best;
       }
+      if (__any_sync(0xffffffffu, flm != 0)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool fl = (flm >> c) & 1u;
+          const unsigned bal = __ballot_sync(0xffffffffu, fl);
+          if (fl) wbuf[wcnt + __popc(bal & ((1u << lane) - 1u))] = (static_cast<unsigned long long>(i[u]) << 32) | jo[c];
+          wcnt += __popc(bal);
+        }
+        __syncwarp();
+        if (wcnt > EV_WBUF - 128) flush_pairs<REC>(a, wbuf, wcnt, lane);
+      }
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) {
+        const unsigned long long x = __shfl_xor_sync(0xffffffffu, best, o);
+        best = x < best ? x : best;
+      }
+      if (sl == 0 && best != ~0ull) atomicMin(&a.row_key[i[u]], best);
     }
   }
   // the warps' remaining pairs: one list reservation for the whole block (a reservation
