@@ -367,10 +367,13 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             const uint32_t sA = a_res ? sAres + kb * TF_A_KB : st;
             const uint32_t sB = a_res ? st : st + TF_A_KB;
             const uint32_t d_tmem = tmem_base + b * TF_BN;
+            // K step kk starts 32 bytes further: +2 in the descriptor's address field (in
+            // 16-byte units; shared addresses stay below 2^18, so the field never carries)
+            const uint64_t ad0 = sw128_kmajor_desc(sA), bd0 = sw128_kmajor_desc(sB);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_kmajor_desc(sA + kk * 32);
-              const uint64_t bd = sw128_kmajor_desc(sB + kk * 32);
+              const uint64_t ad = ad0 + 2u * kk;
+              const uint64_t bd = bd0 + 2u * kk;
               if constexpr (KIND == 2) {
                 if constexpr (PAIR) umma_tf32_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0);
                 else umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
