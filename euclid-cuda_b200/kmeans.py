@@ -102,21 +102,67 @@ class LloydKMeans:
         lloyd:center_stats, lloyd:all_reduce, lloyd:finalize)."""
         with _phase("lloyd:assign"):
             labels, cnt = self.assign(X, C, prepared)
+        return self._update(X, labels, C), labels, cnt
+
+    def fit(self, X, C0, n_iter, upload_chunks=8):
+        """n_iter Lloyd iterations from initial centers C0 (on the GPU); returns (centers,
+        labels int32).  X is the local shard, on C0's device or in host memory (pinned
+        for an asynchronous copy): a host X is copied in `upload_chunks` row blocks on a
+        side stream, and the first iteration assigns each block as soon as it has landed,
+        so the copy overlaps the first assignment (a row's label does not depend on the
+        other rows, so the labels are those of one assignment of the whole shard)."""
+        C = C0.contiguous()
+        labels = None
+        n_iter = int(n_iter)
+        if not X.is_cuda and C.is_cuda:
+            X, labels = self._upload_and_assign(X, C, upload_chunks if n_iter > 0 and not self.store_low else 1)
+            if n_iter > 0 and not self.store_low:
+                C = self._update(X, labels, C)
+                n_iter -= 1
+        prepared = self.prepare(X) if self.store_low else None
+        for _ in range(n_iter):
+            C, labels, _ = self.step(X, C, prepared)
+        return C, labels
+
+    def _upload_and_assign(self, Xh, C, chunks):
+        """Xh (host) copied to C's device in row blocks on a side stream; with chunks > 1
+        each block is assigned on the current stream once it has landed."""
+        dev = C.device
+        n = Xh.size(0)
+        Xd = torch.empty(Xh.shape, dtype=Xh.dtype, device=dev)
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(cur)  # Xd is allocated on the current stream
+        bounds = [shard_rows(n, c, max(1, chunks)) for c in range(max(1, chunks))]
+        events = []
+        with torch.cuda.stream(side):
+            for lo, hi in bounds:
+                if hi > lo:
+                    Xd[lo:hi].copy_(Xh[lo:hi], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(side)
+                events.append(ev)
+        if chunks <= 1:
+            cur.wait_event(events[-1])
+            return Xd, None
+        labels = torch.empty(n, dtype=torch.int32, device=dev)
+        with _phase("lloyd:assign"):
+            for (lo, hi), ev in zip(bounds, events):
+                cur.wait_event(ev)
+                if hi > lo:
+                    lab, _ = self.assign(Xd[lo:hi], C)
+                    labels[lo:hi].copy_(lab)
+        return Xd, labels
+
+    def _update(self, X, labels, C):
+        """The center update of one iteration from its labels."""
         with _phase("lloyd:center_stats"):
             stats = self.center_stats(X, labels)
         if self._world() > 1:
             with _phase("lloyd:all_reduce"):
                 dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=self.group)
         with _phase("lloyd:finalize"):
-            return self.finalize(stats, C), labels, cnt
-
-    def fit(self, X, C0, n_iter):
-        C = C0.contiguous()
-        labels = None
-        prepared = self.prepare(X) if self.store_low else None
-        for _ in range(int(n_iter)):
-            C, labels, _ = self.step(X, C, prepared)
-        return C, labels
+            return self.finalize(stats, C)
 
 
 def kmeanspp(X, k, seed=0):

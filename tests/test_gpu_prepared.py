@@ -74,6 +74,26 @@ def test_lloyd_fit_from_stored_copy():
     assert torch.equal(Ca, Cb)
 
 
+@pytest.mark.parametrize("store_low", [False, True])
+def test_lloyd_fit_from_host_shard(store_low):
+    """fit from a pinned host shard (uploaded in row blocks, each assigned as it lands)
+    gives the centers and labels of fit from the shard already on the device."""
+    rng = np.random.default_rng(4)
+    n, d, k = 30011, 64, 300
+    true_c = rng.uniform(-5, 5, (k, d))
+    Xh = torch.from_numpy((true_c[rng.integers(0, k, n)] + rng.normal(0, 0.5, (n, d))).astype(np.float32))
+    Xh = Xh.pin_memory()
+    X = Xh.cuda()
+    C0 = X[torch.from_numpy(rng.choice(n, k, replace=False)).cuda()].contiguous()
+    Ca, la = LloydKMeans(k, op="bf16_fp32", kappa=0.1, store_low=store_low).fit(X, C0, 3)
+    Cb, lb = LloydKMeans(k, op="bf16_fp32", kappa=0.1, store_low=store_low).fit(Xh, C0, 3, upload_chunks=7)
+    Cc, lc = LloydKMeans(k, op="bf16_fp32", kappa=0.1, store_low=store_low).fit(Xh, C0, 1, upload_chunks=5)
+    Cd, ld = LloydKMeans(k, op="bf16_fp32", kappa=0.1, store_low=store_low).fit(X, C0, 1)
+    device_check()
+    assert torch.equal(la, lb) and torch.equal(Ca, Cb)
+    assert torch.equal(lc, ld) and torch.equal(Cc, Cd)
+
+
 def test_prepared_workspace_is_smaller():
     L = lib()
     op, n, m, d = OPS["bf16_fp32"], 1 << 20, 4096, 64
