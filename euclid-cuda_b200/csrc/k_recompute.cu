@@ -154,18 +154,36 @@ __global__ void __launch_bounds__(RW_WARPS * 32, 4) recompute_argmin_rows_kernel
 // arithmetic and dimension order (direct_dist); flagged elements are stored.  The
 // kernel returns at once when the list held every flagged pair.
 constexpr int RT_B = 64, RT_K = 16;
+constexpr int RT_LD = RT_B + 4;  // shared row stride: 16-byte aligned rows, staggered banks
+
+// four consecutive shared values (16-byte aligned) into registers: one 16-byte load for
+// fp32, two for fp64
+template <typename T>
+__device__ __forceinline__ void rt_lds4(const T* p, T (&v)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 q = *reinterpret_cast<const float4*>(p);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+  } else {
+    const double2 q0 = *reinterpret_cast<const double2*>(p), q1 = *reinterpret_cast<const double2*>(p + 2);
+    v[0] = q0.x; v[1] = q0.y; v[2] = q1.x; v[3] = q1.y;
+  }
+}
 
 template <typename TIN, int REC, typename TOUT, int FLAG>
 __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArgs a) {
   using TACC = typename std::conditional<REC == RC_F64, double, float>::type;
   if (*a.count <= a.cap) return;  // the list path has done it
-  __shared__ TACC As[RT_K][RT_B + 1];
-  __shared__ TACC Bs[RT_K][RT_B + 1];
+  __shared__ __align__(16) TACC As[RT_K][RT_LD];
+  __shared__ __align__(16) TACC Bs[RT_K][RT_LD];
   const TIN* P = static_cast<const TIN*>(a.P);
   const TIN* C = static_cast<const TIN*>(a.C);
   TOUT* D = static_cast<TOUT*>(a.D);
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int64_t nrt = (a.n + RT_B - 1) / RT_B, nct = (a.m + RT_B - 1) / RT_B;
+  // fp32 rows with dim % 4 == 0 on 16-byte boundaries stage 4 dimensions per load
+  bool vec = false;
+  if constexpr (std::is_same<TIN, float>::value)
+    vec = (a.dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(C)) % 16 == 0);
   for (int64_t tile = blockIdx.x; tile < nrt * nct; tile += gridDim.x) {
     const int64_t row0 = (tile / nct) * RT_B, col0 = (tile % nct) * RT_B;
     uint32_t fmask = 0;  // bit 4 r + c: element (row0 + 4 ty + r, col0 + 4 tx + c) is flagged
@@ -193,8 +211,31 @@ __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArg
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[r][c] = 0;
+    uint64_t acc2[4][2];  // fp32: (columns 2h, 2h + 1) of row r
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc2[r][0] = acc2[r][1] = 0ull;
     for (int k0 = 0; k0 < a.dim; k0 += RT_K) {
-      for (int t = threadIdx.x; t < RT_B * RT_K; t += 256) {
+      if constexpr (std::is_same<TIN, float>::value) {
+        if (vec) {
+          // thread t: dimensions k0 + 4 (t % 4) .. + 3 of row / center t / 4 (the dim
+          // is a multiple of 4, so a quad is either whole or past the end)
+          const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
+          const int64_t gi = row0 + rr, gj = col0 + rr;
+          const int gk = k0 + k4;
+          float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), cv = pv;
+          if (gk < a.dim) {
+            if (gi < a.n) pv = __ldg(reinterpret_cast<const float4*>(P + gi * a.dim + gk));
+            if (gj < a.m) cv = __ldg(reinterpret_cast<const float4*>(C + gj * a.dim + gk));
+          }
+          const float pq[4] = {pv.x, pv.y, pv.z, pv.w}, cq[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            As[k4 + q][rr] = static_cast<TACC>(pq[q]);
+            Bs[k4 + q][rr] = static_cast<TACC>(cq[q]);
+          }
+        }
+      }
+      for (int t = threadIdx.x; !vec && t < RT_B * RT_K; t += 256) {
         const int rr = t / RT_K, kk = t % RT_K;
         const int64_t gi = row0 + rr, gj = col0 + rr;
         const int gk = k0 + kk;
@@ -213,26 +254,54 @@ __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArg
       }
       __syncthreads();
       const int kend = min(RT_K, a.dim - k0);  // padded dimensions must not add a term
-      for (int kk = 0; kk < kend; ++kk) {
-        TACC av[4], bv[4];
+      if constexpr (REC == RC_F32) {
+        // fp32: columns in pairs on packed arithmetic, each lane the scalar __fsub_rn /
+        // __fmaf_rn of its pair in k order (the same bits as the loop below)
+        for (int kk = 0; kk < kend; ++kk) {
+          float av[4];
+          rt_lds4(&As[kk][ty * 4], av);
+          uint64_t b01, b23;
+          lds_f2x2(&Bs[kk][tx * 4], b01, b23);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) av[r] = As[kk][ty * 4 + r];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) bv[c] = Bs[kk][tx * 4 + c];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            if constexpr (REC == RC_F64) {
-              const double d = av[r] - bv[c];
-              acc[r][c] = fma(d, d, acc[r][c]);
-            } else {
-              const float d = __fsub_rn(av[r], bv[c]);
-              acc[r][c] = __fmaf_rn(d, d, acc[r][c]);
-            }
+          for (int r = 0; r < 4; ++r) {
+            const uint64_t ar = f2_pack(av[r], av[r]);
+            const uint64_t d01 = f2_sub(ar, b01), d23 = f2_sub(ar, b23);
+            acc2[r][0] = f2_fma(d01, d01, acc2[r][0]);
+            acc2[r][1] = f2_fma(d23, d23, acc2[r][1]);
           }
+        }
+      } else {
+        for (int kk = 0; kk < kend; ++kk) {
+          TACC av[4], bv[4];
+          rt_lds4(&As[kk][ty * 4], av);
+          rt_lds4(&Bs[kk][tx * 4], bv);
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if constexpr (REC == RC_F64) {
+                const double d = av[r] - bv[c];
+                acc[r][c] = fma(d, d, acc[r][c]);
+              } else {
+                const float d = __fsub_rn(av[r], bv[c]);
+                acc[r][c] = __fmaf_rn(d, d, acc[r][c]);
+              }
+            }
+        }
       }
       __syncthreads();
+    }
+    if constexpr (REC == RC_F32) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float lo, hi;
+        f2_unpack(acc2[r][0], lo, hi);
+        acc[r][0] = lo;
+        acc[r][1] = hi;
+        f2_unpack(acc2[r][1], lo, hi);
+        acc[r][2] = lo;
+        acc[r][3] = hi;
+      }
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r)
