@@ -40,7 +40,7 @@ constexpr int TC_EPI_WARPS = 8;  // two warps per TMEM lane quadrant, each ownin
 constexpr int TC_THREADS = (2 + TC_EPI_WARPS) * 32;
 constexpr int TC_A_BYTES = TC_BM * 128;  // one K-block of A: 128 rows x 128 bytes
 constexpr int TC_BAR_BYTES = 256;        // mbarriers, TMEM slot, abort flag
-constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 128 * 4 + 2 * 2 * 128 * 4;  // per-warp center norms + row merge
+constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 128 * 4;  // per-warp center norms
 
 enum TcMode { TM_ARGMIN = 0, TM_D_F32 = 1, TM_D_F16 = 2, TM_D_BF16 = 3 };
 
@@ -98,9 +98,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* accf = aempty + 2;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint64_t* mfull = drain + 1;  // row merge: upper-half warps have published their row minima
-  uint64_t* mdone = mfull + 1;  // row merge: lower-half warps have consumed them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* epi = reinterpret_cast<float*>(stage_base + NST * stage_bytes + TC_BAR_BYTES);
 
@@ -120,8 +118,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&acce[s], TC_EPI_WARPS);
     }
     mbar_init(drain, 1);
-    mbar_init(mfull, TC_EPI_WARPS / 2);
-    mbar_init(mdone, TC_EPI_WARPS / 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -244,8 +240,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row_local = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     float* cc_w = epi + ew * 128;        // this warp's columns: norms
-    float* mv = epi + TC_EPI_WARPS * 128;               // row merge: [2][128] minima
-    uint32_t* mi = reinterpret_cast<uint32_t*>(mv + 256);  //    [2][128] their columns
     const float K = a.K;
 
     // Center metadata of the next tile this warp will process is loaded one tile ahead
@@ -399,23 +393,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if constexpr (ARGMIN) {
         if (!ok) break;
-        // merge the two column halves of each row: upper half publishes, lower half combines
-        const uint32_t par = rt_i & 1u;
-        if (half == 1) {
-          if (rt_i > 0 && !mbar_wait(mdone, par ^ 1u, abort_flag, a.wait_ns)) { ok = false; break; }
-          mv[128 + row_local] = bestv;
-          mi[128 + row_local] = besti;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(mfull);
-        } else {
-          if (!mbar_wait(mfull, par, abort_flag, a.wait_ns)) { ok = false; break; }
-          const float ov = mv[128 + row_local];
-          const uint32_t oi = mi[128 + row_local];
-          __syncwarp();
-          if (lane == 0) mbar_arrive(mdone);
-          if (ov < bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
-          if (row_ok) a.row_key[i] = make_key(bestv, besti);
-        }
+        // the two column halves' minima of a row meet in its key: a 64-bit atomic min of
+        // (distance bits, original index), the smaller index among equal distances, with
+        // no barrier between the halves (the key starts at ~0)
+        if (row_ok) atomicMin(&a.row_key[i], make_key(bestv, besti));
       }
     }
     if (!ok) {
@@ -561,6 +542,11 @@ cudaError_t launch_tc(const DistJob& j) {
   int mode = TM_ARGMIN;
   if (!argmin) mode = (s->out == OUT_F16) ? TM_D_F16 : (s->out == OUT_BF16 ? TM_D_BF16 : TM_D_F32);
   const cudaStream_t st = j.stream;
+  if (argmin && j.row_key) {
+    // the two column halves fold their row minima into the key with an atomic min
+    const cudaError_t e = cudaMemsetAsync(j.row_key, 0xff, static_cast<size_t>(j.n) * sizeof(unsigned long long), st);
+    if (e != cudaSuccess) return e;
+  }
 
 #define TC_CASE1(KIND_, SR_, FL_, MODE_, REC_)                                                      \
   if (kind == KIND_ && s->sround == SR_ && s->flag == FL_ && mode == MODE_ &&                        \
