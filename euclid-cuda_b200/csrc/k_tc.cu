@@ -334,7 +334,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (row_ok) {
               if constexpr (MODE == TM_D_F32) {
                 float* drow = static_cast<float*>(a.D) + i * a.m + j0;
-                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
+                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 31u) == 0)) {
+                  // 32-byte stores: each lane writes whole sectors of its row
+#pragma unroll
+                  for (int e = 0; e < 32; e += 8)
+                    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(drow + e), "f"(v[e]),
+                                 "f"(v[e + 1]), "f"(v[e + 2]), "f"(v[e + 3]), "f"(v[e + 4]), "f"(v[e + 5]), "f"(v[e + 6]),
+                                 "f"(v[e + 7])
+                                 : "memory");
+                } else if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
 #pragma unroll
                   for (int e = 0; e < 32; e += 4)
                     *reinterpret_cast<float4*>(drow + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
@@ -354,7 +362,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                   else
                     hv[e] = __bfloat16_as_ushort(__float2bfloat16_rn(v[e]));
                 }
-                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
+                if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 31u) == 0)) {
+                  // 32-byte stores: each lane writes whole sectors of its row
+#pragma unroll
+                  for (int e = 0; e < 32; e += 16) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) w[q] = hv[e + 2 * q] | (static_cast<uint32_t>(hv[e + 2 * q + 1]) << 16);
+                    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(drow + e), "r"(w[0]),
+                                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                                 : "memory");
+                  }
+                } else if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(drow) & 15u) == 0)) {
 #pragma unroll
                   for (int e = 0; e < 32; e += 8) {
                     uint4 w;
