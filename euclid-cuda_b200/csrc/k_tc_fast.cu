@@ -607,15 +607,18 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
               if (cand && !store) a.redo[i] = 1;
               if (store)
                 region[pos] = (static_cast<unsigned long long>(i) << 32) | static_cast<unsigned long long>(jt + ch * 32);
-              float4* dst = reinterpret_cast<float4*>(region_s + pos * 32);
+              float* dst = region_s + pos * 32;  // 128-byte entries: 32-byte stores of whole sectors
 #pragma unroll
               for (int half = 0; half < 2; ++half) {
                 float raw[16];
                 tmem_ld16(tmem_acc + ch * 32 + half * 16, raw);  // whole warp: the load is .sync.aligned
                 if (store) {
 #pragma unroll
-                  for (int e = 0; e < 16; e += 4)
-                    dst[(half * 16 + e) / 4] = make_float4(raw[e], raw[e + 1], raw[e + 2], raw[e + 3]);
+                  for (int e = 0; e < 16; e += 8)
+                    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + half * 16 + e),
+                                 "f"(raw[e]), "f"(raw[e + 1]), "f"(raw[e + 2]), "f"(raw[e + 3]), "f"(raw[e + 4]),
+                                 "f"(raw[e + 5]), "f"(raw[e + 6]), "f"(raw[e + 7])
+                                 : "memory");
                 }
               }
             }
