@@ -292,19 +292,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t colmask = !row_ok ? 0u : (nvalid >= 32 ? 0xffffffffu : ((1u << nvalid) - 1u));
           {
             uint32_t fm = 0;
+            // two columns at a time on packed fp32: each lane is the scalar operation of
+            // exact_d and of the flag test (the same bits), the S rounding two at a time
+            const uint64_t pp2 = f2_pack(pp, pp), m2 = f2_pack(-2.f, -2.f), K2 = f2_pack(K, K);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float cc = cc_w[c0 + e];
-              const float d = exact_d<SROUND>(v[e], pp, cc);
-              bool fl = false;
-              if constexpr (FLAG == FL_F32) fl = d <= __fmul_rn(K, __fadd_rn(pp, cc));
-              if constexpr (ARGMIN) {
-                if (((colmask >> e) & 1u) && !fl) {
-                  if (d < bestv) { bestv = d; besti = static_cast<uint32_t>(j0 + e); }
-                }
+            for (int e = 0; e < 32; e += 2) {
+              uint64_t cc2;
+              asm volatile("ld.shared.u64 %0, [%1];" : "=l"(cc2) : "r"(smem_u32(cc_w + c0 + e)));
+              float s0 = v[e], s1 = v[e + 1];
+              if constexpr (SROUND == SR_F16) {
+                const float2 r = __half22float2(__floats2half2_rn(s0, s1));
+                s0 = r.x;
+                s1 = r.y;
+              } else if constexpr (SROUND == SR_BF16) {
+                const float2 r = __bfloat1622float2(__floats2bfloat162_rn(s0, s1));
+                s0 = r.x;
+                s1 = r.y;
               }
-              if (fl) fm |= 1u << e;
-              v[e] = d;
+              float d2[2];
+              f2_unpack(f2_add(f2_fma(m2, f2_pack(s0, s1), pp2), cc2), d2[0], d2[1]);
+              float t2[2] = {0.f, 0.f};
+              if constexpr (FLAG == FL_F32) f2_unpack(f2_mul(K2, f2_add(pp2, cc2)), t2[0], t2[1]);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                const float d = fmaxf(d2[q], 0.f);
+                bool fl = false;
+                if constexpr (FLAG == FL_F32) fl = d <= t2[q];
+                if constexpr (ARGMIN) {
+                  if (((colmask >> (e + q)) & 1u) && !fl) {
+                    if (d < bestv) { bestv = d; besti = static_cast<uint32_t>(j0 + e + q); }
+                  }
+                }
+                if (fl) fm |= 1u << (e + q);
+                v[e + q] = d;
+              }
             }
             fm &= colmask;
             if constexpr (FLAG == FL_F32) {
