@@ -220,13 +220,13 @@ static int64_t priv_blocks(int64_t n) {
   return nb < 1 ? 1 : (nb > 2048 ? 2048 : nb);
 }
 
-// Each warp reduces SEG label-sorted rows; NPL = dims per lane (ceil(dim/32)).
+// Each warp reduces SEG label-sorted rows (segsum_rows: fewer when the rows are few, so
+// the grid still fills the SMs); NPL = dims per lane (ceil(dim/32)).
 template <typename TX, int NPL>
 __global__ void __launch_bounds__(256) segsum_kernel(const TX* __restrict__ X, int dim, int k,
                                                      const unsigned long long* __restrict__ offs,
                                                      const unsigned int* __restrict__ perm,
-                                                     double* __restrict__ stats) {
-  constexpr int SEG = 1024;
+                                                     double* __restrict__ stats, const int SEG) {
   const int64_t total = static_cast<int64_t>(offs[k]);  // rows with a label in [0, k)
   const int lane = threadIdx.x & 31;
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -294,8 +294,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) segsum_h_kernel(const float* __restrict__ X, int dim, int k,
                                                        const unsigned long long* __restrict__ offs,
                                                        const unsigned int* __restrict__ perm,
-                                                       double* __restrict__ stats) {
-  constexpr int SEG = 1024;
+                                                       double* __restrict__ stats, const int SEG) {
   constexpr int RB = 4;
   const int64_t total = static_cast<int64_t>(offs[k]);
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
@@ -426,23 +425,28 @@ static cudaError_t stats_t(const TX* X, const TL* labels, int64_t n, int dim, in
     scatter_kernel<TL><<<blocks, 256, 0, st>>>(labels, n, k, cursor, perm);
   }
   // rows with a valid label = offs[k] <= n; the grid covers n positions and each warp
-  // clamps to offs[k] on the device.
-  const int64_t warps = (n + 1023) / 1024;
+  // clamps to offs[k] on the device.  A warp walks its rows one dependent round trip
+  // (label-sorted position, then row) at a time, so a segment of 1024 rows leaves a
+  // small n with few warps per SM: the segment shrinks (to 128 at least) until about 64
+  // warps per SM cover the rows.
+  int seg = 1024;
+  while (seg > 128 && (n + seg - 1) / seg < static_cast<int64_t>(num_sms()) * 64) seg >>= 1;
+  const int64_t warps = (n + seg - 1) / seg;
   const int64_t sblocks = (warps + 7) / 8;
   if constexpr (std::is_same<TX, float>::value) {
     if (dim % 64 == 0 && dim <= 256 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0) {
       const unsigned b = static_cast<unsigned>(sblocks);
-      if (dim == 64) segsum_h_kernel<1><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
-      else if (dim == 128) segsum_h_kernel<2><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
-      else if (dim == 192) segsum_h_kernel<3><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
-      else segsum_h_kernel<4><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats);
+      if (dim == 64) segsum_h_kernel<1><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats, seg);
+      else if (dim == 128) segsum_h_kernel<2><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats, seg);
+      else if (dim == 192) segsum_h_kernel<3><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats, seg);
+      else segsum_h_kernel<4><<<b, 256, 0, st>>>(X, dim, k, offs, perm, stats, seg);
       return cudaGetLastError();
     }
   }
   const int npl = (dim + 31) / 32;
 #define SEG(NPL_)                                                                                        \
   if (npl <= NPL_) {                                                                                     \
-    segsum_kernel<TX, NPL_><<<static_cast<unsigned>(sblocks), 256, 0, st>>>(X, dim, k, offs, perm, stats); \
+    segsum_kernel<TX, NPL_><<<static_cast<unsigned>(sblocks), 256, 0, st>>>(X, dim, k, offs, perm, stats, seg); \
     return cudaGetLastError();                                                                           \
   }
   SEG(1) SEG(2) SEG(4) SEG(8) SEG(16) SEG(32)
