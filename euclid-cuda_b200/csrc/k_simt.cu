@@ -372,6 +372,28 @@ constexpr int THIN_MAX_CF = 10240;  // m * padded dim floats of centers in share
 constexpr int THIN_RB = 128;       // rows per chunk
 enum ThinMode { THIN_DIRECT = 0, THIN_FORM = 1 };
 
+// DIM consecutive staged values of one row (16-byte loads where DIM allows)
+template <int DIM>
+__device__ __forceinline__ void ld_row(const float* src, float* v) {
+  if constexpr (DIM % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < DIM; k += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(src + k);
+      v[k] = x.x;
+      v[k + 1] = x.y;
+      v[k + 2] = x.z;
+      v[k + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < DIM; k += 2) {
+      const float2 x = *reinterpret_cast<const float2*>(src + k);
+      v[k] = x.x;
+      v[k + 1] = x.y;
+    }
+  }
+}
+
 // a flagged pair's direct distance from the staged row and the k-major center column
 // (out of line: it is rare, and keeps the common path's registers free)
 template <int DIM, int REC>
@@ -531,6 +553,152 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
   }
 }
 
+// thin_d_kernel with the centers in registers (padded dim 8; the template takes 2 and 4
+// too, where thin_d_kernel measured as fast or faster).  In thin_d_kernel every k step
+// reads its four center values from shared memory for the 8 outputs a lane forms with
+// them, and those loads fill the L1 data pipe before HBM is saturated.  Here the launch
+// is cut into 64-column slices of D (block b takes slice b mod S of its chunks): lane l
+// of each half-warp owns the columns 64 s + 4 l .. + 3 for the whole launch, with their
+// DIM x 4 values as packed pairs (and their 4 norms) in registers, so a k step reads
+// nothing from shared memory.  Warp w forms rows 16 w .. 16 w + 15 of each chunk, the two
+// half-warps alternating (a warp's 16-byte stores cover two consecutive rows); lane l < 16
+// forms the fmaf norm of row 16 w + l once per chunk and hands it on by shuffle.  The
+// arithmetic is thin_d_kernel's, operation for operation, so D is bit-identical.
+template <int DIM, int REC>
+__device__ __noinline__ float thin_recompute_g(const float* prow, const float* __restrict__ crow, int dim) {
+  DirectAcc<REC> r;
+#pragma unroll
+  for (int k = 0; k < DIM; ++k) r.add(prow[k], k < dim ? crow[k] : 0.f);
+  return static_cast<float>(r.get());
+}
+
+template <int DIM, int MODE, bool FLAG, int REC>
+__global__ void __launch_bounds__(256, 3) thin_dr_kernel(const float* __restrict__ P, const float* __restrict__ C,
+                                                         const float* __restrict__ cc, int64_t n, int m, int dim,
+                                                         float kf, float* __restrict__ D,
+                                                         unsigned long long* __restrict__ count, int slices) {
+  static_assert(DIM == 2 || DIM == 4 || DIM == 8, "register centers: dim <= 8");
+  constexpr int PER = THIN_RB * DIM / 256;
+  __shared__ __align__(16) float ps[THIN_RB * DIM];
+  const int lane = threadIdx.x & 31, hl = lane & 15, h = lane >> 4, w = threadIdx.x >> 5;
+  const int slice = static_cast<int>(blockIdx.x % slices);
+  const int64_t cb = blockIdx.x / slices, nb = gridDim.x / slices;
+  const int j0 = slice * 64 + hl * 4;
+  const bool colok = j0 < m;  // m is a multiple of 4: a lane's columns are all in or all out
+  uint64_t c01[DIM], c23[DIM];
+#pragma unroll
+  for (int k = 0; k < DIM; ++k) {
+    float a[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) a[c] = colok && k < dim ? __ldg(C + static_cast<int64_t>(j0 + c) * dim + k) : 0.f;
+    c01[k] = f2_pack(a[0], a[1]);
+    c23[k] = f2_pack(a[2], a[3]);
+  }
+  uint64_t cc2[2] = {0ull, 0ull};
+  if constexpr (MODE == THIN_FORM) {
+    if (colok) {
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(cc + j0));
+      cc2[0] = f2_pack(c4.x, c4.y);
+      cc2[1] = f2_pack(c4.z, c4.w);
+    }
+  }
+  for (int e = threadIdx.x; e < THIN_RB * DIM; e += blockDim.x) ps[e] = 0.f;  // padding stays zero
+  const int64_t nchunk = (n + THIN_RB - 1) / THIN_RB;
+  const int cvals = THIN_RB * dim;
+  float pre[PER];
+  auto load = [&](int64_t ch) {
+    const int64_t base = ch * THIN_RB * dim, lim = n * dim;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = threadIdx.x + u * 256;
+      pre[u] = (ch < nchunk && e < cvals && base + e < lim) ? __ldg(P + base + e) : 0.f;
+    }
+  };
+  int64_t ch = cb;
+  load(ch);
+  unsigned int flagged = 0;
+  for (; ch < nchunk; ch += nb) {
+    __syncthreads();
+    if (dim == DIM) {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) ps[threadIdx.x + u * 256] = pre[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int e = threadIdx.x + u * 256;
+        if (e < cvals) ps[(e / dim) * DIM + e % dim] = pre[u];
+      }
+    }
+    __syncthreads();
+    load(ch + nb);
+    const int64_t row0 = ch * THIN_RB;
+    float q = 0.f;  // norm of row 16 w + (lane & 15), fmaf in k order
+    if constexpr (MODE == THIN_FORM) {
+      float pv[DIM];
+      ld_row<DIM>(ps + (16 * w + hl) * DIM, pv);
+#pragma unroll
+      for (int k = 0; k < DIM; ++k) q = __fmaf_rn(pv[k], pv[k], q);
+    }
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int rt = 16 * w + 2 * i + h;
+      float pp = 0.f;
+      if constexpr (MODE == THIN_FORM) pp = __shfl_sync(0xffffffffu, q, 2 * i + h);
+      if (!colok || row0 + rt >= n) continue;
+      float pv[DIM];
+      ld_row<DIM>(ps + rt * DIM, pv);
+      uint64_t acc0 = 0ull, acc1 = 0ull;
+#pragma unroll
+      for (int k = 0; k < DIM; ++k) {
+        const uint64_t pk = f2_pack(pv[k], pv[k]);
+        if constexpr (MODE == THIN_DIRECT) {
+          const uint64_t d01 = f2_sub(pk, c01[k]), d23 = f2_sub(pk, c23[k]);
+          acc0 = f2_fma(d01, d01, acc0);
+          acc1 = f2_fma(d23, d23, acc1);
+        } else {
+          acc0 = f2_fma(pk, c01[k], acc0);
+          acc1 = f2_fma(pk, c23[k], acc1);
+        }
+      }
+      float v[4], t[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (MODE == THIN_DIRECT) {
+        f2_unpack(acc0, v[0], v[1]);
+        f2_unpack(acc1, v[2], v[3]);
+      } else {
+        // d = max((pp - 2 s) + cc, 0) and the test threshold K (pp + cc), per lane
+        const uint64_t pp2 = f2_pack(pp, pp), m2 = f2_pack(-2.f, -2.f);
+        f2_unpack(f2_add(f2_fma(m2, acc0, pp2), cc2[0]), v[0], v[1]);
+        f2_unpack(f2_add(f2_fma(m2, acc1, pp2), cc2[1]), v[2], v[3]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = fmaxf(v[c], 0.f);
+        if constexpr (FLAG) {
+          const uint64_t k2 = f2_pack(kf, kf);
+          f2_unpack(f2_mul(k2, f2_add(pp2, cc2[0])), t[0], t[1]);
+          f2_unpack(f2_mul(k2, f2_add(pp2, cc2[1])), t[2], t[3]);
+        }
+      }
+      float* drow = D + (row0 + rt) * m + j0;
+      *reinterpret_cast<float4*>(drow) = make_float4(v[0], v[1], v[2], v[3]);
+      if constexpr (FLAG) {
+        if ((v[0] <= t[0]) | (v[1] <= t[1]) | (v[2] <= t[2]) | (v[3] <= t[3])) {
+          // flagged pairs (rare): their direct distance replaces the stored value
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (v[c] <= t[c]) {
+              drow[c] = thin_recompute_g<DIM, REC>(ps + rt * DIM, C + static_cast<int64_t>(j0 + c) * dim, dim);
+              ++flagged;
+            }
+          }
+        }
+      }
+    }
+  }
+  if constexpr (FLAG) {
+    const unsigned int tot = __reduce_add_sync(0xffffffffu, flagged);
+    if (lane == 0 && tot) atomicAdd(count, static_cast<unsigned long long>(tot));
+  }
+}
+
 // Whether thin_d_kernel serves this D-mode call: fp32 in and out, dim <= 16, m a multiple
 // of 4 with the centers in 40 KB of shared memory, D 16-byte aligned.
 bool thin_d_ok(const OpSpec* s, int64_t m, int dim, const void* D) {
@@ -559,6 +727,22 @@ cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const v
   timing_begin(st, "thin_d_kernel");
   const int pd = dim <= 2 ? 2 : (dim <= 4 ? 4 : (dim <= 8 ? 8 : 16));
   const size_t smem = static_cast<size_t>(m) * pd * 4;
+  // padded dim 8: centers in registers, one wave of 3 blocks per SM over the column slices
+  // (at dim <= 4 the shared-memory form measured as fast or faster)
+  const int slices = static_cast<int>((m + 63) / 64);
+  const int64_t nbx = std::max<int64_t>(1, std::min<int64_t>(nchunk, (num_sms() * 3 + slices - 1) / slices));
+  const int rblocks = static_cast<int>(nbx * slices);
+#define THIN_RGO(DIM_)                                                                                        \
+  if (pd == DIM_) {                                                                                           \
+    if (s->gemm == G_DIRECT)                                                                                  \
+      thin_dr_kernel<DIM_, THIN_DIRECT, false, RC_NONE><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices); \
+    else if (s->flag == FL_NONE)                                                                              \
+      thin_dr_kernel<DIM_, THIN_FORM, false, RC_NONE><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);   \
+    else if (s->rec == RC_F32)                                                                                \
+      thin_dr_kernel<DIM_, THIN_FORM, true, RC_F32><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);     \
+    else                                                                                                      \
+      thin_dr_kernel<DIM_, THIN_FORM, true, RC_F64><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);     \
+  }
 #define THIN_GO(DIM_)                                                                                         \
   if (pd == DIM_) {                                                                                           \
     if (s->gemm == G_DIRECT)                                                                                  \
@@ -572,9 +756,10 @@ cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const v
   }
   THIN_GO(2)
   THIN_GO(4)
-  THIN_GO(8)
+  THIN_RGO(8)
   THIN_GO(16)
 #undef THIN_GO
+#undef THIN_RGO
   cudaError_t e = cudaGetLastError();
   timing_end(st);
   return e;
