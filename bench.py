@@ -559,9 +559,14 @@ def bench_lloyd(ctx):
 
 def lloyd_phases(km, X, C, st, torch):
     """CUDA-event time of each phase of one iteration on this rank (after the timed
-    region): assignment (all of euc_argmin), center statistics, all-reduce, new centers."""
+    region): assignment (all of euc_argmin), center statistics, all-reduce, new centers.
+    A device-side sleep (about 2 ms) ahead of the first event lets the host queue every
+    launch of the iteration first, so each phase is device time, as in the timed loop, and
+    not the host's launch latency of an idle GPU."""
     import torch.distributed as dist
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(4_000_000)
     ev[0].record(st)
     labels, _ = km.assign(X, C)
     ev[1].record(st)

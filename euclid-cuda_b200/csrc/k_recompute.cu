@@ -330,7 +330,17 @@ static cudaError_t go_rec(const DistJob& j) {
   a.kf = j.kf;
   a.kd = j.kd;
   if constexpr (ARGMIN && std::is_same<TIN, float>::value) {
-    recompute_argmin_rows_kernel<REC><<<num_sms() * 8, RW_WARPS * 32, 0, j.stream>>>(a);
+    // one full wave: the kernel walks the list grid-stride, and a second, partial wave
+    // of equal-work blocks would leave most SMs idle at the end
+    static int per_sm = 0;
+    if (per_sm == 0) {
+      int v = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, recompute_argmin_rows_kernel<REC>, RW_WARPS * 32, 0) !=
+              cudaSuccess || v < 1)
+        v = 4;
+      per_sm = v;
+    }
+    recompute_argmin_rows_kernel<REC><<<num_sms() * per_sm, RW_WARPS * 32, 0, j.stream>>>(a);
     return cudaGetLastError();
   }
   const int blocks = num_sms() * 8;
