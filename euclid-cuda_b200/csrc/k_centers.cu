@@ -161,7 +161,15 @@ __global__ void priv_slice_sums_kernel(const unsigned int* __restrict__ T, int n
   const int per = (nb + kPrivSlices - 1) / kPrivSlices;
   const int b0 = sl * per, b1 = min(nb, b0 + per);
   unsigned int t = 0u;
-  for (int b = b0; b < b1; ++b) t += T[static_cast<int64_t>(b) * k + c];
+  int b = b0;
+  for (; b + 8 <= b1; b += 8) {  // eight independent loads in flight
+    unsigned int v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = T[static_cast<int64_t>(b + u) * k + c];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t += v[u];
+  }
+  for (; b < b1; ++b) t += T[static_cast<int64_t>(b) * k + c];
   PS[static_cast<int64_t>(sl) * k + c] = t;
 }
 
@@ -188,7 +196,18 @@ __global__ void priv_offsets_kernel(unsigned int* __restrict__ T, int nb, int k,
   const int per = (nb + kPrivSlices - 1) / kPrivSlices;
   const int b0 = sl * per, b1 = min(nb, b0 + per);
   unsigned int run = static_cast<unsigned int>(offs[c]) + PS[static_cast<int64_t>(sl) * k + c];
-  for (int b = b0; b < b1; ++b) {
+  int b = b0;
+  for (; b + 8 <= b1; b += 8) {  // eight loads issued before the stores that follow them
+    unsigned int v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = T[static_cast<int64_t>(b + u) * k + c];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      T[static_cast<int64_t>(b + u) * k + c] = run;
+      run += v[u];
+    }
+  }
+  for (; b < b1; ++b) {
     const int64_t at = static_cast<int64_t>(b) * k + c;
     const unsigned int t = T[at];
     T[at] = run;
