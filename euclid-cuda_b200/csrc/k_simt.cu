@@ -632,6 +632,8 @@ __global__ void __launch_bounds__(256, 3) thin_dr_kernel(const float* __restrict
     __syncthreads();
     load(ch + nb);
     const int64_t row0 = ch * THIN_RB;
+    const int nrows = static_cast<int>(n - row0 < THIN_RB ? n - row0 : THIN_RB);  // rows of this chunk
+    float* const dbase = D + row0 * m + j0;
     float q = 0.f;  // norm of row 16 w + (lane & 15), fmaf in k order
     if constexpr (MODE == THIN_FORM) {
       float pv[DIM];
@@ -644,7 +646,9 @@ __global__ void __launch_bounds__(256, 3) thin_dr_kernel(const float* __restrict
       const int rt = 16 * w + 2 * i + h;
       float pp = 0.f;
       if constexpr (MODE == THIN_FORM) pp = __shfl_sync(0xffffffffu, q, 2 * i + h);
-      if (!colok || row0 + rt >= n) continue;
+      // (a 32-bit row test and a row pointer off the chunk's base measured 6 % faster for
+      // the form and 3 % slower for the direct sum, which keeps the 64-bit forms)
+      if (!colok || (MODE == THIN_FORM ? rt >= nrows : row0 + rt >= n)) continue;
       float pv[DIM];
       ld_row<DIM>(ps + rt * DIM, pv);
       uint64_t acc0 = 0ull, acc1 = 0ull;
@@ -677,7 +681,7 @@ __global__ void __launch_bounds__(256, 3) thin_dr_kernel(const float* __restrict
           f2_unpack(f2_mul(k2, f2_add(pp2, cc2[1])), t[2], t[3]);
         }
       }
-      float* drow = D + (row0 + rt) * m + j0;
+      float* drow = MODE == THIN_FORM ? dbase + static_cast<int64_t>(rt) * m : D + (row0 + rt) * m + j0;
       *reinterpret_cast<float4*>(drow) = make_float4(v[0], v[1], v[2], v[3]);
       if constexpr (FLAG) {
         if ((v[0] <= t[0]) | (v[1] <= t[1]) | (v[2] <= t[2]) | (v[3] <= t[3])) {
