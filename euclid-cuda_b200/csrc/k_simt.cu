@@ -448,6 +448,8 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
     __syncthreads();
     load(ch + gridDim.x);
     const int64_t row0 = ch * THIN_RB;
+    const int nrows = static_cast<int>(n - row0 < THIN_RB ? n - row0 : THIN_RB);
+    float* const dbase = D + row0 * m;
 #pragma unroll 1
     for (int rr = hw; rr < THIN_RB; rr += 16 * R) {
       // R rows at a time (rr, rr + 16, ...): the centers' values are read once for all
@@ -456,7 +458,7 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
 #pragma unroll
       for (int t = 0; t < R; ++t) {
         const int rt = rr + 16 * t;
-        ok[t] = row0 + rt < n;
+        ok[t] = rt < nrows;
 #pragma unroll
         for (int k = 0; k < DIM; k += 2) {
           const float2 v = *reinterpret_cast<const float2*>(ps + rt * DIM + k);
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
               }
             }
           }
-          *reinterpret_cast<float4*>(D + (row0 + rt) * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(dbase + static_cast<int64_t>(rt) * m + j0) = make_float4(v[0], v[1], v[2], v[3]);
         }
         if constexpr (FLAG) {
           // flagged pairs (rare): their direct distance replaces the stored value
@@ -540,7 +542,7 @@ __global__ void __launch_bounds__(256, 4) thin_d_kernel(const float* __restrict_
             const int b = __ffs(fmask) - 1;
             fmask &= fmask - 1u;
             const int rt = rr + 16 * (b >> 2), c = b & 3;
-            D[(row0 + rt) * m + j0 + c] = thin_recompute<DIM, REC>(ps + rt * DIM, csT + j0 + c, m);
+            dbase[static_cast<int64_t>(rt) * m + j0 + c] = thin_recompute<DIM, REC>(ps + rt * DIM, csT + j0 + c, m);
             ++flagged;
           }
         }
