@@ -446,10 +446,10 @@ static cudaError_t stats_t(const TX* X, const TL* labels, int64_t n, int dim, in
   // rows with a valid label = offs[k] <= n; the grid covers n positions and each warp
   // clamps to offs[k] on the device.  A warp walks its rows one dependent round trip
   // (label-sorted position, then row) at a time, so a segment of 1024 rows leaves a
-  // small n with few warps per SM: the segment shrinks (to 128 at least) until about 64
+  // small n with few warps per SM: the segment shrinks (to 256 at least) until about 64
   // warps per SM cover the rows.
   int seg = 1024;
-  while (seg > 128 && (n + seg - 1) / seg < static_cast<int64_t>(num_sms()) * 64) seg >>= 1;
+  while (seg > 256 && (n + seg - 1) / seg < static_cast<int64_t>(num_sms()) * 64) seg >>= 1;
   const int64_t warps = (n + seg - 1) / seg;
   const int64_t sblocks = (warps + 7) / 8;
   if constexpr (std::is_same<TX, float>::value) {
