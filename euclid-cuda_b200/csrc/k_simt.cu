@@ -705,6 +705,131 @@ __global__ void __launch_bounds__(256, 3) thin_dr_kernel(const float* __restrict
   }
 }
 
+// thin_dr_kernel's form for padded dim 16, where four columns' 16 values would take 64
+// registers: lane l of a warp owns columns 64 s + 2 l, + 1 of its slice (16 packed pairs,
+// 32 registers) and the warp forms one row of the slice at a time, the 32 lanes' 8-byte
+// stores covering the row's 256 bytes.  Warp w takes rows 16 w .. 16 w + 15 of each
+// chunk; lane l < 16 forms the fmaf norm of row 16 w + l once per chunk.  The
+// arithmetic is thin_d_kernel's, operation for operation.
+template <int DIM, int MODE, bool FLAG, int REC>
+__global__ void __launch_bounds__(256, 3) thin_dr2_kernel(const float* __restrict__ P, const float* __restrict__ C,
+                                                          const float* __restrict__ cc, int64_t n, int m, int dim,
+                                                          float kf, float* __restrict__ D,
+                                                          unsigned long long* __restrict__ count, int slices) {
+  static_assert(DIM == 16, "two columns a lane: dim 16");
+  constexpr int PER = THIN_RB * DIM / 256;
+  __shared__ __align__(16) float ps[THIN_RB * DIM];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int slice = static_cast<int>(blockIdx.x % slices);
+  const int64_t cb = blockIdx.x / slices, nb = gridDim.x / slices;
+  const int j0 = slice * 64 + lane * 2;
+  const bool colok = j0 < m;  // m is a multiple of 4: both columns are in or both out
+  uint64_t c01[DIM];
+#pragma unroll
+  for (int k = 0; k < DIM; ++k) {
+    const float a0 = colok && k < dim ? __ldg(C + static_cast<int64_t>(j0) * dim + k) : 0.f;
+    const float a1 = colok && k < dim ? __ldg(C + static_cast<int64_t>(j0 + 1) * dim + k) : 0.f;
+    c01[k] = f2_pack(a0, a1);
+  }
+  uint64_t cc2 = 0ull;
+  if constexpr (MODE == THIN_FORM) {
+    if (colok) {
+      const float2 c2 = __ldg(reinterpret_cast<const float2*>(cc + j0));
+      cc2 = f2_pack(c2.x, c2.y);
+    }
+  }
+  for (int e = threadIdx.x; e < THIN_RB * DIM; e += blockDim.x) ps[e] = 0.f;  // padding stays zero
+  const int64_t nchunk = (n + THIN_RB - 1) / THIN_RB;
+  const int cvals = THIN_RB * dim;
+  float pre[PER];
+  auto load = [&](int64_t ch) {
+    const int64_t base = ch * THIN_RB * dim, lim = n * dim;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = threadIdx.x + u * 256;
+      pre[u] = (ch < nchunk && e < cvals && base + e < lim) ? __ldg(P + base + e) : 0.f;
+    }
+  };
+  int64_t ch = cb;
+  load(ch);
+  unsigned int flagged = 0;
+  for (; ch < nchunk; ch += nb) {
+    __syncthreads();
+    if (dim == DIM) {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) ps[threadIdx.x + u * 256] = pre[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int e = threadIdx.x + u * 256;
+        if (e < cvals) ps[(e / dim) * DIM + e % dim] = pre[u];
+      }
+    }
+    __syncthreads();
+    load(ch + nb);
+    const int64_t row0 = ch * THIN_RB;
+    const int nrows = static_cast<int>(n - row0 < THIN_RB ? n - row0 : THIN_RB);  // rows of this chunk
+    float* const dbase = D + row0 * m + j0;
+    float q = 0.f;  // norm of row 16 w + (lane & 15), fmaf in k order
+    if constexpr (MODE == THIN_FORM) {
+      float pv[DIM];
+      ld_row<DIM>(ps + (16 * w + (lane & 15)) * DIM, pv);
+#pragma unroll
+      for (int k = 0; k < DIM; ++k) q = __fmaf_rn(pv[k], pv[k], q);
+    }
+#pragma unroll 2
+    for (int i = 0; i < 16; ++i) {
+      const int rt = 16 * w + i;
+      float pp = 0.f;
+      if constexpr (MODE == THIN_FORM) pp = __shfl_sync(0xffffffffu, q, i);
+      if (!colok || rt >= nrows) continue;
+      float pv[DIM];
+      ld_row<DIM>(ps + rt * DIM, pv);
+      uint64_t acc = 0ull;
+#pragma unroll
+      for (int k = 0; k < DIM; ++k) {
+        const uint64_t pk = f2_pack(pv[k], pv[k]);
+        if constexpr (MODE == THIN_DIRECT) {
+          const uint64_t d01 = f2_sub(pk, c01[k]);
+          acc = f2_fma(d01, d01, acc);
+        } else {
+          acc = f2_fma(pk, c01[k], acc);
+        }
+      }
+      float v0, v1, t0 = 0.f, t1 = 0.f;
+      if constexpr (MODE == THIN_DIRECT) {
+        f2_unpack(acc, v0, v1);
+      } else {
+        // d = max((pp - 2 s) + cc, 0) and the test threshold K (pp + cc), per lane
+        const uint64_t pp2 = f2_pack(pp, pp);
+        f2_unpack(f2_add(f2_fma(f2_pack(-2.f, -2.f), acc, pp2), cc2), v0, v1);
+        v0 = fmaxf(v0, 0.f);
+        v1 = fmaxf(v1, 0.f);
+        if constexpr (FLAG) f2_unpack(f2_mul(f2_pack(kf, kf), f2_add(pp2, cc2)), t0, t1);
+      }
+      float* drow = dbase + static_cast<int64_t>(rt) * m;
+      *reinterpret_cast<float2*>(drow) = make_float2(v0, v1);
+      if constexpr (FLAG) {
+        if ((v0 <= t0) | (v1 <= t1)) {
+          // flagged pairs (rare): their direct distance replaces the stored value
+          if (v0 <= t0) {
+            drow[0] = thin_recompute_g<DIM, REC>(ps + rt * DIM, C + static_cast<int64_t>(j0) * dim, dim);
+            ++flagged;
+          }
+          if (v1 <= t1) {
+            drow[1] = thin_recompute_g<DIM, REC>(ps + rt * DIM, C + static_cast<int64_t>(j0 + 1) * dim, dim);
+            ++flagged;
+          }
+        }
+      }
+    }
+  }
+  if constexpr (FLAG) {
+    const unsigned int tot = __reduce_add_sync(0xffffffffu, flagged);
+    if (lane == 0 && tot) atomicAdd(count, static_cast<unsigned long long>(tot));
+  }
+}
+
 // Whether thin_d_kernel serves this D-mode call: fp32 in and out, dim <= 16, m a multiple
 // of 4 with the centers in 40 KB of shared memory, D 16-byte aligned.
 bool thin_d_ok(const OpSpec* s, int64_t m, int dim, const void* D) {
@@ -749,6 +874,17 @@ cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const v
     else                                                                                                      \
       thin_dr_kernel<DIM_, THIN_FORM, true, RC_F64><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);     \
   }
+#define THIN_R2GO(DIM_)                                                                                       \
+  if (pd == DIM_) {                                                                                           \
+    if (s->gemm == G_DIRECT)                                                                                  \
+      thin_dr2_kernel<DIM_, THIN_DIRECT, false, RC_NONE><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices); \
+    else if (s->flag == FL_NONE)                                                                              \
+      thin_dr2_kernel<DIM_, THIN_FORM, false, RC_NONE><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);   \
+    else if (s->rec == RC_F32)                                                                                \
+      thin_dr2_kernel<DIM_, THIN_FORM, true, RC_F32><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);     \
+    else                                                                                                      \
+      thin_dr2_kernel<DIM_, THIN_FORM, true, RC_F64><<<rblocks, 256, 0, st>>>(Pf, Cf, ccf, n, mi, dim, kf, Df, count, slices);     \
+  }
 #define THIN_GO(DIM_)                                                                                         \
   if (pd == DIM_) {                                                                                           \
     if (s->gemm == G_DIRECT)                                                                                  \
@@ -763,9 +899,10 @@ cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const v
   THIN_GO(2)
   THIN_GO(4)
   THIN_RGO(8)
-  THIN_GO(16)
+  THIN_R2GO(16)
 #undef THIN_GO
 #undef THIN_RGO
+#undef THIN_R2GO
   cudaError_t e = cudaGetLastError();
   timing_end(st);
   return e;

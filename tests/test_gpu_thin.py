@@ -20,10 +20,11 @@ def cuda(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
-# dims 5..8 pad to 8 (centers held in registers, 64-column slices: 68 and 200 columns end
-# in a partial slice), the others to 2, 4, 16 (centers in shared memory)
+# dims 5..8 pad to 8 and 9..16 to 16 (centers held in registers, 64-column slices: 12,
+# 68 and 200 columns end in a partial slice), the others to 2 and 4 (centers in shared
+# memory)
 SHAPES = [(1, 4, 1), (1000, 64, 2), (4097, 64, 3), (777, 64, 4), (2048, 200, 8), (513, 12, 16), (300, 1024, 8),
-          (1500, 68, 6), (129, 8, 5), (3000, 64, 7)]
+          (1500, 68, 6), (129, 8, 5), (3000, 64, 7), (2000, 64, 16), (777, 200, 12), (301, 68, 9)]
 
 
 def data(n, m, d, seed):
