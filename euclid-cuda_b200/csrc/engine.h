@@ -197,6 +197,9 @@ cudaError_t launch_thin_d(const OpSpec* s, const void* P, const void* C, const v
 cudaError_t launch_direct(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
                           void* D, cudaStream_t st);
 cudaError_t launch_recompute(const DistJob& j);
+// every pair flagged, few centers: first-index argmin of the direct distances of all pairs
+cudaError_t launch_dense_argmin(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
+                                int64_t* labels, int32_t* labels32, float* md, cudaStream_t st);
 cudaError_t launch_keys_to_labels(const unsigned long long* keys, int64_t n, int64_t* labels, int32_t* labels32,
                                   float* mind, cudaStream_t st);
 cudaError_t launch_f64_to_labels(const long long* idx, int64_t n, int64_t* labels, int32_t* labels32,

@@ -312,6 +312,168 @@ __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArg
   }
 }
 
+// All-flagged argmin over few centers: every pair is flagged (the range test of the
+// all-flagged route), so the label is the first index of the smallest direct distance
+// over all m centers.  With few centers the certified screen's bounds separate
+// nothing, and it would evaluate every group after two screens; here each block takes
+// 64-row tiles and sweeps all center tiles with recompute_dense_tiled_kernel's staging
+// and arithmetic (fp32: packed lanes, each the scalar __fsub_rn / __fmaf_rn in k order;
+// fp64: fma in k order), keeping per thread the first-index minimum of its 4 rows over
+// its columns in increasing order; the 16 threads of a row then take the (distance,
+// index) minimum by shuffle.  Distances are compared as the operator stores them,
+// rounded to fp32 (the certified path's keys do the same), so fp64 values that round
+// alike tie and the first index wins; min_dist is that fp32 value.
+template <int REC>
+__global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restrict__ P, const float* __restrict__ C,
+                                                           int64_t n, int64_t m, int dim, int64_t* __restrict__ labels,
+                                                           int32_t* __restrict__ labels32, float* __restrict__ md) {
+  using TACC = typename std::conditional<REC == RC_F64, double, float>::type;
+  __shared__ __align__(16) TACC As[RT_K][RT_LD];
+  __shared__ __align__(16) TACC Bs[RT_K][RT_LD];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t nrt = (n + RT_B - 1) / RT_B, nct = (m + RT_B - 1) / RT_B;
+  const bool vec = (dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(C)) % 16 == 0);
+  for (int64_t rtile = blockIdx.x; rtile < nrt; rtile += gridDim.x) {
+    const int64_t row0 = rtile * RT_B;
+    float bv[4];
+    uint32_t bj[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      bv[r] = __int_as_float(0x7f800000);
+      bj[r] = 0xffffffffu;
+    }
+    for (int64_t ct = 0; ct < nct; ++ct) {
+      const int64_t col0 = ct * RT_B;
+      TACC acc[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0;
+      uint64_t acc2[4][2];  // fp32: (columns 2h, 2h + 1) of row r
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc2[r][0] = acc2[r][1] = 0ull;
+      for (int k0 = 0; k0 < dim; k0 += RT_K) {
+        if (vec) {
+          const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
+          const int64_t gi = row0 + rr, gj = col0 + rr;
+          const int gk = k0 + k4;
+          float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), cv = pv;
+          if (gk < dim) {
+            if (gi < n) pv = __ldg(reinterpret_cast<const float4*>(P + gi * dim + gk));
+            if (gj < m) cv = __ldg(reinterpret_cast<const float4*>(C + gj * dim + gk));
+          }
+          const float pq[4] = {pv.x, pv.y, pv.z, pv.w}, cq[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            As[k4 + q][rr] = static_cast<TACC>(pq[q]);
+            Bs[k4 + q][rr] = static_cast<TACC>(cq[q]);
+          }
+        } else {
+          for (int t = threadIdx.x; t < RT_B * RT_K; t += 256) {
+            const int rr = t / RT_K, kk = t % RT_K;
+            const int64_t gi = row0 + rr, gj = col0 + rr;
+            const int gk = k0 + kk;
+            TACC pv = 0, cv = 0;
+            if (gk < dim) {
+              if (gi < n) pv = static_cast<TACC>(P[gi * dim + gk]);
+              if (gj < m) cv = static_cast<TACC>(C[gj * dim + gk]);
+            }
+            As[kk][rr] = pv;
+            Bs[kk][rr] = cv;
+          }
+        }
+        __syncthreads();
+        const int kend = min(RT_K, dim - k0);  // padded dimensions must not add a term
+        if constexpr (REC == RC_F32) {
+          for (int kk = 0; kk < kend; ++kk) {
+            float av[4];
+            rt_lds4(&As[kk][ty * 4], av);
+            uint64_t b01, b23;
+            lds_f2x2(&Bs[kk][tx * 4], b01, b23);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint64_t ar = f2_pack(av[r], av[r]);
+              const uint64_t d01 = f2_sub(ar, b01), d23 = f2_sub(ar, b23);
+              acc2[r][0] = f2_fma(d01, d01, acc2[r][0]);
+              acc2[r][1] = f2_fma(d23, d23, acc2[r][1]);
+            }
+          }
+        } else {
+          for (int kk = 0; kk < kend; ++kk) {
+            double av[4], bw[4];
+            rt_lds4(&As[kk][ty * 4], av);
+            rt_lds4(&Bs[kk][tx * 4], bw);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const double d = av[r] - bw[c];
+                acc[r][c] = fma(d, d, acc[r][c]);
+              }
+          }
+        }
+        __syncthreads();
+      }
+      if constexpr (REC == RC_F32) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          f2_unpack(acc2[r][0], acc[r][0], acc[r][1]);
+          f2_unpack(acc2[r][1], acc[r][2], acc[r][3]);
+        }
+      }
+      // this thread's columns in increasing order: a strict comparison keeps the first
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int64_t j = col0 + tx * 4 + c;
+          const float v = static_cast<float>(acc[r][c]);
+          if (j < m && v < bv[r]) {
+            bv[r] = v;
+            bj[r] = static_cast<uint32_t>(j);
+          }
+        }
+    }
+    // the row's 16 threads: (distance, index) minimum
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv[r], o);
+        const uint32_t oj = __shfl_xor_sync(0xffffffffu, bj[r], o);
+        if (ov < bv[r] || (ov == bv[r] && oj < bj[r])) {
+          bv[r] = ov;
+          bj[r] = oj;
+        }
+      }
+      const int64_t i = row0 + ty * 4 + r;
+      if (tx == 0 && i < n) {
+        if (labels) labels[i] = static_cast<int64_t>(bj[r]);
+        if (labels32) labels32[i] = static_cast<int32_t>(bj[r]);
+        if (md) md[i] = bv[r];
+      }
+    }
+  }
+}
+
+cudaError_t launch_dense_argmin(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int dim,
+                                int64_t* labels, int32_t* labels32, float* md, cudaStream_t st) {
+  const int64_t nrt = (n + RT_B - 1) / RT_B;
+  if (nrt == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(nrt, 0x7fffffff));
+  const float* Pf = static_cast<const float*>(P);
+  const float* Cf = static_cast<const float*>(C);
+  if (s->rec != RC_F64 && s->rec != RC_F32) return cudaErrorNotSupported;
+  timing_begin(st, "dense_argmin_kernel");
+  if (s->rec == RC_F64)
+    dense_argmin_kernel<RC_F64><<<blocks, 256, 0, st>>>(Pf, Cf, n, m, dim, labels, labels32, md);
+  else
+    dense_argmin_kernel<RC_F32><<<blocks, 256, 0, st>>>(Pf, Cf, n, m, dim, labels, labels32, md);
+  cudaError_t e = cudaGetLastError();
+  timing_end(st);
+  return e;
+}
+
 template <typename TIN, int REC, typename TOUT, int FLAG, bool ARGMIN>
 static cudaError_t go_rec(const DistJob& j) {
   RecArgs a{};

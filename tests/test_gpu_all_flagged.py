@@ -3,8 +3,8 @@
 With K >= 2.5 the reference's cancellation test flags every pair whose norms lie in
 the safe range (tests/test_oracle.py::test_all_flagged_route_flags_every_pair pins
 that on the oracle), so its D is the direct recompute of every pair.  The engine then
-runs the certified argmin in both the screen and the exact mode and reports n * m
-flagged pairs; a call with a row or center outside the range (NaN, a norm below
+runs the certified argmin in both the screen and the exact mode (a dense sweep of all
+pairs when there are at most 512 centers) and reports n * m flagged pairs; a call with a row or center outside the range (NaN, a norm below
 2^-13, above 6.0e4 for the fp16 operators) takes the exact epilogue instead.  Either
 way the labels (first index of the smallest D value), the minimum distances and the
 count must equal the oracle's bit for bit.
@@ -14,7 +14,7 @@ import pytest
 import torch
 
 import _ops
-from _lib import device_check
+from _lib import device_check, lib
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -56,6 +56,53 @@ def test_all_flagged_route_matches_oracle(name, exact):
     C = np.concatenate([P[rng.choice(n, k - 8, replace=False)], P[:8]]).astype(np.float32)  # duplicates: first index
     flag = check_against_oracle(name, P, C, 50.0, exact)
     assert flag.all()
+    device_check()
+
+
+@pytest.mark.parametrize("name", OPS)
+@pytest.mark.parametrize("exact", [False, True])
+@pytest.mark.parametrize("n,d,k", [(701, 64, 300), (600, 70, 512), (65, 36, 7)])
+def test_all_flagged_few_centers(name, exact, n, d, k):
+    # few centers, clustered data: the certified bounds decide most rows and the route
+    # stays certified (the dense sweep takes over only where they fail, below); labels,
+    # distances and count as the oracle's.  d = 70 and 36 are not multiples of 16, 7 and
+    # 300 centers leave partial tiles, 512 is the most the dense sweep would take
+    rng = np.random.default_rng(n + k)
+    true_c = rng.normal(size=(max(2, k // 4), d))
+    P = (true_c[rng.integers(0, true_c.shape[0], n)] + 0.3 * rng.normal(size=(n, d))).astype(np.float32)
+    C = np.concatenate([P[rng.choice(n, k - 2, replace=False)], P[:2]]).astype(np.float32)  # duplicates
+    flag = check_against_oracle(name, P, C, 50.0, exact)
+    assert flag.all()
+    device_check()
+
+
+@pytest.mark.parametrize("name", ["bf16_fp64", "bf16_fp32"])
+def test_c3_shape_offset_dense_sweep(name):
+    # C3's recipe (offset 1000, kappa 5: K = 5.16 flags every pair) on 2048 rows: the
+    # norms dwarf the distances, the certified screen decides few rows and the route
+    # sweeps every pair densely.  Centers 3 and 5 differ by one fp32 ulp in dimension 7
+    # and rows 0..39 sit on center 5 there: center 3 is farther by ulp^2 in fp64, far
+    # below the stored distance's fp32 ulp, so the stored values tie and the first
+    # index, 3, is the label (a comparison in fp64 would give 5).
+    rng = np.random.default_rng(11)
+    n, d, k = 2048, 64, 256
+    P = (rng.normal(size=(n, d)) + 1000.0).astype(np.float32)
+    C = (rng.normal(size=(k, d)) + 1000.0).astype(np.float32)
+    C[5] = C[3]
+    C[5, 7] = np.nextafter(C[3, 7], np.float32(2000.0))
+    P[:40] = C[5] + 0.3 * rng.normal(size=(40, d)).astype(np.float32)
+    P[:40, 7] = C[5, 7]
+    L = lib()
+    for exact in (False, True):
+        L.euc_set_kernel_timing(1)
+        try:
+            flag = check_against_oracle(name, P, C, 5.0, exact)
+            assert L.euc_last_kernel_name() == b"dense_argmin_kernel"
+        finally:
+            L.euc_set_kernel_timing(0)
+        assert flag.all()
+    lab, _, _ = _ops.run_argmin(name, cuda(P), cuda(C), 5.0)
+    assert (lab[:40].cpu().numpy() == 3).all()
     device_check()
 
 
