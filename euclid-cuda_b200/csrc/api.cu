@@ -240,7 +240,7 @@ struct RunOut {
   int tile_T = 0;
 };
 
-// all-flagged argmin whose bounds fail: at most this many centers take the dense sweep
+// certified argmin whose bounds fail: at most this many centers take the dense sweep
 constexpr int64_t kDenseArgminMaxM = 512;
 
 static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n, int64_t m, int64_t dim,
@@ -443,12 +443,13 @@ static int run_distance(const OpSpec* s, const void* P, const void* C, int64_t n
     // others; their direct distances, and the rows evaluated whole
     float* md = static_cast<float*>(o.min_dist);
     e = launch_cert_rows(j, o.labels, o.labels32, md);
-    // all-flagged route over few centers: when the first screen's bounds decide fewer
-    // than half of the rows (norms far larger than the distances, as in C3's offset
-    // points), the rest would go through a second screen and every group; one dense
-    // sweep of all pairs gives the same labels and distances sooner (C3, 2^22 x 256 x 64
-    // bf16_fp64: 68.0 ms certified).  It rewrites every row's outputs.
-    if (e == cudaSuccess && all_flagged && m <= kDenseArgminMaxM && j.cert_ng > 0 && j.cert_ent_n) {
+    // few centers: when the first screen's bounds decide fewer than half of the rows
+    // (norms far larger than the distances, as in C3's offset points), the rest would go
+    // through a second screen and every group; one dense sweep of all pairs, minimum of
+    // the same keys, gives the same labels and distances sooner (C3, 2^22 x 256 x 64
+    // bf16_fp64: 68.0 ms certified).  It rewrites every row's outputs; the count is the
+    // n m direct distances it takes (the all-flagged route's count too).
+    if (e == cudaSuccess && m <= kDenseArgminMaxM && j.cert_ng > 0 && j.cert_ent_n) {
       unsigned int decided = 0;
       e = cudaMemcpyAsync(&decided, j.cert_ent_n, sizeof(decided), cudaMemcpyDeviceToHost, st);
       if (e == cudaSuccess) e = cudaStreamSynchronize(st);

@@ -320,9 +320,10 @@ __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArg
 // and arithmetic (fp32: packed lanes, each the scalar __fsub_rn / __fmaf_rn in k order;
 // fp64: fma in k order), keeping per thread the first-index minimum of its 4 rows over
 // its columns in increasing order; the 16 threads of a row then take the (distance,
-// index) minimum by shuffle.  Distances are compared as the operator stores them,
-// rounded to fp32 (the certified path's keys do the same), so fp64 values that round
-// alike tie and the first index wins; min_dist is that fp32 value.
+// index) minimum by shuffle.  The minimum is taken over the certified path's keys, the
+// distance as the operator stores it (rounded to fp32) above the center index, so the
+// outputs are the certified argmin's for any input (fp64 values that round alike tie
+// and the first index wins; NaN distances sort last).
 template <int REC>
 __global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restrict__ P, const float* __restrict__ C,
                                                            int64_t n, int64_t m, int dim, int64_t* __restrict__ labels,
@@ -335,13 +336,7 @@ __global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restri
   const bool vec = (dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(C)) % 16 == 0);
   for (int64_t rtile = blockIdx.x; rtile < nrt; rtile += gridDim.x) {
     const int64_t row0 = rtile * RT_B;
-    float bv[4];
-    uint32_t bj[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      bv[r] = __int_as_float(0x7f800000);
-      bj[r] = 0xffffffffu;
-    }
+    unsigned long long bk[4] = {~0ull, ~0ull, ~0ull, ~0ull};
     for (int64_t ct = 0; ct < nct; ++ct) {
       const int64_t col0 = ct * RT_B;
       TACC acc[4][4];
@@ -421,16 +416,14 @@ __global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restri
           f2_unpack(acc2[r][1], acc[r][2], acc[r][3]);
         }
       }
-      // this thread's columns in increasing order: a strict comparison keeps the first
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int64_t j = col0 + tx * 4 + c;
-          const float v = static_cast<float>(acc[r][c]);
-          if (j < m && v < bv[r]) {
-            bv[r] = v;
-            bj[r] = static_cast<uint32_t>(j);
+          if (j < m) {
+            const unsigned long long key = make_key(static_cast<float>(acc[r][c]), static_cast<uint32_t>(j));
+            bk[r] = key < bk[r] ? key : bk[r];
           }
         }
     }
@@ -439,18 +432,15 @@ __global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restri
     for (int r = 0; r < 4; ++r) {
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv[r], o);
-        const uint32_t oj = __shfl_xor_sync(0xffffffffu, bj[r], o);
-        if (ov < bv[r] || (ov == bv[r] && oj < bj[r])) {
-          bv[r] = ov;
-          bj[r] = oj;
-        }
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, bk[r], o);
+        bk[r] = other < bk[r] ? other : bk[r];
       }
       const int64_t i = row0 + ty * 4 + r;
       if (tx == 0 && i < n) {
-        if (labels) labels[i] = static_cast<int64_t>(bj[r]);
-        if (labels32) labels32[i] = static_cast<int32_t>(bj[r]);
-        if (md) md[i] = bv[r];
+        const uint32_t j = static_cast<uint32_t>(bk[r] & 0xffffffffull);
+        if (labels) labels[i] = static_cast<int64_t>(j);
+        if (labels32) labels32[i] = static_cast<int32_t>(j);
+        if (md) md[i] = __uint_as_float(static_cast<uint32_t>(bk[r] >> 32));
       }
     }
   }

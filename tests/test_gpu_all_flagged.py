@@ -103,6 +103,17 @@ def test_c3_shape_offset_dense_sweep(name):
         assert flag.all()
     lab, _, _ = _ops.run_argmin(name, cuda(P), cuda(C), 5.0)
     assert (lab[:40].cpu().numpy() == 3).all()
+    # the certified mode takes the same sweep; its count is the n k direct distances
+    L.euc_set_kernel_timing(1)
+    try:
+        lab, md, cnt = _ops.run_argmin(name, cuda(P), cuda(C), 5.0, exact="certified")
+        assert L.euc_last_kernel_name() == b"dense_argmin_kernel"
+    finally:
+        L.euc_set_kernel_timing(0)
+    lo, mo = O.certified_argmin(name, P, C)
+    np.testing.assert_array_equal(lab.cpu().numpy(), lo)
+    np.testing.assert_array_equal(md.cpu().numpy(), mo)
+    assert int(cnt.item()) == n * k and (lo[:40] == 3).all()
     device_check()
 
 
