@@ -214,25 +214,35 @@ __global__ void __launch_bounds__(256) recompute_dense_tiled_kernel(const RecArg
     uint64_t acc2[4][2];  // fp32: (columns 2h, 2h + 1) of row r
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc2[r][0] = acc2[r][1] = 0ull;
+    // fp32 rows with dim % 4 == 0 on 16-byte boundaries: thread t holds dimensions
+    // k0 + 4 (t % 4) .. + 3 of row / center t / 4 (a quad is whole or past the end),
+    // fetched one slab ahead so that the loads are in flight while a slab is formed
+    float4 pvn = make_float4(0.f, 0.f, 0.f, 0.f), cvn = pvn;
+    auto fetch = [&](int k0) {
+      if constexpr (std::is_same<TIN, float>::value) {
+        const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
+        const int64_t gi = row0 + rr, gj = col0 + rr;
+        const int gk = k0 + k4;
+        pvn = make_float4(0.f, 0.f, 0.f, 0.f);
+        cvn = pvn;
+        if (gk < a.dim) {
+          if (gi < a.n) pvn = __ldg(reinterpret_cast<const float4*>(P + gi * a.dim + gk));
+          if (gj < a.m) cvn = __ldg(reinterpret_cast<const float4*>(C + gj * a.dim + gk));
+        }
+      }
+    };
+    if (vec) fetch(0);
     for (int k0 = 0; k0 < a.dim; k0 += RT_K) {
       if constexpr (std::is_same<TIN, float>::value) {
         if (vec) {
-          // thread t: dimensions k0 + 4 (t % 4) .. + 3 of row / center t / 4 (the dim
-          // is a multiple of 4, so a quad is either whole or past the end)
           const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
-          const int64_t gi = row0 + rr, gj = col0 + rr;
-          const int gk = k0 + k4;
-          float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), cv = pv;
-          if (gk < a.dim) {
-            if (gi < a.n) pv = __ldg(reinterpret_cast<const float4*>(P + gi * a.dim + gk));
-            if (gj < a.m) cv = __ldg(reinterpret_cast<const float4*>(C + gj * a.dim + gk));
-          }
-          const float pq[4] = {pv.x, pv.y, pv.z, pv.w}, cq[4] = {cv.x, cv.y, cv.z, cv.w};
+          const float pq[4] = {pvn.x, pvn.y, pvn.z, pvn.w}, cq[4] = {cvn.x, cvn.y, cvn.z, cvn.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             As[k4 + q][rr] = static_cast<TACC>(pq[q]);
             Bs[k4 + q][rr] = static_cast<TACC>(cq[q]);
           }
+          if (k0 + RT_K < a.dim) fetch(k0 + RT_K);
         }
       }
       for (int t = threadIdx.x; !vec && t < RT_B * RT_K; t += 256) {
@@ -347,22 +357,30 @@ __global__ void __launch_bounds__(256) dense_argmin_kernel(const float* __restri
       uint64_t acc2[4][2];  // fp32: (columns 2h, 2h + 1) of row r
 #pragma unroll
       for (int r = 0; r < 4; ++r) acc2[r][0] = acc2[r][1] = 0ull;
+      // the 16-byte staging fetches one slab ahead (as in recompute_dense_tiled_kernel)
+      float4 pvn = make_float4(0.f, 0.f, 0.f, 0.f), cvn = pvn;
+      auto fetch = [&](int k0) {
+        const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
+        const int64_t gi = row0 + rr, gj = col0 + rr;
+        const int gk = k0 + k4;
+        pvn = make_float4(0.f, 0.f, 0.f, 0.f);
+        cvn = pvn;
+        if (gk < dim) {
+          if (gi < n) pvn = __ldg(reinterpret_cast<const float4*>(P + gi * dim + gk));
+          if (gj < m) cvn = __ldg(reinterpret_cast<const float4*>(C + gj * dim + gk));
+        }
+      };
+      if (vec) fetch(0);
       for (int k0 = 0; k0 < dim; k0 += RT_K) {
         if (vec) {
           const int rr = threadIdx.x >> 2, k4 = (threadIdx.x & 3) * 4;
-          const int64_t gi = row0 + rr, gj = col0 + rr;
-          const int gk = k0 + k4;
-          float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), cv = pv;
-          if (gk < dim) {
-            if (gi < n) pv = __ldg(reinterpret_cast<const float4*>(P + gi * dim + gk));
-            if (gj < m) cv = __ldg(reinterpret_cast<const float4*>(C + gj * dim + gk));
-          }
-          const float pq[4] = {pv.x, pv.y, pv.z, pv.w}, cq[4] = {cv.x, cv.y, cv.z, cv.w};
+          const float pq[4] = {pvn.x, pvn.y, pvn.z, pvn.w}, cq[4] = {cvn.x, cvn.y, cvn.z, cvn.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             As[k4 + q][rr] = static_cast<TACC>(pq[q]);
             Bs[k4 + q][rr] = static_cast<TACC>(cq[q]);
           }
+          if (k0 + RT_K < dim) fetch(k0 + RT_K);
         } else {
           for (int t = threadIdx.x; t < RT_B * RT_K; t += 256) {
             const int rr = t / RT_K, kk = t % RT_K;
