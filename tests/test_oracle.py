@@ -160,6 +160,31 @@ def test_certified_oracle_is_the_fully_flagged_operator(name):
     assert (md[:3] == 0).all()
 
 
+@pytest.mark.parametrize("name", ["bf16_fp64", "bf16_fp32"])
+def test_certified_oracle_ties_on_the_stored_fp32_value(name):
+    # the label is the first index among distances equal AS STORED (fp32): centers 3 and
+    # 5 differ by one fp32 ulp in dimension 7 and the rows sit on center 5 there, so
+    # center 3 is farther by ulp^2 in exact arithmetic but the stored values tie and 3
+    # wins, as argmin_first of the operator's D gives (C3's offset-1000 regime, where the
+    # engine sweeps every pair densely)
+    rng = np.random.default_rng(11)
+    n, d, k = 64, 64, 16
+    P = (rng.normal(size=(n, d)) + 1000.0).astype(np.float32)
+    C = (rng.normal(size=(k, d)) + 1000.0).astype(np.float32)
+    C[5] = C[3]
+    C[5, 7] = np.nextafter(C[3, 7], np.float32(2000.0))
+    P[:10] = C[5] + 0.3 * rng.normal(size=(10, d)).astype(np.float32)
+    P[:10, 7] = C[5, 7]
+    exact = ((P[:10, None, :].astype(np.float64) - C[None, [3, 5], :].astype(np.float64)) ** 2).sum(-1)
+    assert (exact[:, 0] > exact[:, 1]).all()  # center 5 is closer before rounding
+    D, flag, _ = O.mix(name, P, C, kappa=5.0)
+    assert flag.all()
+    lab, md = O.certified_argmin(name, P, C)
+    np.testing.assert_array_equal(lab, O.argmin_first(D))
+    np.testing.assert_array_equal(md, D[np.arange(n), lab])
+    assert (D[:10, 3] == D[:10, 5]).all() and (lab[:10] == 3).all()
+
+
 def test_certified_oracle_rejects_half_arithmetic_recompute():
     P = np.ones((2, 3), np.float32)
     with pytest.raises(ValueError):
